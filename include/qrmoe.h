@@ -1,0 +1,177 @@
+/*
+ * qrmoe.h -- C ABI of libqrmoe.so, the B200 (sm_100a) implementation of
+ * QuantRunner's MoE FFN layer.
+ *
+ * The reference runs this layer on the CPU inside StreamingEngine (C#):
+ *   MoeFfn         src/QuantRunner.Core/Runtime/StreamingEngine.cs:626-667
+ *   LegacyMoeInto  StreamingEngine.cs:670-712
+ *   GlmMoeFfn      StreamingEngine.cs:720-790
+ * called from ForwardLegacy (StreamingEngine.cs:259-262) and ForwardGlm5
+ * (StreamingEngine.cs:320-330), each expert product going through the public
+ * operator DotKernels.MatVecParallel(QuantFormat, byte* w, long rows,
+ * long cols, float* x, float* y) (src/QuantRunner.Core/Kernels/
+ * DotKernels.cs:610).  A P/Invoke shim binds the entry points below so the
+ * engine can hand a whole MoE layer to the GPU.
+ *
+ * Conventions: every function returns QRM_OK (0) or a negative QRM_E_* code;
+ * qrm_last_error() then describes the failure (thread-local, valid until the
+ * next call on the same thread).  Pointers named *_dev are device pointers of
+ * the layer's device; all others are host pointers.  Calls on one qrm_layer
+ * must not overlap (the reference engine is single-threaded too,
+ * StreamingEngine.cs:39,103-117); distinct layers are independent.  There is
+ * no CPU fallback: without a usable sm_100 device, qrm_create fails.
+ */
+#ifndef QRMOE_H
+#define QRMOE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QRM_ABI_VERSION 1
+
+/* Status codes.  The reference throws; the shim maps a negative code to
+ * InvalidOperationException(qrm_last_error()). */
+enum {
+    QRM_OK = 0,
+    QRM_E_INVALID = -1,   /* bad argument or shape  (ArgumentException, Dtypes.cs:63) */
+    QRM_E_FORMAT = -2,    /* format id not supported (NotSupportedException, DotKernels.cs:44) */
+    QRM_E_SIZE = -3,      /* byte count != Dtypes.TensorBytes (Dtypes.cs:60-65) */
+    QRM_E_STATE = -4,     /* a tensor the forward needs was never uploaded (KeyNotFoundException, ModelStore.cs:79-80) */
+    QRM_E_CUDA = -5,      /* CUDA runtime error */
+    QRM_E_NCCL = -6,      /* NCCL error (expert-parallel layers) */
+    QRM_E_TIMEOUT = -7,   /* a bounded device wait or a collective gave up */
+    QRM_E_NOMEM = -8,     /* device allocation failed */
+    QRM_E_CAPACITY = -9   /* request exceeds a fixed capacity */
+};
+
+/* QuantFormat ids as stored in .qw headers (src/QuantRunner.Core/Dtypes.cs:6-26).
+ * Expert matrices may use Q4_0, Q8_0, Q4_K, Q6_K or TRI. */
+enum {
+    QRM_F32 = 0, QRM_F16 = 1, QRM_BF16 = 2, QRM_Q4_0 = 3, QRM_Q8_0 = 4,
+    QRM_Q4_K = 6, QRM_Q6_K = 7, QRM_TRI = 8
+};
+
+/* Which matrix of an expert (canonical names, src/QuantRunner.Core/Models/
+ * NameMapper.cs:7-12: l{i}.e{j}.w_gate / w_up / w_down, shared l{i}.sw_*). */
+enum { QRM_GATE = 0, QRM_UP = 1, QRM_DOWN = 2 };
+#define QRM_SHARED_EXPERT (-1)
+
+/* Forward flags. */
+enum {
+    QRM_APPLY_NORM = 1,    /* input is the residual stream: xn = RmsNorm(x, ffn_norm) first
+                              (StreamingEngine.cs:259-260 / 320-321) */
+    QRM_ADD_RESIDUAL = 2   /* MoeFfn semantics: out = x + sum_j w_j y_j (StreamingEngine.cs:665);
+                              without it out = sum_j w_j y_j (LegacyMoeInto / GlmMoeFfn) */
+};
+
+/* Layer description: the MoE fields of ModelConfig (src/QuantRunner.Core/
+ * Models/ModelConfig.cs:22-61) plus storage formats and placement. */
+typedef struct qrm_layer_desc {
+    int32_t d_model;       /* "dim"          ModelConfig.cs:14 */
+    int32_t n_experts;     /* "n_experts"    ModelConfig.cs:23 */
+    int32_t n_active;      /* "n_active"     ModelConfig.cs:24 (top-k = min(n_active, 8), StreamingEngine.cs:628) */
+    int32_t expert_ffn;    /* EffectiveExpertFfn ModelConfig.cs:25,67 (also the shared expert's width, StreamingEngine.cs:723,784) */
+    int32_t moe_sigmoid;   /* "moe_sigmoid"  ModelConfig.cs:57: 1 = GlmMoeFfn routing */
+    float   routed_scale;  /* "routed_scale" ModelConfig.cs:58 */
+    int32_t n_shared;      /* "n_shared"     ModelConfig.cs:59 (GLM shared expert when > 0) */
+    float   swiglu_limit;  /* "swiglu_limit" ModelConfig.cs:61 (GLM only; 0 = plain SiLU) */
+    float   rms_eps;       /* "rms_eps"      ModelConfig.cs:22 */
+    int32_t fmt_gate, fmt_up, fmt_down;          /* routed experts' storage formats */
+    int32_t fmt_sh_gate, fmt_sh_up, fmt_sh_down; /* shared expert's storage formats */
+    int32_t device;        /* CUDA device ordinal */
+    int32_t max_tokens;    /* largest T per forward (buffers are sized for it) */
+} qrm_layer_desc;
+
+typedef struct qrm_layer qrm_layer;
+
+/* ---- library ---- */
+int         qrm_version(void);          /* QRM_ABI_VERSION */
+const char* qrm_last_error(void);
+
+/* ---- layer lifetime ----
+ * qrm_create: replaces the per-layer state the engine reads through W()
+ * (StreamingEngine.cs:186-192) and the PrefetchPipeline staging
+ * (PrefetchPipeline.cs:64-166): the layer's experts live in HBM. */
+int  qrm_create(const qrm_layer_desc* desc, qrm_layer** out);
+void qrm_destroy(qrm_layer* layer);
+
+/* ---- uploads (host bytes are copied; the caller may unmap afterwards) ----
+ * Replace Dequant1D(l{i}.ffn_norm) (StreamingEngine.cs:196-201,259),
+ * Store.Get(l{i}.router) (:639) and l{i}.router_bias (:738-739), with the
+ * tensors already widened to f32 (F16/BF16 widening is exact, Dtypes.cs:76-129). */
+int qrm_upload_norm(qrm_layer* layer, const float* w /* [d] */);
+int qrm_upload_router(qrm_layer* layer, const float* w /* [E x d] */, const float* bias /* [E] or NULL */);
+/* Harness-only per-expert logit offset (added after the router dot; NULL
+ * clears it).  No counterpart in the reference. */
+int qrm_upload_logit_offset(qrm_layer* layer, const float* offset /* [E] or NULL */);
+/* One expert matrix in its .qw block bytes (l{i}.e{j}.w_gate/w_up/w_down,
+ * gate/up [f x d], down [d x f], row-major, blocks along columns,
+ * ModelStore.cs:30-42).  expert = QRM_SHARED_EXPERT for l{i}.sw_*.  nbytes must
+ * equal Dtypes.TensorBytes(rows*cols, fmt).  No requantisation: the bytes are
+ * stored as they are, with each block's fields grouped by kind for aligned
+ * loads (qrm_download_expert returns the original bytes). */
+int qrm_upload_expert(qrm_layer* layer, int expert, int which, int fmt,
+                      const void* bytes, size_t nbytes);
+int qrm_upload_expert_device(qrm_layer* layer, int expert, int which, int fmt,
+                             const void* bytes_dev, size_t nbytes);
+int qrm_download_expert(qrm_layer* layer, int expert, int which, void* bytes, size_t nbytes);
+
+/* ---- forward ----
+ * One MoE layer over T tokens (the reference runs T sequential Forward calls).
+ * x [T x d] f32, out [T x d] f32.  Optional outputs (NULL to skip):
+ * topk_idx [T x k] int32 (the experts in the reference's sorted order),
+ * topk_w [T x k] f32 (their combine weights).  Synchronous. */
+int qrm_forward(qrm_layer* layer, const float* x, int T, int flags, float* out,
+                int32_t* topk_idx, float* topk_w);
+/* Same on device buffers, asynchronous on `stream` (a cudaStream_t; NULL =
+ * the layer's own stream).  Call qrm_sync (or synchronise the stream) before
+ * reading results; qrm_sync reports device-side errors of earlier forwards. */
+int qrm_forward_device(qrm_layer* layer, const float* x_dev, int T, int flags, float* out_dev,
+                       int32_t* topk_idx_dev, float* topk_w_dev, void* stream);
+int qrm_sync(qrm_layer* layer);
+/* Dispatch of the last forward: perm [T*k] lists the assignments
+ * a = t*k + j sorted by expert (stable: a ascending inside an expert) and
+ * offsets [E+1] delimits each expert's run. */
+int qrm_last_dispatch(qrm_layer* layer, int32_t* perm, int32_t* offsets);
+/* Router logits [T x E] and normalised input xn [T x d] of the last forward
+ * (debug/parity; NULL to skip either). */
+int qrm_last_router(qrm_layer* layer, float* logits, float* xn);
+
+/* Per-stage device timing of forwards (CUDA events on the forward's stream).
+ * qrm_last_profile fills ms[QRM_STAGE_COUNT] for the last forward
+ * (route, topk, dispatch, gate/up, down, combine; stages that did not run
+ * report 0) and bytes[QRM_STAGE_COUNT] with the algorithmic HBM bytes of
+ * the gate/up and down stages (compressed expert bytes of the experts the
+ * batch selected, plus activations).  No counterpart in the reference
+ * (its `bench` command times whole tokens, Commands.cs:801-829). */
+enum { QRM_STAGE_ROUTE = 0, QRM_STAGE_TOPK, QRM_STAGE_DISPATCH, QRM_STAGE_GATEUP, QRM_STAGE_DOWN,
+       QRM_STAGE_COMBINE, QRM_STAGE_COUNT };
+int qrm_set_profiling(qrm_layer* layer, int on);
+int qrm_last_profile(qrm_layer* layer, float* ms, double* bytes);
+
+/* ---- operator API: DotKernels.MatVecParallel / DotKernels.GEMM on the GPU ----
+ * (DotKernels.cs:610-660).  A qrm_matrix holds one [rows x cols] matrix in
+ * HBM; qrm_matrix_gemv computes y[t] = W x[t] for T tokens
+ * (x_dev [T x cols], y_dev [T x rows]). */
+typedef struct qrm_matrix qrm_matrix;
+int  qrm_matrix_create(int device, int fmt, int64_t rows, int64_t cols,
+                       const void* bytes, size_t nbytes, qrm_matrix** out);
+void qrm_matrix_destroy(qrm_matrix* m);
+int  qrm_matrix_gemv(qrm_matrix* m, const float* x_dev, int T, float* y_dev, void* stream);
+
+/* ---- synthetic weights on the device (the reference's `synthesize`,
+ * src/QuantRunner.Cli/Program.cs:247-369) ----
+ * qrm_synth_gaussian fills dst_dev[n] with sigma * N(0,1) from a
+ * counter-based generator (splitmix64 + Box-Muller); qrm_synth_quantize runs
+ * the reference quantiser (BlockQuantizer.cs; fmt 108 = QuantizeTriLegacy)
+ * on the device, byte-identical to the CPU one. */
+int qrm_synth_gaussian(float* dst_dev, int64_t n, uint64_t seed, float sigma, void* stream);
+int qrm_synth_quantize(int fmt, const float* src_dev, int64_t n, void* dst_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QRMOE_H */

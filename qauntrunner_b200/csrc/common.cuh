@@ -1,0 +1,58 @@
+// common.cuh -- shared device helpers and device-side descriptors.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qrm {
+
+// QuantFormat ids (Dtypes.cs:6-26)
+enum Fmt : int32_t { F32 = 0, F16 = 1, BF16 = 2, Q4_0 = 3, Q8_0 = 4, Q4_K = 6, Q6_K = 7, TRI = 8 };
+
+// Dtypes.BlockSpec (Dtypes.cs:38-57)
+__host__ __device__ inline bool block_spec(int fmt, int* bs, int* bb) {
+    switch (fmt) {
+        case F32: *bs = 1; *bb = 4; return true;
+        case F16: *bs = 1; *bb = 2; return true;
+        case BF16: *bs = 1; *bb = 2; return true;
+        case Q4_0: *bs = 32; *bb = 20; return true;
+        case Q8_0: *bs = 32; *bb = 34; return true;
+        case Q4_K: *bs = 256; *bb = 144; return true;
+        case Q6_K: *bs = 256; *bb = 210; return true;
+        case TRI: *bs = 64; *bb = 18; return true;
+        default: return false;
+    }
+}
+
+inline bool is_expert_fmt(int fmt) {
+    return fmt == Q4_0 || fmt == Q8_0 || fmt == Q4_K || fmt == Q6_K || fmt == TRI;
+}
+
+// A quantised matrix in HBM.  Q4_K keeps the .qw block bytes unchanged
+// (144-byte blocks are 16-byte aligned).  The formats whose blocks are not a
+// multiple of 16 bytes are stored with each block's fields grouped by kind
+// ("split" layout) so every field is loaded with aligned vector loads; the
+// blocks are numbered row-major (row r, block b -> r*blocks_per_row + b):
+//   Q4_0: qs[nb][16]  | d[nb] (f16)
+//   Q8_0: qs[nb][32]  | d[nb]
+//   Q6_K: ql[nb][128] | qh[nb][64] | sc[nb][16] | d[nb]
+//   TRI : codes[nb][16] | scale[nb]
+// The total size equals the .qw size; no byte value changes.
+struct MatDev {
+    const uint8_t* base;
+    int32_t fmt;
+    int32_t rows;
+    int32_t cols;
+    int32_t pad;
+    int64_t nb;  // number of blocks
+};
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// Bounded spin wait limit (device waits never spin forever).
+constexpr long long kSpinLimit = 1ll << 26;
+
+// Device-side error flag bits, read back by qrm_sync().
+enum : uint32_t { ERR_TIMEOUT = 1u, ERR_BOUNDS = 2u, ERR_INTERNAL = 4u };
+
+}  // namespace qrm

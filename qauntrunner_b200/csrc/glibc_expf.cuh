@@ -33,20 +33,19 @@
 namespace qrm {
 
 // T[i] = bits(2^(i/32)) - (i << 47), i = 0..31
+#define QRM_EXPF_TABLE \
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull, \
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull, \
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull, \
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull, \
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull, \
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull, \
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull, \
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull
 #if defined(__CUDACC__)
-__device__ __constant__ static const uint64_t kExpfTab[32] = {
-#else
-static const uint64_t kExpfTab[32] = {
+__device__ __constant__ static const uint64_t kExpfTabDev[32] = {QRM_EXPF_TABLE};
 #endif
-    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
-    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
-    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
-    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
-    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
-    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
-    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
-    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
-};
+static const uint64_t kExpfTabHost[32] = {QRM_EXPF_TABLE};
 
 QRM_HD uint32_t f32_bits(float f) {
 #if defined(__CUDA_ARCH__)
@@ -125,7 +124,11 @@ QRM_HD float expf_glibc(float x) {
     uint64_t ki = f64_bits(kd);
     kd = add64(kd, -kShift);
     double r = fma64(kInvLn2N, xd, -kd);
-    uint64_t t = kExpfTab[ki % 32];
+#if defined(__CUDA_ARCH__)
+    uint64_t t = kExpfTabDev[ki % 32];
+#else
+    uint64_t t = kExpfTabHost[ki % 32];
+#endif
     t += ki << (52 - 5);
     double s = f64_from(t);
     double z = fma64(kC0, r, kC1);

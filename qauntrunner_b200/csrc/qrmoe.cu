@@ -1,0 +1,773 @@
+// qrmoe.cu -- the C ABI of libqrmoe.so (include/qrmoe.h): layer state in
+// HBM, uploads, the forward launch sequence and the matrix operator API.
+//
+// Forward launch sequence on the layer's stream (all device-resident):
+//   route      RMSNorm + router logits, bit-exact emulation (route.cuh)
+//   topk       softmax / sigmoid top-k and combine weights (route.cuh)
+//   dispatch   stable counting sort -> perm, offsets, active expert list
+//   gate/up    fused dequant GEMV + SwiGLU over (expert, row tile) items
+//   down       fused dequant GEMV
+//   combine    weighted sum in slot order (+ residual, + shared expert)
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <map>
+#include <tuple>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/qrmoe.h"
+#include "combine.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "layout.cuh"
+#include "route.cuh"
+
+extern "C" int qrm_synth_quantize_impl(int fmt, const float* src, long long n, void* dst, cudaStream_t s);
+extern "C" int qrm_synth_gaussian_impl(float* dst, long long n, uint64_t seed, float sigma, cudaStream_t s);
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define QRM_CUDA(expr)                                                                          \
+    do {                                                                                        \
+        cudaError_t e_ = (expr);                                                                \
+        if (e_ != cudaSuccess) return fail(QRM_E_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+    } while (0)
+
+int64_t tensor_bytes(int fmt, int64_t rows, int64_t cols) {
+    int bs, bb;
+    if (!qrm::block_spec(fmt, &bs, &bb)) return -1;
+    if (cols % bs != 0) return -1;
+    return rows * (cols / bs) * bb;
+}
+
+const char* which_name(int which) { return which == 0 ? "w_gate" : which == 1 ? "w_up" : "w_down"; }
+
+// Template dispatch of the expert GEMV kernel.
+template <int FMT, int M, int R>
+cudaError_t launch_gemv_nt(int nt, const qrm::GemvParams& p, int grid, int block, cudaStream_t s) {
+    switch (nt) {
+        case 1: qrm::expert_gemv_kernel<FMT, M, R, 1><<<grid, block, 0, s>>>(p); break;
+        case 2: qrm::expert_gemv_kernel<FMT, M, R, 2><<<grid, block, 0, s>>>(p); break;
+        default: qrm::expert_gemv_kernel<FMT, M, R, 4><<<grid, block, 0, s>>>(p); break;
+    }
+    return cudaGetLastError();
+}
+
+template <int FMT, int M, int R>
+int gemv_occupancy(int nt, int block) {
+    int nb = 0;
+    switch (nt) {
+        case 1: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, qrm::expert_gemv_kernel<FMT, M, R, 1>, block, 0); break;
+        case 2: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, qrm::expert_gemv_kernel<FMT, M, R, 2>, block, 0); break;
+        default: cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, qrm::expert_gemv_kernel<FMT, M, R, 4>, block, 0); break;
+    }
+    return std::max(nb, 1);
+}
+
+constexpr int kRGateUp = 4;   // rows per gate/up item (x2 matrices)
+constexpr int kRDown = 8;     // rows per down item
+
+// gate/up (M=2) or down (M=1) for one format
+int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_count, cudaStream_t s) {
+    const int U = p.cols / 32;
+    const int block = (U + 31) / 32 * 32;
+    int occ = 1;
+    cudaError_t err = cudaSuccess;
+#define QRM_GEMV_CASE(F)                                                                        \
+    case F:                                                                                     \
+        if (gateup) {                                                                           \
+            occ = gemv_occupancy<F, 2, kRGateUp>(nt, block);                                    \
+            err = launch_gemv_nt<F, 2, kRGateUp>(nt, p, sm_count * occ, block, s);              \
+        } else {                                                                                \
+            occ = gemv_occupancy<F, 1, kRDown>(nt, block);                                      \
+            err = launch_gemv_nt<F, 1, kRDown>(nt, p, sm_count * occ, block, s);                \
+        }                                                                                       \
+        break;
+    switch (fmt) {
+        QRM_GEMV_CASE(qrm::Q4_K)
+        QRM_GEMV_CASE(qrm::Q4_0)
+        QRM_GEMV_CASE(qrm::Q8_0)
+        QRM_GEMV_CASE(qrm::Q6_K)
+        QRM_GEMV_CASE(qrm::TRI)
+        default: return fail(QRM_E_FORMAT, "format %d has no expert kernel", fmt);
+    }
+#undef QRM_GEMV_CASE
+    if (err != cudaSuccess) return fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(err));
+    return QRM_OK;
+}
+
+int pick_nt(int T) { return T <= 1 ? 1 : (T <= 8 ? 2 : 4); }
+
+}  // namespace
+
+// ---------------------------------------------------------------- layer
+
+struct qrm_layer {
+    qrm_layer_desc desc{};
+    int k = 0;
+    int first_expert = 0, n_local = 0;  // routed experts held by this layer
+    bool shared_enabled = false;        // GLM layer with n_shared > 0
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    // weights
+    uint8_t* slab = nullptr;
+    std::vector<qrm::MatDev> mats;      // (E+1)*3
+    std::vector<size_t> mat_bytes;
+    qrm::MatDev* mats_dev = nullptr;
+    std::vector<uint8_t> uploaded;      // (E+1)*3
+    float* norm_w = nullptr;
+    float* router = nullptr;
+    float* router_bias = nullptr;
+    float* offset = nullptr;
+    bool has_norm = false, has_router = false, has_bias = false, has_offset = false;
+    // work buffers
+    int cap_T = 0;
+    float *x = nullptr, *xn = nullptr, *logits = nullptr, *topk_w = nullptr;
+    float *h = nullptr, *hs = nullptr, *y = nullptr, *ys = nullptr, *out = nullptr;
+    int32_t *topk_idx = nullptr, *perm = nullptr, *inv_perm = nullptr, *offsets = nullptr, *active = nullptr;
+    qrm::Schedule* sched = nullptr;
+    uint8_t* staging = nullptr;
+    size_t staging_bytes = 0;
+    int last_T = 0;
+    const float* last_xn = nullptr;
+    // per-stage timing
+    bool profiling = false;
+    bool profiled_last = false;
+    cudaEvent_t ev[QRM_STAGE_COUNT + 1] = {};
+    bool last_shared = false;
+    // CUDA graphs of the forward, keyed by buffers, T, flags and profiling
+    using GraphKey = std::tuple<const void*, const void*, const void*, const void*, int, int, int>;
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+};
+
+static void clear_graphs(qrm_layer* L) {
+    for (auto& kv : L->graphs) cudaGraphExecDestroy(kv.second);
+    L->graphs.clear();
+}
+
+static void free_layer(qrm_layer* L) {
+    if (!L) return;
+    cudaSetDevice(L->desc.device);
+    if (L->stream) cudaStreamSynchronize(L->stream);
+    void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_bias, L->offset, L->x, L->xn,
+                    L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
+                    L->inv_perm, L->offsets, L->active, L->sched, L->staging};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    clear_graphs(L);
+    for (cudaEvent_t e : L->ev)
+        if (e) cudaEventDestroy(e);
+    if (L->stream) cudaStreamDestroy(L->stream);
+    delete L;
+}
+
+static int check_desc(const qrm_layer_desc* d) {
+    if (!d) return fail(QRM_E_INVALID, "desc is NULL");
+    if (d->d_model <= 0 || d->expert_ffn <= 0 || d->n_experts <= 0 || d->n_active <= 0)
+        return fail(QRM_E_INVALID, "d_model, expert_ffn, n_experts and n_active must be positive");
+    if (d->n_experts > qrm::kMaxE) return fail(QRM_E_CAPACITY, "n_experts %d > %d", d->n_experts, qrm::kMaxE);
+    if (std::min(d->n_active, 8) > d->n_experts) return fail(QRM_E_INVALID, "top-k exceeds n_experts");
+    if (d->d_model % 32 || d->expert_ffn % 32) return fail(QRM_E_INVALID, "d_model and expert_ffn must be multiples of 32");
+    if (d->d_model / 32 > qrm::kGemvMaxThreads || d->expert_ffn / 32 > qrm::kGemvMaxThreads)
+        return fail(QRM_E_CAPACITY, "rows longer than %d columns are not supported", 32 * qrm::kGemvMaxThreads);
+    if (d->max_tokens <= 0) return fail(QRM_E_INVALID, "max_tokens must be positive");
+    const int fm[6] = {d->fmt_gate, d->fmt_up, d->fmt_down, d->fmt_sh_gate, d->fmt_sh_up, d->fmt_sh_down};
+    const bool shared = d->moe_sigmoid && d->n_shared > 0;
+    for (int i = 0; i < (shared ? 6 : 3); i++) {
+        if (!qrm::is_expert_fmt(fm[i])) return fail(QRM_E_FORMAT, "format %d is not an expert format", fm[i]);
+        int bs, bb;
+        qrm::block_spec(fm[i], &bs, &bb);
+        int cols = (i % 3 == 2) ? d->expert_ffn : d->d_model;
+        if (cols % bs) return fail(QRM_E_INVALID, "%d columns are not a multiple of the %d-weight block", cols, bs);
+    }
+    if (d->fmt_gate != d->fmt_up || (shared && d->fmt_sh_gate != d->fmt_sh_up))
+        return fail(QRM_E_FORMAT, "gate and up must share a format");
+    return QRM_OK;
+}
+
+static int alloc_work(qrm_layer* L, int T) {
+    const int d = L->desc.d_model, E = L->desc.n_experts, f = L->desc.expert_ffn, k = L->k;
+    const size_t Tk = (size_t)T * k;
+    QRM_CUDA(cudaMalloc(&L->x, sizeof(float) * T * d));
+    QRM_CUDA(cudaMalloc(&L->xn, sizeof(float) * T * d));
+    QRM_CUDA(cudaMalloc(&L->out, sizeof(float) * T * d));
+    QRM_CUDA(cudaMalloc(&L->logits, sizeof(float) * T * E));
+    QRM_CUDA(cudaMalloc(&L->topk_w, sizeof(float) * Tk));
+    QRM_CUDA(cudaMalloc(&L->topk_idx, sizeof(int32_t) * Tk));
+    QRM_CUDA(cudaMalloc(&L->perm, sizeof(int32_t) * Tk));
+    QRM_CUDA(cudaMalloc(&L->inv_perm, sizeof(int32_t) * Tk));
+    QRM_CUDA(cudaMalloc(&L->offsets, sizeof(int32_t) * (E + 1)));
+    QRM_CUDA(cudaMalloc(&L->active, sizeof(int32_t) * (E + 1)));
+    QRM_CUDA(cudaMalloc(&L->sched, sizeof(qrm::Schedule)));
+    QRM_CUDA(cudaMemset(L->sched, 0, sizeof(qrm::Schedule)));
+    QRM_CUDA(cudaMalloc(&L->h, sizeof(float) * Tk * f));
+    QRM_CUDA(cudaMalloc(&L->y, sizeof(float) * Tk * d));
+    if (L->shared_enabled) {
+        QRM_CUDA(cudaMalloc(&L->hs, sizeof(float) * T * f));
+        QRM_CUDA(cudaMalloc(&L->ys, sizeof(float) * T * d));
+    }
+    L->cap_T = T;
+    return QRM_OK;
+}
+
+extern "C" int qrm_version(void) { return QRM_ABI_VERSION; }
+extern "C" const char* qrm_last_error(void) { return g_err.c_str(); }
+
+extern "C" int qrm_create(const qrm_layer_desc* desc, qrm_layer** out) {
+    if (!out) return fail(QRM_E_INVALID, "out is NULL");
+    *out = nullptr;
+    int rc = check_desc(desc);
+    if (rc) return rc;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(QRM_E_CUDA, "no CUDA device");
+    if (desc->device < 0 || desc->device >= ndev) return fail(QRM_E_INVALID, "device %d out of range", desc->device);
+    cudaDeviceProp prop;
+    QRM_CUDA(cudaGetDeviceProperties(&prop, desc->device));
+    if (prop.major != 10) return fail(QRM_E_CUDA, "device %d is sm_%d%d; libqrmoe is built for sm_100a", desc->device, prop.major, prop.minor);
+    QRM_CUDA(cudaSetDevice(desc->device));
+    qrm_layer* L = new qrm_layer();
+    L->desc = *desc;
+    L->k = std::min(desc->n_active, 8);
+    L->first_expert = 0;
+    L->n_local = desc->n_experts;
+    L->shared_enabled = desc->moe_sigmoid && desc->n_shared > 0;
+    L->sm_count = prop.multiProcessorCount;
+    auto bail = [&](int code) { free_layer(L); return code; };
+    if (cudaStreamCreateWithFlags(&L->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(QRM_E_CUDA, "stream creation failed"));
+    const int E = desc->n_experts, d = desc->d_model, f = desc->expert_ffn;
+    // slab for all matrices this layer holds
+    L->mats.assign((size_t)(E + 1) * 3, qrm::MatDev{});
+    L->mat_bytes.assign((size_t)(E + 1) * 3, 0);
+    L->uploaded.assign((size_t)(E + 1) * 3, 0);
+    size_t total = 0;
+    std::vector<size_t> off((size_t)(E + 1) * 3, 0);
+    for (int e = 0; e <= E; e++) {
+        bool sh = e == E;
+        if (sh && !L->shared_enabled) continue;
+        if (!sh && (e < L->first_expert || e >= L->first_expert + L->n_local)) continue;
+        for (int w = 0; w < 3; w++) {
+            int fmt = sh ? (&desc->fmt_sh_gate)[w] : (&desc->fmt_gate)[w];
+            int rows = w == 2 ? d : f, cols = w == 2 ? f : d;
+            int64_t nb = tensor_bytes(fmt, rows, cols);
+            size_t i = (size_t)e * 3 + w;
+            off[i] = total;
+            L->mat_bytes[i] = (size_t)nb;
+            int bs, bb;
+            qrm::block_spec(fmt, &bs, &bb);
+            L->mats[i] = qrm::MatDev{nullptr, fmt, rows, cols, 0, (int64_t)rows * cols / bs};
+            total += ((size_t)nb + 255) / 256 * 256;
+        }
+    }
+    if (cudaMalloc(&L->slab, total) != cudaSuccess)
+        return bail(fail(QRM_E_NOMEM, "cannot allocate %zu bytes of expert weights", total));
+    for (size_t i = 0; i < L->mats.size(); i++)
+        if (L->mat_bytes[i]) L->mats[i].base = L->slab + off[i];
+    if (cudaMalloc(&L->mats_dev, sizeof(qrm::MatDev) * L->mats.size()) != cudaSuccess ||
+        cudaMemcpy(L->mats_dev, L->mats.data(), sizeof(qrm::MatDev) * L->mats.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+        return bail(fail(QRM_E_NOMEM, "matrix table allocation failed"));
+    if (cudaMalloc(&L->norm_w, sizeof(float) * d) != cudaSuccess || cudaMalloc(&L->router, sizeof(float) * (size_t)E * d) != cudaSuccess ||
+        cudaMalloc(&L->router_bias, sizeof(float) * E) != cudaSuccess || cudaMalloc(&L->offset, sizeof(float) * E) != cudaSuccess)
+        return bail(fail(QRM_E_NOMEM, "router allocation failed"));
+    rc = alloc_work(L, desc->max_tokens);
+    if (rc) return bail(rc);
+    // kernels with large dynamic shared memory
+    if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+        return bail(fail(QRM_E_CUDA, "route kernel attribute"));
+    *out = L;
+    return QRM_OK;
+}
+
+extern "C" void qrm_destroy(qrm_layer* layer) { free_layer(layer); }
+
+extern "C" int qrm_upload_norm(qrm_layer* L, const float* w) {
+    if (!L || !w) return fail(QRM_E_INVALID, "NULL argument");
+    clear_graphs(L);
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    QRM_CUDA(cudaMemcpy(L->norm_w, w, sizeof(float) * L->desc.d_model, cudaMemcpyHostToDevice));
+    L->has_norm = true;
+    return QRM_OK;
+}
+
+extern "C" int qrm_upload_router(qrm_layer* L, const float* w, const float* bias) {
+    if (!L || !w) return fail(QRM_E_INVALID, "NULL argument");
+    clear_graphs(L);
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    QRM_CUDA(cudaMemcpy(L->router, w, sizeof(float) * (size_t)L->desc.n_experts * L->desc.d_model, cudaMemcpyHostToDevice));
+    if (bias) QRM_CUDA(cudaMemcpy(L->router_bias, bias, sizeof(float) * L->desc.n_experts, cudaMemcpyHostToDevice));
+    L->has_bias = bias != nullptr;
+    L->has_router = true;
+    return QRM_OK;
+}
+
+extern "C" int qrm_upload_logit_offset(qrm_layer* L, const float* offset) {
+    if (!L) return fail(QRM_E_INVALID, "NULL layer");
+    clear_graphs(L);
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    if (offset) QRM_CUDA(cudaMemcpy(L->offset, offset, sizeof(float) * L->desc.n_experts, cudaMemcpyHostToDevice));
+    L->has_offset = offset != nullptr;
+    return QRM_OK;
+}
+
+static int mat_index(qrm_layer* L, int expert, int which, size_t* idx) {
+    if (which < 0 || which > 2) return fail(QRM_E_INVALID, "which must be 0 (gate), 1 (up) or 2 (down)");
+    const int E = L->desc.n_experts;
+    int e;
+    if (expert == QRM_SHARED_EXPERT) {
+        if (!L->shared_enabled) return fail(QRM_E_INVALID, "this layer has no shared expert (needs moe_sigmoid and n_shared > 0)");
+        e = E;
+    } else {
+        if (expert < 0 || expert >= E) return fail(QRM_E_INVALID, "expert %d out of range [0, %d)", expert, E);
+        if (expert < L->first_expert || expert >= L->first_expert + L->n_local)
+            return fail(QRM_E_INVALID, "expert %d is not held by this layer", expert);
+        e = expert;
+    }
+    *idx = (size_t)e * 3 + which;
+    return QRM_OK;
+}
+
+static int upload_common(qrm_layer* L, int expert, int which, int fmt, const void* bytes, size_t nbytes, bool dev) {
+    if (!L || !bytes) return fail(QRM_E_INVALID, "NULL argument");
+    clear_graphs(L);
+    size_t i;
+    int rc = mat_index(L, expert, which, &i);
+    if (rc) return rc;
+    const qrm::MatDev& m = L->mats[i];
+    if (fmt != m.fmt)
+        return fail(QRM_E_FORMAT, "l.e%d.%s: format %d, layer expects %d", expert, which_name(which), fmt, m.fmt);
+    if (nbytes != L->mat_bytes[i])
+        return fail(QRM_E_SIZE, "l.e%d.%s: %zu bytes, TensorBytes(%d x %d) = %zu", expert, which_name(which), nbytes,
+                    m.rows, m.cols, L->mat_bytes[i]);
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    uint8_t* dst = const_cast<uint8_t*>(m.base);
+    if (fmt == qrm::Q4_K) {
+        QRM_CUDA(cudaMemcpyAsync(dst, bytes, nbytes, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, L->stream));
+    } else {
+        const uint8_t* src = (const uint8_t*)bytes;
+        if (!dev) {
+            if (L->staging_bytes < nbytes) {
+                if (L->staging) cudaFree(L->staging);
+                L->staging = nullptr;
+                L->staging_bytes = 0;
+                if (cudaMalloc(&L->staging, nbytes) != cudaSuccess) return fail(QRM_E_NOMEM, "staging allocation failed");
+                L->staging_bytes = nbytes;
+            }
+            QRM_CUDA(cudaMemcpyAsync(L->staging, bytes, nbytes, cudaMemcpyHostToDevice, L->stream));
+            src = L->staging;
+        }
+        int bs, bb;
+        qrm::block_spec(fmt, &bs, &bb);
+        long long nb = (long long)(nbytes / bb);
+        qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(fmt, bb, src, dst, nb, 1);
+        QRM_CUDA(cudaGetLastError());
+    }
+    QRM_CUDA(cudaStreamSynchronize(L->stream));
+    L->uploaded[i] = 1;
+    return QRM_OK;
+}
+
+extern "C" int qrm_upload_expert(qrm_layer* L, int expert, int which, int fmt, const void* bytes, size_t nbytes) {
+    return upload_common(L, expert, which, fmt, bytes, nbytes, false);
+}
+extern "C" int qrm_upload_expert_device(qrm_layer* L, int expert, int which, int fmt, const void* bytes_dev, size_t nbytes) {
+    return upload_common(L, expert, which, fmt, bytes_dev, nbytes, true);
+}
+
+extern "C" int qrm_download_expert(qrm_layer* L, int expert, int which, void* bytes, size_t nbytes) {
+    if (!L || !bytes) return fail(QRM_E_INVALID, "NULL argument");
+    size_t i;
+    int rc = mat_index(L, expert, which, &i);
+    if (rc) return rc;
+    if (!L->uploaded[i]) return fail(QRM_E_STATE, "l.e%d.%s was never uploaded", expert, which_name(which));
+    if (nbytes != L->mat_bytes[i]) return fail(QRM_E_SIZE, "buffer is %zu bytes, tensor is %zu", nbytes, L->mat_bytes[i]);
+    const qrm::MatDev& m = L->mats[i];
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    if (m.fmt == qrm::Q4_K) {
+        QRM_CUDA(cudaMemcpy(bytes, m.base, nbytes, cudaMemcpyDeviceToHost));
+        return QRM_OK;
+    }
+    uint8_t* tmp = nullptr;
+    QRM_CUDA(cudaMalloc(&tmp, nbytes));
+    int bs, bb;
+    qrm::block_spec(m.fmt, &bs, &bb);
+    qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, m.base, tmp, (long long)(nbytes / bb), 0);
+    cudaError_t e1 = cudaStreamSynchronize(L->stream);
+    cudaError_t e2 = cudaMemcpy(bytes, tmp, nbytes, cudaMemcpyDeviceToHost);
+    cudaFree(tmp);
+    if (e1 != cudaSuccess || e2 != cudaSuccess) return fail(QRM_E_CUDA, "download failed: %s", cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
+    return QRM_OK;
+}
+
+static int forward_checks(qrm_layer* L, int T, int flags) {
+    if (T <= 0) return fail(QRM_E_INVALID, "T must be positive");
+    if (T > L->cap_T) return fail(QRM_E_CAPACITY, "T = %d exceeds max_tokens = %d", T, L->cap_T);
+    if (!L->has_router) return fail(QRM_E_STATE, "tensor l.router was never uploaded");
+    if ((flags & QRM_APPLY_NORM) && !L->has_norm) return fail(QRM_E_STATE, "tensor l.ffn_norm was never uploaded");
+    if (flags & ~(QRM_APPLY_NORM | QRM_ADD_RESIDUAL)) return fail(QRM_E_INVALID, "unknown flags 0x%x", flags);
+    const int E = L->desc.n_experts;
+    for (int e = L->first_expert; e < L->first_expert + L->n_local; e++)
+        for (int w = 0; w < 3; w++)
+            if (!L->uploaded[(size_t)e * 3 + w]) return fail(QRM_E_STATE, "tensor l.e%d.%s was never uploaded", e, which_name(w));
+    if (L->shared_enabled) {
+        int n = L->uploaded[(size_t)E * 3] + L->uploaded[(size_t)E * 3 + 1] + L->uploaded[(size_t)E * 3 + 2];
+        if (n != 0 && n != 3) return fail(QRM_E_STATE, "shared expert is only partly uploaded");
+    }
+    return QRM_OK;
+}
+
+static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* topk_idx,
+                          float* topk_w, cudaStream_t s) {
+    const qrm_layer_desc& D = L->desc;
+    const int d = D.d_model, E = D.n_experts, f = D.expert_ffn, k = L->k;
+    const bool shared = L->shared_enabled && L->uploaded[(size_t)E * 3];
+    const bool prof = L->profiling;
+    auto mark = [&](int i) { if (prof) cudaEventRecord(L->ev[i], s); };
+    mark(0);
+    // 1. RMSNorm + router logits
+    const float* xn = L->xn;
+    if (T <= qrm::route_small_max_tokens(d)) {
+        qrm::RouteParams rp{x, L->norm_w, L->router, L->has_offset ? L->offset : nullptr, L->xn, L->logits, T, d, E,
+                            (flags & QRM_APPLY_NORM) ? 1 : 0, D.rms_eps};
+        int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
+        qrm::route_small_kernel<<<grid, qrm::kRouteThreads, qrm::route_small_smem(d, T), s>>>(rp);
+    } else {
+        if (flags & QRM_APPLY_NORM) {
+            qrm::rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, L->norm_w, L->xn, T, d, D.rms_eps);
+        } else {
+            xn = x;
+        }
+        dim3 grid((T + qrm::kLT - 1) / qrm::kLT, (E + qrm::kLE - 1) / qrm::kLE);
+        qrm::logits_tiled_kernel<<<grid, 256, 0, s>>>(xn, L->router, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
+    }
+    QRM_CUDA(cudaGetLastError());
+    mark(1);
+    L->last_xn = xn;
+    // 2. top-k
+    qrm::TopkParams tp{L->logits, L->has_bias ? L->router_bias : nullptr, topk_idx, topk_w, T, E, k,
+                       D.moe_sigmoid ? 1 : 0, D.routed_scale};
+    qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
+    QRM_CUDA(cudaGetLastError());
+    mark(2);
+    // 3. dispatch
+    qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->offsets, L->active, L->sched, T, k, E,
+                           L->first_expert, L->n_local, shared ? 1 : 0};
+    qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, 0, s>>>(dp);
+    QRM_CUDA(cudaGetLastError());
+    mark(3);
+    // 4. gate/up (+ SwiGLU) and 5. down
+    const int nt = pick_nt(T);
+    const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU
+    const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
+    for (int stage = 0; stage < 2; stage++) {
+        const bool gu = stage == 0;
+        qrm::GemvParams gp{};
+        gp.mats = L->mats_dev;
+        gp.active = L->active;
+        gp.offsets = L->offsets;
+        gp.perm = L->perm;
+        gp.n_active = &L->sched->n_active;
+        gp.x_routed = gu ? xn : L->h;
+        gp.x_shared = gu ? xn : L->hs;
+        gp.out_routed = gu ? L->h : L->y;
+        gp.out_shared = gu ? L->hs : L->ys;
+        gp.T = T;
+        gp.k = k;
+        gp.E = E;
+        gp.rows = gu ? f : d;
+        gp.cols = gu ? d : f;
+        gp.tiles = (gp.rows + (gu ? kRGateUp : kRDown) - 1) / (gu ? kRGateUp : kRDown);
+        gp.limit = limit;
+        gp.routed_by_token = gu ? 1 : 0;
+        gp.has_shared = shared ? 1 : 0;
+        const int fr = gu ? D.fmt_gate : D.fmt_down;
+        const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
+        if (same_fmt) {
+            gp.mode = 0;
+            gp.ctr = &L->sched->ctr[gu ? 0 : 2];
+            int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, s);
+            if (rc) return rc;
+        } else {
+            gp.mode = 1;
+            gp.ctr = &L->sched->ctr[gu ? 0 : 2];
+            int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, s);
+            if (rc) return rc;
+            gp.mode = 2;
+            gp.ctr = &L->sched->ctr[gu ? 1 : 3];
+            rc = launch_gemv(fs, gu, nt, gp, L->sm_count, s);
+            if (rc) return rc;
+        }
+        mark(gu ? 4 : 5);
+    }
+    // 6. combine
+    qrm::CombineParams cp{(flags & QRM_ADD_RESIDUAL) ? x : nullptr, L->y, shared ? L->ys : nullptr, L->inv_perm,
+                          topk_w, out, T, k, d};
+    long long n4 = (long long)T * (d / 4);
+    int cgrid = (int)std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 16);
+    qrm::combine_kernel<<<cgrid, 256, 0, s>>>(cp);
+    QRM_CUDA(cudaGetLastError());
+    mark(6);
+    L->last_T = T;
+    L->profiled_last = prof;
+    L->last_shared = shared;
+    return QRM_OK;
+}
+
+// Runs the forward as a CUDA graph (captured once per buffer set, T, flags
+// and profiling state; uploads invalidate the cache) launched on `s`.
+static int run_forward(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* idx, float* w,
+                       cudaStream_t s) {
+    qrm_layer::GraphKey key{x, out, idx, w, T, flags, L->profiling ? 1 : 0};
+    auto it = L->graphs.find(key);
+    if (it == L->graphs.end()) {
+        if (L->graphs.size() >= 32) clear_graphs(L);
+        QRM_CUDA(cudaStreamBeginCapture(L->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = launch_forward(L, x, T, flags, out, idx, w, L->stream);
+        cudaGraph_t g = nullptr;
+        cudaError_t ce = cudaStreamEndCapture(L->stream, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ce != cudaSuccess) return fail(QRM_E_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+        cudaGraphExec_t ex = nullptr;
+        ce = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) return fail(QRM_E_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
+        it = L->graphs.emplace(key, ex).first;
+    }
+    QRM_CUDA(cudaGraphLaunch(it->second, s));
+    L->last_T = T;
+    L->profiled_last = L->profiling;
+    L->last_xn = (T > qrm::route_small_max_tokens(L->desc.d_model) && !(flags & QRM_APPLY_NORM)) ? x : L->xn;
+    return QRM_OK;
+}
+
+extern "C" int qrm_forward_device(qrm_layer* L, const float* x_dev, int T, int flags, float* out_dev,
+                                  int32_t* topk_idx_dev, float* topk_w_dev, void* stream) {
+    if (!L || !x_dev || !out_dev) return fail(QRM_E_INVALID, "NULL argument");
+    int rc = forward_checks(L, T, flags);
+    if (rc) return rc;
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    cudaStream_t s = stream ? (cudaStream_t)stream : L->stream;
+    return run_forward(L, x_dev, T, flags, out_dev, topk_idx_dev ? topk_idx_dev : L->topk_idx,
+                       topk_w_dev ? topk_w_dev : L->topk_w, s);
+}
+
+extern "C" int qrm_sync(qrm_layer* L) {
+    if (!L) return fail(QRM_E_INVALID, "NULL layer");
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    QRM_CUDA(cudaDeviceSynchronize());
+    int32_t err = 0;
+    QRM_CUDA(cudaMemcpy(&err, &L->sched->err, sizeof(int32_t), cudaMemcpyDeviceToHost));
+    if (err) {
+        QRM_CUDA(cudaMemset(&L->sched->err, 0, sizeof(int32_t)));
+        if (err & qrm::ERR_TIMEOUT) return fail(QRM_E_TIMEOUT, "a device wait timed out");
+        return fail(QRM_E_INVALID, "device reported error flags 0x%x (expert index out of range)", err);
+    }
+    return QRM_OK;
+}
+
+extern "C" int qrm_forward(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* topk_idx, float* topk_w) {
+    if (!L || !x || !out) return fail(QRM_E_INVALID, "NULL argument");
+    int rc = forward_checks(L, T, flags);
+    if (rc) return rc;
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    const size_t xb = sizeof(float) * (size_t)T * L->desc.d_model;
+    QRM_CUDA(cudaMemcpyAsync(L->x, x, xb, cudaMemcpyHostToDevice, L->stream));
+    rc = run_forward(L, L->x, T, flags, L->out, L->topk_idx, L->topk_w, L->stream);
+    if (rc) return rc;
+    QRM_CUDA(cudaMemcpyAsync(out, L->out, xb, cudaMemcpyDeviceToHost, L->stream));
+    if (topk_idx) QRM_CUDA(cudaMemcpyAsync(topk_idx, L->topk_idx, sizeof(int32_t) * T * L->k, cudaMemcpyDeviceToHost, L->stream));
+    if (topk_w) QRM_CUDA(cudaMemcpyAsync(topk_w, L->topk_w, sizeof(float) * T * L->k, cudaMemcpyDeviceToHost, L->stream));
+    QRM_CUDA(cudaStreamSynchronize(L->stream));
+    return qrm_sync(L);
+}
+
+extern "C" int qrm_last_dispatch(qrm_layer* L, int32_t* perm, int32_t* offsets) {
+    if (!L) return fail(QRM_E_INVALID, "NULL layer");
+    if (!L->last_T) return fail(QRM_E_STATE, "no forward has run");
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    QRM_CUDA(cudaDeviceSynchronize());
+    if (perm) QRM_CUDA(cudaMemcpy(perm, L->perm, sizeof(int32_t) * L->last_T * L->k, cudaMemcpyDeviceToHost));
+    if (offsets) QRM_CUDA(cudaMemcpy(offsets, L->offsets, sizeof(int32_t) * (L->desc.n_experts + 1), cudaMemcpyDeviceToHost));
+    return QRM_OK;
+}
+
+extern "C" int qrm_last_router(qrm_layer* L, float* logits, float* xn) {
+    if (!L) return fail(QRM_E_INVALID, "NULL layer");
+    if (!L->last_T) return fail(QRM_E_STATE, "no forward has run");
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    QRM_CUDA(cudaDeviceSynchronize());
+    if (logits) QRM_CUDA(cudaMemcpy(logits, L->logits, sizeof(float) * L->last_T * L->desc.n_experts, cudaMemcpyDeviceToHost));
+    if (xn) QRM_CUDA(cudaMemcpy(xn, L->last_xn, sizeof(float) * L->last_T * L->desc.d_model, cudaMemcpyDeviceToHost));
+    return QRM_OK;
+}
+
+extern "C" int qrm_set_profiling(qrm_layer* L, int on) {
+    if (!L) return fail(QRM_E_INVALID, "NULL layer");
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    if (on && !L->ev[0])
+        for (cudaEvent_t& e : L->ev) QRM_CUDA(cudaEventCreate(&e));
+    L->profiling = on != 0;
+    return QRM_OK;
+}
+
+extern "C" int qrm_last_profile(qrm_layer* L, float* ms, double* bytes) {
+    if (!L) return fail(QRM_E_INVALID, "NULL layer");
+    if (!L->last_T || !L->profiled_last) return fail(QRM_E_STATE, "the last forward ran without profiling");
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    QRM_CUDA(cudaEventSynchronize(L->ev[QRM_STAGE_COUNT]));
+    if (ms)
+        for (int i = 0; i < QRM_STAGE_COUNT; i++) QRM_CUDA(cudaEventElapsedTime(&ms[i], L->ev[i], L->ev[i + 1]));
+    if (bytes) {
+        int32_t na = 0;
+        QRM_CUDA(cudaMemcpy(&na, &L->sched->n_active, sizeof na, cudaMemcpyDeviceToHost));
+        const int E = L->desc.n_experts, T = L->last_T, k = L->k;
+        const double d = L->desc.d_model, f = L->desc.expert_ffn;
+        const size_t e0 = (size_t)L->first_expert * 3;
+        double gu = (double)na * (L->mat_bytes[e0] + L->mat_bytes[e0 + 1]);
+        double dn = (double)na * L->mat_bytes[e0 + 2];
+        int tok_sh = L->last_shared ? T : 0;
+        if (L->last_shared) {
+            gu += (double)L->mat_bytes[(size_t)E * 3] + L->mat_bytes[(size_t)E * 3 + 1];
+            dn += (double)L->mat_bytes[(size_t)E * 3 + 2];
+        }
+        // activations: xn read once, h written / read once, y written once
+        gu += 4.0 * (T * d + ((double)T * k + tok_sh) * f);
+        dn += 4.0 * (((double)T * k + tok_sh) * f + ((double)T * k + tok_sh) * d);
+        for (int i = 0; i < QRM_STAGE_COUNT; i++) bytes[i] = 0;
+        bytes[QRM_STAGE_GATEUP] = gu;
+        bytes[QRM_STAGE_DOWN] = dn;
+    }
+    return QRM_OK;
+}
+
+// ---------------------------------------------------------------- matrix operator
+
+struct qrm_matrix {
+    int device = 0;
+    int sm_count = 0;
+    int64_t bytes = 0;
+    qrm::MatDev mat{};
+    qrm::MatDev* mats_dev = nullptr;  // [3]; slot 2 is the matrix
+    uint8_t* data = nullptr;
+    int32_t* misc = nullptr;          // active[1], offsets[2], n_active, ctr
+};
+
+extern "C" int qrm_matrix_create(int device, int fmt, int64_t rows, int64_t cols, const void* bytes, size_t nbytes,
+                                 qrm_matrix** out) {
+    if (!out || !bytes) return fail(QRM_E_INVALID, "NULL argument");
+    *out = nullptr;
+    if (!qrm::is_expert_fmt(fmt)) return fail(QRM_E_FORMAT, "format %d has no GPU kernel", fmt);
+    if (rows <= 0 || cols <= 0 || cols % 32 || cols / 32 > qrm::kGemvMaxThreads || rows > (1 << 30))
+        return fail(QRM_E_INVALID, "unsupported shape %lld x %lld", (long long)rows, (long long)cols);
+    int64_t nb = tensor_bytes(fmt, rows, cols);
+    if (nb < 0) return fail(QRM_E_INVALID, "cols %lld not a multiple of the block size", (long long)cols);
+    if ((size_t)nb != nbytes) return fail(QRM_E_SIZE, "%zu bytes, TensorBytes = %lld", nbytes, (long long)nb);
+    cudaDeviceProp prop;
+    QRM_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(QRM_E_CUDA, "device %d is not sm_100", device);
+    QRM_CUDA(cudaSetDevice(device));
+    qrm_matrix* M = new qrm_matrix();
+    M->device = device;
+    M->sm_count = prop.multiProcessorCount;
+    M->bytes = nb;
+    auto bail = [&](int code) {
+        if (M->data) cudaFree(M->data);
+        if (M->mats_dev) cudaFree(M->mats_dev);
+        if (M->misc) cudaFree(M->misc);
+        delete M;
+        return code;
+    };
+    uint8_t* staging = nullptr;
+    if (cudaMalloc(&M->data, nbytes) != cudaSuccess || cudaMalloc(&staging, nbytes) != cudaSuccess)
+        return bail(fail(QRM_E_NOMEM, "matrix allocation failed"));
+    cudaMemcpy(staging, bytes, nbytes, cudaMemcpyHostToDevice);
+    int bs, bb;
+    qrm::block_spec(fmt, &bs, &bb);
+    if (fmt == qrm::Q4_K) cudaMemcpy(M->data, staging, nbytes, cudaMemcpyDeviceToDevice);
+    else qrm::relayout_kernel<<<M->sm_count * 8, 256>>>(fmt, bb, staging, M->data, (long long)(nbytes / bb), 1);
+    cudaError_t e = cudaDeviceSynchronize();
+    cudaFree(staging);
+    if (e != cudaSuccess) return bail(fail(QRM_E_CUDA, "matrix upload: %s", cudaGetErrorString(e)));
+    M->mat = qrm::MatDev{M->data, fmt, (int32_t)rows, (int32_t)cols, 0, rows * cols / bs};
+    qrm::MatDev tab[3] = {M->mat, M->mat, M->mat};
+    int32_t misc[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // active[0]=0, offsets, n_active=0, ctr
+    if (cudaMalloc(&M->mats_dev, sizeof tab) != cudaSuccess || cudaMalloc(&M->misc, sizeof misc) != cudaSuccess)
+        return bail(fail(QRM_E_NOMEM, "matrix table allocation failed"));
+    cudaMemcpy(M->mats_dev, tab, sizeof tab, cudaMemcpyHostToDevice);
+    cudaMemcpy(M->misc, misc, sizeof misc, cudaMemcpyHostToDevice);
+    *out = M;
+    return QRM_OK;
+}
+
+extern "C" void qrm_matrix_destroy(qrm_matrix* M) {
+    if (!M) return;
+    cudaSetDevice(M->device);
+    cudaDeviceSynchronize();
+    if (M->data) cudaFree(M->data);
+    if (M->mats_dev) cudaFree(M->mats_dev);
+    if (M->misc) cudaFree(M->misc);
+    delete M;
+}
+
+extern "C" int qrm_matrix_gemv(qrm_matrix* M, const float* x_dev, int T, float* y_dev, void* stream) {
+    if (!M || !x_dev || !y_dev) return fail(QRM_E_INVALID, "NULL argument");
+    if (T <= 0) return fail(QRM_E_INVALID, "T must be positive");
+    QRM_CUDA(cudaSetDevice(M->device));
+    cudaStream_t s = (cudaStream_t)stream;
+    // the matrix runs as the "shared expert" slot of a one-expert layer
+    QRM_CUDA(cudaMemsetAsync(M->misc + 4, 0, sizeof(int32_t), s));
+    qrm::GemvParams gp{};
+    gp.mats = M->mats_dev;
+    gp.active = M->misc;        // active[0] = 0
+    gp.offsets = M->misc + 1;
+    gp.perm = M->misc;
+    gp.n_active = M->misc + 3;  // 0 routed slots
+    gp.ctr = M->misc + 4;
+    gp.x_routed = x_dev;
+    gp.x_shared = x_dev;
+    gp.out_routed = y_dev;
+    gp.out_shared = y_dev;
+    gp.T = T;
+    gp.k = 1;
+    gp.E = 0;
+    gp.rows = M->mat.rows;
+    gp.cols = M->mat.cols;
+    gp.tiles = (gp.rows + kRDown - 1) / kRDown;
+    gp.limit = 0.f;
+    gp.routed_by_token = 0;
+    gp.mode = 2;
+    gp.has_shared = 1;
+    return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, s);
+}
+
+// ---------------------------------------------------------------- synthetic data
+
+extern "C" int qrm_synth_gaussian(float* dst_dev, int64_t n, uint64_t seed, float sigma, void* stream) {
+    if (!dst_dev) return fail(QRM_E_INVALID, "NULL argument");
+    int rc = qrm_synth_gaussian_impl(dst_dev, n, seed, sigma, (cudaStream_t)stream);
+    return rc ? fail(rc, "synthetic Gaussian launch failed") : QRM_OK;
+}
+
+extern "C" int qrm_synth_quantize(int fmt, const float* src_dev, int64_t n, void* dst_dev, void* stream) {
+    if (!src_dev || !dst_dev) return fail(QRM_E_INVALID, "NULL argument");
+    int rc = qrm_synth_quantize_impl(fmt, src_dev, n, dst_dev, (cudaStream_t)stream);
+    return rc ? fail(rc, "quantiser launch failed (format %d, n %lld)", fmt, (long long)n) : QRM_OK;
+}

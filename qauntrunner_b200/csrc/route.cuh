@@ -1,0 +1,474 @@
+// route.cuh -- RMSNorm, router logits, top-k and dispatch.
+//
+// Routing must reproduce the reference bit for bit, so these kernels emulate
+// the reference's float operation order exactly (no FMA contraction: every
+// product and sum goes through __fmul_rn / __fadd_rn):
+//  * TransformerOps.RmsNorm (TransformerOps.cs:12-40): eight lane sums
+//    acc[j] over columns c = j mod 8, each a sequential chain of
+//    acc + x*x, then HSum (SimdMath.cs:17-22) = ((0+acc0)+acc1)+...+acc7,
+//    the tail columns, scale = 1/sqrt(ss/n + eps), out = (x*scale)*w.
+//  * Router logits = SimdMath.DotF32 (SimdMath.cs:34-53) of each router row
+//    with xn, the same eight-chain structure.
+//  * Softmax (StreamingEngine.cs:642-647) with a sequential sum, SelectTopK
+//    (801-810); GLM sigmoid + bias + SelectTopKIndices (730-767, 793-799).
+// A chain of d/8 dependent adds cannot be split, so parallelism comes from
+// running the T*E*8 chains side by side.
+#pragma once
+#include "common.cuh"
+#include "glibc_expf.cuh"
+
+namespace qrm {
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// Sequential HSum of eight lane accumulators (SimdMath.HSum).
+__device__ __forceinline__ float hsum8_seq(const float* a) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) s = __fadd_rn(s, a[i]);
+    return s;
+}
+
+// ---------------------------------------------------------------------------
+// Small-T router: each CTA owns EPC experts and all T tokens (T <= 8 and
+// small enough for shared memory), loads the router rows and the inputs into
+// shared memory with cp.async (all bytes in flight at once, one commit group
+// per column chunk), recomputes the RMSNorm of its tokens in place and runs
+// the T*EPC*8 logit chains.  CTA 0 also writes xn for the expert kernels.
+// Shared memory: W[EPC][d] | X[T][d] (normalised in place) | red | scl.
+constexpr int kSmallT = 8;
+constexpr int kRouteEPC = 2;
+constexpr int kRouteThreads = 128;
+constexpr int kRouteChunks = 4;
+
+struct RouteParams {
+    const float* x;        // [T x d]
+    const float* norm_w;   // [d] or null
+    const float* router;   // [E x d]
+    const float* offset;   // [E] or null
+    float* xn;             // [T x d] out
+    float* logits;         // [T x E] out
+    int T, d, E;
+    int apply_norm;
+    float eps;
+};
+
+inline size_t route_small_smem(int d, int T) {
+    return sizeof(float) * ((size_t)(kRouteEPC + T) * d + (size_t)T * kRouteEPC * 8 + T);
+}
+inline int route_small_max_tokens(int d) {
+    int t = kSmallT;
+    while (t > 0 && route_small_smem(d, t) > 220 * 1024) t--;
+    return t;
+}
+
+template <int C>
+__device__ __forceinline__ void cp_async_wait_chunk() {
+    cp_async_wait<kRouteChunks - 1 - C>();
+}
+
+__global__ void __launch_bounds__(kRouteThreads)
+route_small_kernel(RouteParams p) {
+    extern __shared__ __align__(16) float smem[];
+    const int d = p.d, T = p.T;
+    const int e0 = blockIdx.x * kRouteEPC;
+    const int ne = min(kRouteEPC, p.E - e0);
+    float* W = smem;                        // [EPC][d]
+    float* X = W + kRouteEPC * d;           // [T][d]
+    float* red = X + T * d;                 // [T*EPC*8]
+    float* scl = red + T * kRouteEPC * 8;   // [T]
+    const int tid = threadIdx.x;
+    const int d4 = d / 4;                   // d % 4 == 0 (host check)
+    const int d8 = d / 8 * 8;
+    const int g8 = d8 / 8;
+    const int chg = (g8 + kRouteChunks - 1) / kRouteChunks;   // 8-column groups per chunk
+
+    // issue every load now; chunk c = columns [8*c*chg, 8*(c+1)*chg), the
+    // last chunk also carries the < 8 tail columns
+    for (int c = 0; c < kRouteChunks; c++) {
+        int lo = min(d4, 2 * c * chg);
+        int hi = (c == kRouteChunks - 1) ? d4 : min(d4, 2 * (c + 1) * chg);
+        int w4 = hi - lo, rows = ne + T;
+        for (int i = tid; i < rows * w4; i += kRouteThreads) {
+            int r = i / w4, q = lo + i % w4;
+            if (r < ne) cp_async16(W + r * d + 4 * q, p.router + (size_t)(e0 + r) * d + 4 * q);
+            else cp_async16(X + (r - ne) * d + 4 * q, p.x + (size_t)(r - ne) * d + 4 * q);
+        }
+        cp_async_commit();
+    }
+
+    // RMSNorm chains, thread (t, j) for t < T, j < 8, chunk by chunk as data lands
+    const bool norm_thread = p.apply_norm && tid < T * 8;
+    const int nt = tid >> 3, nj = tid & 7;
+    float acc = 0.f;
+#define QRM_ROUTE_CHUNK(C)                                                        \
+    cp_async_wait_chunk<C>();                                                     \
+    __syncthreads();                                                              \
+    if (norm_thread) {                                                            \
+        const float* xr = X + nt * d;                                             \
+        int stop = min(d8, 8 * ((C) + 1) * chg);                                  \
+        for (int i = 8 * (C) * chg; i < stop; i += 8) {                           \
+            float v = xr[i + nj];                                                 \
+            acc = __fadd_rn(acc, __fmul_rn(v, v));                                \
+        }                                                                         \
+    }
+    QRM_ROUTE_CHUNK(0)
+    QRM_ROUTE_CHUNK(1)
+    QRM_ROUTE_CHUNK(2)
+    QRM_ROUTE_CHUNK(3)
+#undef QRM_ROUTE_CHUNK
+    if (p.apply_norm) {
+        if (norm_thread) red[nt * 8 + nj] = acc;
+        __syncthreads();
+        if (tid < T) {
+            const float* xr = X + tid * d;
+            float ss = 0.f;
+            int i = 0;
+            if (d >= 8) { ss = hsum8_seq(red + tid * 8); i = d8; }
+            for (; i < d; i++) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+            float v = __fadd_rn(__fdiv_rn(ss, (float)d), p.eps);
+            scl[tid] = __fdiv_rn(1.f, __fsqrt_rn(v));
+        }
+        __syncthreads();
+        for (int i = tid; i < T * d; i += kRouteThreads) {
+            int t = i / d, c = i - t * d;
+            float v = __fmul_rn(X[i], scl[t]);
+            if (p.norm_w) v = __fmul_rn(v, p.norm_w[c]);
+            X[i] = v;
+        }
+        __syncthreads();
+    }
+    if (blockIdx.x == 0)
+        for (int i = tid; i < T * d; i += kRouteThreads) p.xn[i] = X[i];
+
+    // logit chains: thread (t, e, j)
+    const int lt = tid / (kRouteEPC * 8), le = (tid >> 3) % kRouteEPC, lj = tid & 7;
+    const bool lthread = lt < T && le < ne;
+    if (lthread) {
+        const float* wr = W + le * d;
+        const float* xr = X + lt * d;
+        float la = 0.f;
+        for (int i = 0; i < d8; i += 8) la = __fadd_rn(la, __fmul_rn(wr[i + lj], xr[i + lj]));
+        red[(lt * kRouteEPC + le) * 8 + lj] = la;
+    }
+    __syncthreads();
+    if (tid < T * ne) {
+        int t = tid / ne, e = tid - t * ne;
+        const float* wr = W + e * d;
+        const float* xr = X + t * d;
+        float s = 0.f;
+        int i = 0;
+        if (d >= 8) { s = hsum8_seq(red + (t * kRouteEPC + e) * 8); i = d8; }
+        for (; i < d; i++) s = __fadd_rn(s, __fmul_rn(wr[i], xr[i]));
+        if (p.offset) s = __fadd_rn(s, p.offset[e0 + e]);
+        p.logits[(size_t)t * p.E + e0 + e] = s;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Large-T RMSNorm: one warp per token; lanes 0..7 run the eight chains.
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               float* __restrict__ xn, int T, int d, float eps) {
+    int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (warp >= T) return;
+    const float* xr = x + (size_t)warp * d;
+    const int d8 = d / 8 * 8;
+    float acc = 0.f;
+    if (lane < 8 && d >= 8)
+        for (int i = lane; i < d8; i += 8) acc = __fadd_rn(acc, __fmul_rn(xr[i], xr[i]));
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) a[j] = __shfl_sync(0xffffffffu, acc, j);
+    float ss = 0.f;
+    int i0 = 0;
+    if (d >= 8) { ss = hsum8_seq(a); i0 = d8; }
+    for (int i = i0; i < d; i++) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+    float scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
+    float* o = xn + (size_t)warp * d;
+    for (int i = lane; i < d; i += 32) {
+        float v = __fmul_rn(xr[i], scale);
+        if (w) v = __fmul_rn(v, w[i]);
+        o[i] = v;
+    }
+}
+
+// Large-T router logits: CTA tile of 16 tokens x 16 experts, 256 threads,
+// thread = (token pair, expert quad, lane j) -> 8 independent chains.
+constexpr int kLT = 16, kLE = 16, kLCH = 64;
+__global__ void __launch_bounds__(256)
+logits_tiled_kernel(const float* __restrict__ xn, const float* __restrict__ router,
+                    const float* __restrict__ offset, float* __restrict__ logits, int T, int d, int E) {
+    __shared__ __align__(16) float Xs[2][kLT][kLCH];
+    __shared__ __align__(16) float Ws[2][kLE][kLCH];
+    __shared__ float red[kLT][kLE][9];
+    const int tid = threadIdx.x;
+    const int j = tid & 7, eg = (tid >> 3) & 3, tg = tid >> 5;
+    const int t0 = blockIdx.x * kLT, e0 = blockIdx.y * kLE;
+    const int d8 = d / 8 * 8;
+    const int nch = d8 / kLCH;               // full chunks (d8 % 64 handled below)
+    float acc[2][4];
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) acc[a][b] = 0.f;
+
+    auto load = [&](int buf, int c) {
+        // 16 rows x 64 cols each of X and W: 2 * 256 float4 -> 2 per thread
+        for (int i = tid; i < 2 * kLT * (kLCH / 4); i += 256) {
+            int isw = i >= kLT * (kLCH / 4);
+            int k = isw ? i - kLT * (kLCH / 4) : i;
+            int r = k / (kLCH / 4), q = k % (kLCH / 4);
+            if (!isw) {
+                int t = t0 + r;
+                if (t < T) cp_async16(&Xs[buf][r][4 * q], xn + (size_t)t * d + c * kLCH + 4 * q);
+                else *(float4*)&Xs[buf][r][4 * q] = make_float4(0, 0, 0, 0);
+            } else {
+                int e = e0 + r;
+                if (e < E) cp_async16(&Ws[buf][r][4 * q], router + (size_t)e * d + c * kLCH + 4 * q);
+                else *(float4*)&Ws[buf][r][4 * q] = make_float4(0, 0, 0, 0);
+            }
+        }
+        cp_async_commit();
+    };
+    if (nch > 0) load(0, 0);
+    for (int c = 0; c < nch; c++) {
+        if (c + 1 < nch) { load((c + 1) & 1, c + 1); cp_async_wait<1>(); }
+        else cp_async_wait<0>();
+        __syncthreads();
+        const int b = c & 1;
+#pragma unroll
+        for (int s = 0; s < kLCH / 8; s++) {
+            const int col = 8 * s + j;
+            float xv0 = Xs[b][2 * tg][col], xv1 = Xs[b][2 * tg + 1][col];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                float wv = Ws[b][4 * eg + q][col];
+                acc[0][q] = __fadd_rn(acc[0][q], __fmul_rn(wv, xv0));
+                acc[1][q] = __fadd_rn(acc[1][q], __fmul_rn(wv, xv1));
+            }
+        }
+        __syncthreads();
+    }
+    // remaining full groups of 8 columns beyond the last 64-column chunk
+    for (int i = nch * kLCH; i < d8; i += 8) {
+#pragma unroll
+        for (int a = 0; a < 2; a++) {
+            int t = t0 + 2 * tg + a;
+            float xv = t < T ? xn[(size_t)t * d + i + j] : 0.f;
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                int e = e0 + 4 * eg + q;
+                float wv = e < E ? router[(size_t)e * d + i + j] : 0.f;
+                acc[a][q] = __fadd_rn(acc[a][q], __fmul_rn(wv, xv));
+            }
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 2; a++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) red[2 * tg + a][4 * eg + q][j] = acc[a][q];
+    __syncthreads();
+    {
+        int tt = tid >> 4, ee = tid & 15;
+        int t = t0 + tt, e = e0 + ee;
+        if (t < T && e < E) {
+            float s;
+            int i;
+            if (d >= 8) { s = hsum8_seq(red[tt][ee]); i = d8; }
+            else { s = 0.f; i = 0; }
+            for (; i < d; i++) s = __fadd_rn(s, __fmul_rn(router[(size_t)e * d + i], xn[(size_t)t * d + i]));
+            if (offset) s = __fadd_rn(s, offset[e]);
+            logits[(size_t)t * E + e] = s;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Top-k: one warp per token.
+// Ranking = Array.Sort(idx, (a, b) => v[b].CompareTo(v[a])): value
+// descending, NaN last; exact ties by index ascending.
+__device__ __forceinline__ bool rank_before(float va, int ia, float vb, int ib) {
+    bool na = isnan(va), nb = isnan(vb);
+    if (na != nb) return nb;
+    if (!na && va != vb) return va > vb;
+    return ia < ib;
+}
+
+constexpr int kMaxE = 512;   // GlmMoeFfn caps n_experts at 512 (StreamingEngine.cs:733)
+constexpr int kMaxK = 8;     // StreamingEngine.cs:628
+
+struct TopkParams {
+    const float* logits;      // [T x E]
+    const float* bias;        // [E] or null (GLM router_bias)
+    int32_t* topk_idx;        // [T x k]
+    float* topk_w;            // [T x k]
+    int T, E, k;
+    int sigmoid;
+    float routed_scale;
+};
+
+__global__ void topk_kernel(TopkParams p) {
+    __shared__ float sv[4][kMaxE];   // 4 warps per CTA
+    __shared__ float sc[4][kMaxE];
+    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 4 + wib;
+    if (t >= p.T) return;
+    const int E = p.E, k = p.k;
+    const float* lg = p.logits + (size_t)t * E;
+    float* v = sv[wib];     // ranking values
+    float* s = sc[wib];     // weight source values
+    if (!p.sigmoid) {
+        // max from float.MinValue; comparisons skip NaN like the reference loop
+        float mx = -3.40282347e+38f;
+        for (int i = lane; i < E; i += 32) { float a = lg[i]; if (a > mx) mx = a; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) { float b = __shfl_xor_sync(0xffffffffu, mx, o); if (b > mx) mx = b; }
+        for (int i = lane; i < E; i += 32) s[i] = expf_glibc(__fsub_rn(lg[i], mx));
+        __syncwarp();
+        float sum = 0.f;
+        if (lane == 0)
+            for (int i = 0; i < E; i++) sum = __fadd_rn(sum, s[i]);
+        sum = __shfl_sync(0xffffffffu, sum, 0);
+        float inv = __fdiv_rn(1.f, sum);
+        for (int i = lane; i < E; i += 32) { float q = __fmul_rn(s[i], inv); s[i] = q; v[i] = q; }
+    } else {
+        for (int i = lane; i < E; i += 32) {
+            float sg = __fdiv_rn(1.f, __fadd_rn(1.f, expf_glibc(-lg[i])));
+            s[i] = sg;
+            v[i] = p.bias ? __fadd_rn(sg, p.bias[i]) : sg;
+        }
+    }
+    __syncwarp();
+    // k rounds of warp argmax under the reference ordering
+    int sel[kMaxK];
+    for (int r = 0; r < k; r++) {
+        float bv = 0.f;
+        int bi = -1;
+        for (int i = lane; i < E; i += 32) {
+            float a = v[i];
+            bool used = false;
+            for (int q = 0; q < r; q++) used |= (sel[q] == i);
+            if (used) continue;
+            if (bi < 0 || rank_before(a, i, bv, bi)) { bv = a; bi = i; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (bi < 0 || rank_before(ov, oi, bv, bi))) { bv = ov; bi = oi; }
+        }
+        sel[r] = bi;
+    }
+    if (lane == 0) {
+        int32_t* oi = p.topk_idx + (size_t)t * k;
+        float* ow = p.topk_w + (size_t)t * k;
+        if (!p.sigmoid) {
+            float sum = 0.f;
+            for (int r = 0; r < k; r++) sum = __fadd_rn(sum, s[sel[r]]);
+            if (sum <= 0.f) sum = 1.f;
+            for (int r = 0; r < k; r++) { oi[r] = sel[r]; ow[r] = __fdiv_rn(s[sel[r]], sum); }
+        } else {
+            float wsum = 0.f;
+            for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, s[sel[r]]);
+            float inv2 = __fdiv_rn(1.f, __fadd_rn(wsum, 1e-20f));
+            for (int r = 0; r < k; r++) {
+                oi[r] = sel[r];
+                ow[r] = __fmul_rn(__fmul_rn(s[sel[r]], inv2), p.routed_scale);
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Dispatch: stable counting sort of the T*k assignments a = t*k + j by
+// expert (order inside an expert = a ascending), one CTA.  Also builds the
+// work schedule of the expert kernels.
+struct Schedule {
+    int32_t n_active;         // routed experts (of the local window) with assignments
+    int32_t err;              // device error flags (ERR_*)
+    int32_t ctr[4];           // work counters: gate/up, gate/up shared, down, down shared
+    int32_t pad[2];
+};
+
+struct DispatchParams {
+    const int32_t* topk_idx;  // [T*k]
+    int32_t* perm;            // [T*k]
+    int32_t* inv_perm;        // [T*k]
+    int32_t* offsets;         // [E+1]
+    int32_t* active;          // [E+1] slot -> expert (E = shared)
+    Schedule* sched;
+    int T, k, E;
+    int first_expert, n_local;  // local expert window (EP); full range otherwise
+    int has_shared;
+};
+
+constexpr int kDispatchThreads = 1024;
+
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchParams p) {
+    __shared__ int cnt[kMaxE + 1];
+    __shared__ int base[kMaxE + 1];
+    __shared__ int wcnt[kDispatchThreads / 32][64];  // per-warp counts, experts in 64-wide windows
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = p.E, n = p.T * p.k;
+    for (int e = tid; e <= E; e += kDispatchThreads) cnt[e] = 0;
+    __syncthreads();
+    for (int a = tid; a < n; a += kDispatchThreads) {
+        int e = p.topk_idx[a];
+        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+        else atomicOr(&p.sched->err, (int)ERR_BOUNDS);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0, na = 0;
+        for (int e = 0; e < E; e++) {
+            base[e] = run;
+            p.offsets[e] = run;
+            if (cnt[e] > 0 && e >= p.first_expert && e < p.first_expert + p.n_local) p.active[na++] = e;
+            run += cnt[e];
+        }
+        p.offsets[E] = run;
+        if (p.has_shared) p.active[na] = E;
+        p.sched->n_active = na;
+        for (int c = 0; c < 4; c++) p.sched->ctr[c] = 0;
+    }
+    __syncthreads();
+    // stable scatter, 1024 assignments per round
+    for (int r0 = 0; r0 < n; r0 += kDispatchThreads) {
+        int a = r0 + tid;
+        int e = a < n ? p.topk_idx[a] : -1;
+        if (e >= E) e = -1;
+        unsigned peers = __match_any_sync(0xffffffffu, e);
+        int rank_w = __popc(peers & ((1u << lane) - 1));
+        int leader = __ffs(peers) - 1;
+        // prefix over earlier warps of this round: count assignments to e
+        // in warps w' < warp, via a windowed per-warp histogram
+        int before = 0;
+        for (int w0 = 0; w0 < E; w0 += 64) {
+            for (int i = lane; i < 64; i += 32) wcnt[warp][i] = 0;
+            __syncwarp();
+            if (e >= w0 && e < w0 + 64 && lane == leader) wcnt[warp][e - w0] = __popc(peers);
+            __syncthreads();
+            if (e >= w0 && e < w0 + 64)
+                for (int w = 0; w < warp; w++) before += wcnt[w][e - w0];
+            __syncthreads();
+        }
+        if (e >= 0) {
+            int pos = base[e] + before + rank_w;
+            p.perm[pos] = a;
+            p.inv_perm[a] = pos;
+        }
+        __syncthreads();
+        // advance bases by this round's counts
+        if (e >= 0 && lane == leader) atomicAdd(&base[e], __popc(peers));
+        __syncthreads();
+    }
+}
+
+}  // namespace qrm
