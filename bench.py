@@ -61,29 +61,36 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
-        self.index = index
+    def __init__(self, ident):
+        self.ident = ident
         self.path = tempfile.mktemp(prefix="qrm_clocks_", suffix=".csv")
         self.proc = None
+        self.error = None
 
     def start(self):
         try:
             self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+            self.errf = open(self.path + ".err", "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.ident}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.fh, stderr=subprocess.DEVNULL)
-        except Exception:
+                                         stdout=self.fh, stderr=self.errf)
+        except Exception as ex:
             self.proc = None
+            self.error = str(ex)
 
     def stop(self):
         if self.proc is None:
-            return None
+            return {"error": self.error}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
         self.fh.close()
+        self.errf.close()
+        with open(self.path + ".err") as fh:
+            err = fh.read().strip()
+        os.unlink(self.path + ".err")
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as fh:
@@ -101,7 +108,7 @@ class ClockSampler:
                         reasons.add(n)
         os.unlink(self.path)
         if not sm:
-            return None
+            return {"error": err[-300:] or "no samples"}
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -252,19 +259,23 @@ def run_ours(args, rank, world, dist):
         layer.forward_device(xs[i].data_ptr(), T, out.data_ptr(), flags, idx.data_ptr(), wts.data_ptr(), sp)
 
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            flush.fill_(float(i))
-            step(i)
+        for prof in (False, True):   # capture both forward graphs before timing
+            layer.set_profiling(prof)
+            for i in range(args.warmup):
+                flush.fill_(float(i))
+                step(i)
     torch.cuda.synchronize()
     layer.sync()
 
-    # ---- timed region: device-resident inputs
-    layer.set_profiling(True)
+    # ---- timed region: device-resident inputs, K back-to-back steps
     ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    stage_ms = np.zeros(Q.STAGE_COUNT)
-    stage_bytes = np.zeros(Q.STAGE_COUNT)
-    clocks = ClockSampler(dev)
+    try:
+        ident = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        ident = str(dev)
+    clocks = ClockSampler(ident)
+    layer.set_profiling(False)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -275,17 +286,29 @@ def run_ours(args, rank, world, dist):
             ev0[i].record(stream)
             step(args.warmup + i)
             ev1[i].record(stream)
-            ms, by = layer.last_profile()   # waits for this step; outside the events
-            stage_ms += ms
-            stage_bytes += by
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
     clock_info = clocks.stop()
-    layer.set_profiling(False)
     layer.sync()
     step_ms = [ev0[i].elapsed_time(ev1[i]) for i in range(args.steps)]
     total_ms = float(sum(step_ms))
+
+    # ---- per-stage breakdown (library events inside the forward graph), same inputs
+    stage_ms = np.zeros(Q.STAGE_COUNT)
+    stage_bytes = np.zeros(Q.STAGE_COUNT)
+    nprof = min(args.steps, 64)
+    layer.set_profiling(True)
+    with torch.cuda.stream(stream):
+        for i in range(nprof):
+            flush.fill_(float(i))
+            step(args.warmup + i)
+            ms, by = layer.last_profile()
+            stage_ms += ms
+            stage_bytes += by
+    layer.set_profiling(False)
+    torch.cuda.synchronize()
+    layer.sync()
 
     # ---- e2e: host (pinned) buffers through the C ABI, copies inside the timed region
     xh = xs.cpu().pin_memory()
@@ -325,11 +348,11 @@ def run_ours(args, rank, world, dist):
 
     peaks, peak_kind = measured_peaks()
     peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
-    gu_ms, gu_bytes = stage_ms[3], stage_bytes[3]
+    gu_ms, gu_bytes = stage_ms[3], stage_bytes[3]   # over the nprof breakdown steps
     achieved = gu_bytes / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else 0.0
     traffic = traffic_from_profiles()
-    layer_bytes = stage_bytes[3] + stage_bytes[4] + args.steps * (W["n_experts"] * d * 4 + T * d * 4 * 2)
-    layer_gbs = layer_bytes / (total_ms / 1000.0) / 1e9
+    layer_bytes = (stage_bytes[3] + stage_bytes[4]) / nprof + (W["n_experts"] * d * 4 + T * d * 4 * 2)
+    layer_gbs = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
 
     if rank != 0:
         layer.close()
@@ -354,8 +377,8 @@ def run_ours(args, rank, world, dist):
                       peak=peak, unit="GB/s", frac=achieved / peak if peak else None, peak_kind=peak_kind,
                       traffic=traffic),
         layer_hbm=dict(achieved_gbs=layer_gbs, frac_of_8tbs=layer_gbs / NOMINAL_HBM_GBS,
-                       frac_of_measured=layer_gbs / peak, bytes_per_step=layer_bytes / args.steps),
-        stage_ms_per_step={n: float(stage_ms[i] / args.steps) for i, n in enumerate(Q.STAGES)},
+                       frac_of_measured=layer_gbs / peak, bytes_per_step=layer_bytes),
+        stage_ms_per_step={n: float(stage_ms[i] / nprof) for i, n in enumerate(Q.STAGES)},
         cpu_baseline=cpu,
         e2e=dict(value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * d * 4, d2h_bytes_per_step=T * d * 4),
         gpu_launches=launches_per_step * args.steps,
@@ -369,14 +392,18 @@ def run_ours(args, rank, world, dist):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=None, help="profiling runs only: fewer experts")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.experts:
+        WORKLOAD["n_experts"] = args.experts
+        WORKLOAD["name"] += f"_e{args.experts}"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     dist = None

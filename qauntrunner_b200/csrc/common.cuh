@@ -49,9 +49,6 @@ struct MatDev {
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
-// Bounded spin wait limit (device waits never spin forever).
-constexpr long long kSpinLimit = 1ll << 26;
-
 // Device-side error flag bits, read back by qrm_sync().
 enum : uint32_t { ERR_TIMEOUT = 1u, ERR_BOUNDS = 2u, ERR_INTERNAL = 4u };
 

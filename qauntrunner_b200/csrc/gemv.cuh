@@ -16,10 +16,10 @@
 // and the CTA reduces the row sums with a transposing warp reduction plus one
 // shared-memory pass -- a fixed order, so results are deterministic.
 //
-// Integer codes become floats without a conversion instruction: a code byte
-// placed in bits 16..23 of 0x40000000 reads as 2 + q/64 (2 + q/4 for a high
-// nibble already shifted by 4), so sum(q*x) = 64*(sum(F*x) - 2*sum(x)).  The
-// cancellation costs at most ~4 bits of the 24-bit significand.
+// Integer codes become floats without a conversion instruction: a code byte b
+// placed in the mantissa of 2.0f (bits 16..22 for b < 128, 15..22 otherwise)
+// reads as F = 2 + b/64 (or 2 + b/128), so sum(b*x) = 64*(sum(F*x) - 2*sum(x))
+// (or 128*(...)).  The cancellation costs at most ~5 of the 24 significand bits.
 #pragma once
 #include "common.cuh"
 #include "glibc_expf.cuh"
@@ -40,21 +40,23 @@ __device__ __forceinline__ uint2 ld_stream8(const void* p) {
 }
 __device__ __forceinline__ uint16_t ld_u16(const void* p) { return __ldg((const unsigned short*)p); }
 
-// byte K of w placed as 0x40kk0000 -> 2 + w_K/64 (written as shift and mask;
-// the __byte_perm intrinsic made ptxas spill these kernels heavily)
-template <int K>
+// Byte K of w placed at bit POS of 0x40000000 reads as F = 2 + b * 2^(POS-22):
+// POS 16 gives 2 + b/64 for b < 128 (bit 23 is the exponent's low bit, so
+// larger bytes must use POS 15: 2 + b/128).  Written as shift and mask; the
+// __byte_perm intrinsic made ptxas spill these kernels heavily.
+template <int K, int POS>
 __device__ __forceinline__ float bfk(uint32_t w) {
-    uint32_t v = K < 2 ? (w << (16 - 8 * K)) : (w >> (8 * K - 16));
-    return __uint_as_float((v & 0x00FF0000u) | 0x40000000u);
+    uint32_t v = (8 * K <= POS) ? (w << (POS - 8 * K)) : (w >> (8 * K - POS));
+    return __uint_as_float((v & (0xFFu << POS)) | 0x40000000u);
 }
 
 // sum_{k<4} F(byte k of w) * x[o+k]  (x passed by value so it stays in registers)
-#define QRM_DOT4(w, X, o, acc)                              \
-    do {                                                    \
-        (acc) = fmaf(bfk<0>(w), (X)[(o) + 0], (acc));      \
-        (acc) = fmaf(bfk<1>(w), (X)[(o) + 1], (acc));      \
-        (acc) = fmaf(bfk<2>(w), (X)[(o) + 2], (acc));      \
-        (acc) = fmaf(bfk<3>(w), (X)[(o) + 3], (acc));      \
+#define QRM_DOT4(w, X, o, acc, POS)                               \
+    do {                                                          \
+        (acc) = fmaf(bfk<0, POS>(w), (X)[(o) + 0], (acc));        \
+        (acc) = fmaf(bfk<1, POS>(w), (X)[(o) + 1], (acc));        \
+        (acc) = fmaf(bfk<2, POS>(w), (X)[(o) + 2], (acc));        \
+        (acc) = fmaf(bfk<3, POS>(w), (X)[(o) + 3], (acc));        \
     } while (0)
 
 // ---------------------------------------------------------------- units
@@ -130,12 +132,12 @@ template <> struct WUnit<Q4_K> {
         const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
         for (int w = 0; w < 4; w++) {
-            QRM_DOT4(q[w] & 0x0F0F0F0Fu, xu.x, 4 * w, al);
-            QRM_DOT4(q[w] & 0xF0F0F0F0u, xu.x, 16 + 4 * w, ah);
+            QRM_DOT4(q[w] & 0x0F0F0F0Fu, xu.x, 4 * w, al, 16);
+            QRM_DOT4(q[w] & 0xF0F0F0F0u, xu.x, 16 + 4 * w, ah, 15);
         }
         float sxl = xu.s[0] + xu.s[1], sxh = xu.s[2] + xu.s[3];
         float qxl = 64.f * (al - 2.f * sxl);
-        float qxh = 4.f * (ah - 2.f * sxh);
+        float qxh = 8.f * (ah - 2.f * sxh);
         return d * ((float)scA * qxl + (float)scB * qxh) - dmin * ((float)mA * sxl + (float)mB * sxh);
     }
 };
@@ -155,11 +157,11 @@ template <> struct WUnit<Q4_0> {
         const uint32_t q[4] = {qs.x, qs.y, qs.z, qs.w};
 #pragma unroll
         for (int w = 0; w < 4; w++) {
-            QRM_DOT4(q[w] & 0x0F0F0F0Fu, xu.x, 4 * w, al);
-            QRM_DOT4(q[w] & 0xF0F0F0F0u, xu.x, 16 + 4 * w, ah);
+            QRM_DOT4(q[w] & 0x0F0F0F0Fu, xu.x, 4 * w, al, 16);
+            QRM_DOT4(q[w] & 0xF0F0F0F0u, xu.x, 16 + 4 * w, ah, 15);
         }
         float sxl = xu.s[0] + xu.s[1], sxh = xu.s[2] + xu.s[3];
-        float qx = 64.f * (al - 2.f * sxl) + 4.f * (ah - 2.f * sxh);
+        float qx = 64.f * (al - 2.f * sxl) + 8.f * (ah - 2.f * sxh);
         return h2f(dh) * (qx - 8.f * (sxl + sxh));
     }
 };
@@ -175,13 +177,14 @@ template <> struct WUnit<Q8_0> {
         dh = ld_u16(m.base + m.nb * 32 + blk * 2);
     }
     __device__ __forceinline__ float dot(const XUnit& xu) const {
-        // (q + 128) as an unsigned byte: F = 2 + (q+128)/64 -> sum q x = 64*(sum F x - 4 sum x)
+        // b = q + 128 as an unsigned byte at POS 15: F = 2 + b/128 = 3 + q/128
+        // -> sum q x = 128*(sum F x - 3 sum x)
         const uint32_t q[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         float a = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; w++) QRM_DOT4(q[w] ^ 0x80808080u, xu.x, 4 * w, a);
+        for (int w = 0; w < 8; w++) QRM_DOT4(q[w] ^ 0x80808080u, xu.x, 4 * w, a, 15);
         float sx = (xu.s[0] + xu.s[1]) + (xu.s[2] + xu.s[3]);
-        return h2f(dh) * (64.f * (a - 4.f * sx));
+        return h2f(dh) * (128.f * (a - 3.f * sx));
     }
 };
 
@@ -212,10 +215,10 @@ template <> struct WUnit<Q6_K> {
             uint32_t q2 = (B[w] & 0x0F0F0F0Fu) | (((H[w] >> 2) & 0x03030303u) << 4);
             uint32_t q3 = ((A[w] >> 4) & 0x0F0F0F0Fu) | (((H[w] >> 4) & 0x03030303u) << 4);
             uint32_t q4 = ((B[w] >> 4) & 0x0F0F0F0Fu) | (((H[w] >> 6) & 0x03030303u) << 4);
-            QRM_DOT4(q1, xu.x, 0 + 4 * w, acc[0]);
-            QRM_DOT4(q2, xu.x, 8 + 4 * w, acc[1]);
-            QRM_DOT4(q3, xu.x, 16 + 4 * w, acc[2]);
-            QRM_DOT4(q4, xu.x, 24 + 4 * w, acc[3]);
+            QRM_DOT4(q1, xu.x, 0 + 4 * w, acc[0], 16);
+            QRM_DOT4(q2, xu.x, 8 + 4 * w, acc[1], 16);
+            QRM_DOT4(q3, xu.x, 16 + 4 * w, acc[2], 16);
+            QRM_DOT4(q4, xu.x, 24 + 4 * w, acc[3], 16);
         }
         // sc bytes: [0..8) = sc[8h .. 8h+8); group g uses byte is + 2g (int8)
         float r = 0.f;
@@ -358,7 +361,7 @@ expert_gemv_kernel(GemvParams p) {
     const int slot_base = p.mode == 2 ? n_active : 0;
     int it = 0;
     for (;;) {
-        if (tid == 0) s_item[it & 1] = atomicAdd(p.ctr, 1);
+        if (tid == 0) s_item[it & 1] = blockIdx.x + it * gridDim.x;   // static striding
         __syncthreads();
         const int item = s_item[it & 1];
         it++;

@@ -23,6 +23,7 @@
 #include "combine.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "gemv_tma.cuh"
 #include "layout.cuh"
 #include "route.cuh"
 
@@ -83,20 +84,92 @@ int gemv_occupancy(int nt, int block) {
 constexpr int kRGateUp = 4;   // rows per gate/up item (x2 matrices)
 constexpr int kRDown = 8;     // rows per down item
 
-// gate/up (M=2) or down (M=1) for one format
-int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_count, cudaStream_t s) {
+// Bulk-copy staged kernel: G consumer groups, NT tokens per pass.
+template <int FMT, int M, int R, int NT, int G>
+int launch_tma_g(const qrm::GemvParams& p, const qrm::TmaConfig& cfg, int cwg, int sm_count, int32_t* err,
+                 cudaStream_t s) {
+    auto fn = qrm::expert_gemv_tma_kernel<FMT, M, R, NT, G>;
+    const size_t smem = qrm::tma_smem_bytes(cfg);
+    static bool attr_set = false;  // one per instantiation
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+            return fail(QRM_E_CUDA, "expert kernel attribute");
+        attr_set = true;
+    }
+    fn<<<sm_count, (G * cwg + 1) * 32, smem, s>>>(p, cfg, err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
+}
+
+// Pick the tile height R, consumer groups G and tokens per pass NT:
+// gate/up R = 8 (16 matrix rows per item); down R = 32 when the row is short
+// enough for 4+ consumer groups, else 8.  NT keeps pairs*NT <= 32.
+template <int FMT, int M, int R>
+int launch_tma_r(int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s, bool* used) {
+    qrm::TmaConfig cfg;
+    *used = false;
+    if (p.rows % R) return QRM_OK;
+    qrm::GemvParams q = p;
+    q.tiles = p.rows / R;
+    if (!qrm::tma_plan<FMT>(M, R, p.cols, 227 * 1024, &cfg)) return QRM_OK;
+    const int cwg = (p.cols / 32 + 31) / 32;
+    int G = 16;
+    while (G > 1 && (G * cwg > 16 || (M * R) % G)) G >>= 1;
+    constexpr int kPairsMax = M * R;
+    const int pairs = kPairsMax / G;
+    if (M == 1 && R == 32 && G < 4) return QRM_OK;   // caller falls back to R = 8
+    *used = true;
+    const bool one = nt <= 1 || pairs > 8;
+#define QRM_TMA_G(GG)                                                                             \
+    case GG:                                                                                      \
+        if constexpr ((M * R) % GG == 0 && (M * R) / GG <= 32) {                                  \
+            if (one || (M * R) / GG > 8) return launch_tma_g<FMT, M, R, 1, GG>(q, cfg, cwg, sm_count, err, s); \
+            if constexpr ((M * R) / GG <= 8) return launch_tma_g<FMT, M, R, 4, GG>(q, cfg, cwg, sm_count, err, s); \
+        }                                                                                         \
+        break;
+    switch (G) {
+        QRM_TMA_G(16)
+        QRM_TMA_G(8)
+        QRM_TMA_G(4)
+        QRM_TMA_G(2)
+        QRM_TMA_G(1)
+        default: break;
+    }
+#undef QRM_TMA_G
+    *used = false;
+    return QRM_OK;
+}
+
+template <int FMT, int M>
+int launch_tma(int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s, bool* used) {
+    if (M == 1) {
+        int rc = launch_tma_r<FMT, 1, 32>(nt, p, sm_count, err, s, used);
+        if (rc || *used) return rc;
+    }
+    return launch_tma_r<FMT, M, 8>(nt, p, sm_count, err, s, used);
+}
+
+// gate/up (M=2) or down (M=1) for one format: the bulk-copy staged kernel
+// when the tile fields are 16-byte multiples, else the register kernel.
+int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s) {
     const int U = p.cols / 32;
     const int block = (U + 31) / 32 * 32;
     int occ = 1;
-    cudaError_t err = cudaSuccess;
+    cudaError_t e = cudaSuccess;
+    bool used = false;
+    int rc = QRM_OK;
 #define QRM_GEMV_CASE(F)                                                                        \
     case F:                                                                                     \
         if (gateup) {                                                                           \
+            rc = launch_tma<F, 2>(nt, p, sm_count, err, s, &used);                    \
+            if (rc || used) return rc;                                                          \
             occ = gemv_occupancy<F, 2, kRGateUp>(nt, block);                                    \
-            err = launch_gemv_nt<F, 2, kRGateUp>(nt, p, sm_count * occ, block, s);              \
+            e = launch_gemv_nt<F, 2, kRGateUp>(nt, p, sm_count * occ, block, s);                \
         } else {                                                                                \
+            rc = launch_tma<F, 1>(nt, p, sm_count, err, s, &used);                      \
+            if (rc || used) return rc;                                                          \
             occ = gemv_occupancy<F, 1, kRDown>(nt, block);                                      \
-            err = launch_gemv_nt<F, 1, kRDown>(nt, p, sm_count * occ, block, s);                \
+            e = launch_gemv_nt<F, 1, kRDown>(nt, p, sm_count * occ, block, s);                  \
         }                                                                                       \
         break;
     switch (fmt) {
@@ -108,7 +181,7 @@ int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_c
         default: return fail(QRM_E_FORMAT, "format %d has no expert kernel", fmt);
     }
 #undef QRM_GEMV_CASE
-    if (err != cudaSuccess) return fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(err));
+    if (e != cudaSuccess) return fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
     return QRM_OK;
 }
 
@@ -288,8 +361,9 @@ extern "C" int qrm_create(const qrm_layer_desc* desc, qrm_layer** out) {
     rc = alloc_work(L, desc->max_tokens);
     if (rc) return bail(rc);
     // kernels with large dynamic shared memory
-    if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
-        return bail(fail(QRM_E_CUDA, "route kernel attribute"));
+    if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(qrm::dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+        return bail(fail(QRM_E_CUDA, "kernel attribute"));
     *out = L;
     return QRM_OK;
 }
@@ -437,7 +511,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const int d = D.d_model, E = D.n_experts, f = D.expert_ffn, k = L->k;
     const bool shared = L->shared_enabled && L->uploaded[(size_t)E * 3];
     const bool prof = L->profiling;
-    auto mark = [&](int i) { if (prof) cudaEventRecord(L->ev[i], s); };
+    auto mark = [&](int i) { if (prof) cudaEventRecordWithFlags(L->ev[i], s, cudaEventRecordExternal); };
     mark(0);
     // 1. RMSNorm + router logits
     const float* xn = L->xn;
@@ -458,16 +532,18 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     QRM_CUDA(cudaGetLastError());
     mark(1);
     L->last_xn = xn;
-    // 2. top-k
+    // 2. top-k and 3. dispatch (fused into one single-CTA kernel for small T)
     qrm::TopkParams tp{L->logits, L->has_bias ? L->router_bias : nullptr, topk_idx, topk_w, T, E, k,
                        D.moe_sigmoid ? 1 : 0, D.routed_scale};
-    qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
-    QRM_CUDA(cudaGetLastError());
+    const bool fused = T <= qrm::kFusedTopkMaxT;
+    if (!fused) {
+        qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
+        QRM_CUDA(cudaGetLastError());
+    }
     mark(2);
-    // 3. dispatch
     qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->offsets, L->active, L->sched, T, k, E,
                            L->first_expert, L->n_local, shared ? 1 : 0};
-    qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, 0, s>>>(dp);
+    qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, T, fused), s>>>(dp, tp, fused ? 1 : 0);
     QRM_CUDA(cudaGetLastError());
     mark(3);
     // 4. gate/up (+ SwiGLU) and 5. down
@@ -500,16 +576,16 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         if (same_fmt) {
             gp.mode = 0;
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
-            int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, s);
+            int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, &L->sched->err, s);
             if (rc) return rc;
         } else {
             gp.mode = 1;
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
-            int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, s);
+            int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, &L->sched->err, s);
             if (rc) return rc;
             gp.mode = 2;
             gp.ctr = &L->sched->ctr[gu ? 1 : 3];
-            rc = launch_gemv(fs, gu, nt, gp, L->sm_count, s);
+            rc = launch_gemv(fs, gu, nt, gp, L->sm_count, &L->sched->err, s);
             if (rc) return rc;
         }
         mark(gu ? 4 : 5);
@@ -755,7 +831,7 @@ extern "C" int qrm_matrix_gemv(qrm_matrix* M, const float* x_dev, int T, float* 
     gp.routed_by_token = 0;
     gp.mode = 2;
     gp.has_shared = 1;
-    return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, s);
+    return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, M->misc + 5, s);
 }
 
 // ---------------------------------------------------------------- synthetic data

@@ -27,6 +27,23 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+// acc + sum over i = lane, lane+8, ... < n8 of a[i]*b[i], in that order (one
+// Vector256 lane of SimdMath.DotF32 / RmsNorm).  Sixteen products are loaded
+// ahead so the dependent adds run back to back.
+__device__ __forceinline__ float lane_chain(const float* __restrict__ a, const float* __restrict__ b, int lane,
+                                            int n8, float acc) {
+    int i = 0;
+    for (; i + 128 <= n8; i += 128) {
+        float p[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) p[u] = __fmul_rn(a[i + 8 * u + lane], b[i + 8 * u + lane]);
+#pragma unroll
+        for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, p[u]);
+    }
+    for (; i < n8; i += 8) acc = __fadd_rn(acc, __fmul_rn(a[i + lane], b[i + lane]));
+    return acc;
+}
+
 // Sequential HSum of eight lane accumulators (SimdMath.HSum).
 __device__ __forceinline__ float hsum8_seq(const float* a) {
     float s = 0.f;
@@ -111,12 +128,9 @@ route_small_kernel(RouteParams p) {
     cp_async_wait_chunk<C>();                                                     \
     __syncthreads();                                                              \
     if (norm_thread) {                                                            \
-        const float* xr = X + nt * d;                                             \
-        int stop = min(d8, 8 * ((C) + 1) * chg);                                  \
-        for (int i = 8 * (C) * chg; i < stop; i += 8) {                           \
-            float v = xr[i + nj];                                                 \
-            acc = __fadd_rn(acc, __fmul_rn(v, v));                                \
-        }                                                                         \
+        const float* xr = X + nt * d + 8 * (C) * chg;                             \
+        int stop = min(d8, 8 * ((C) + 1) * chg) - 8 * (C) * chg;                  \
+        if (stop > 0) acc = lane_chain(xr, xr, nj, stop, acc);                    \
     }
     QRM_ROUTE_CHUNK(0)
     QRM_ROUTE_CHUNK(1)
@@ -136,11 +150,14 @@ route_small_kernel(RouteParams p) {
             scl[tid] = __fdiv_rn(1.f, __fsqrt_rn(v));
         }
         __syncthreads();
-        for (int i = tid; i < T * d; i += kRouteThreads) {
-            int t = i / d, c = i - t * d;
-            float v = __fmul_rn(X[i], scl[t]);
-            if (p.norm_w) v = __fmul_rn(v, p.norm_w[c]);
-            X[i] = v;
+        for (int t = 0; t < T; t++) {
+            const float sc = scl[t];
+            float* xr = X + t * d;
+            for (int c = tid; c < d; c += kRouteThreads) {
+                float v = __fmul_rn(xr[c], sc);
+                if (p.norm_w) v = __fmul_rn(v, p.norm_w[c]);
+                xr[c] = v;
+            }
         }
         __syncthreads();
     }
@@ -153,9 +170,7 @@ route_small_kernel(RouteParams p) {
     if (lthread) {
         const float* wr = W + le * d;
         const float* xr = X + lt * d;
-        float la = 0.f;
-        for (int i = 0; i < d8; i += 8) la = __fadd_rn(la, __fmul_rn(wr[i + lj], xr[i + lj]));
-        red[(lt * kRouteEPC + le) * 8 + lj] = la;
+        red[(lt * kRouteEPC + le) * 8 + lj] = lane_chain(wr, xr, lj, d8, 0.f);
     }
     __syncthreads();
     if (tid < T * ne) {
@@ -181,8 +196,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     const float* xr = x + (size_t)warp * d;
     const int d8 = d / 8 * 8;
     float acc = 0.f;
-    if (lane < 8 && d >= 8)
-        for (int i = lane; i < d8; i += 8) acc = __fadd_rn(acc, __fmul_rn(xr[i], xr[i]));
+    if (lane < 8 && d >= 8) acc = lane_chain(xr, xr, lane, d8, 0.f);
     float a[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) a[j] = __shfl_sync(0xffffffffu, acc, j);
@@ -314,16 +328,11 @@ struct TopkParams {
     float routed_scale;
 };
 
-__global__ void topk_kernel(TopkParams p) {
-    __shared__ float sv[4][kMaxE];   // 4 warps per CTA
-    __shared__ float sc[4][kMaxE];
-    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * 4 + wib;
-    if (t >= p.T) return;
+// One warp ranks the E scores of token t.  v (ranking values) and s (weight
+// sources) are this warp's shared scratch of kMaxE floats each.
+__device__ __forceinline__ void topk_token(const TopkParams& p, int t, int lane, float* v, float* s) {
     const int E = p.E, k = p.k;
     const float* lg = p.logits + (size_t)t * E;
-    float* v = sv[wib];     // ranking values
-    float* s = sc[wib];     // weight source values
     if (!p.sigmoid) {
         // max from float.MinValue; comparisons skip NaN like the reference loop
         float mx = -3.40282347e+38f;
@@ -333,8 +342,17 @@ __global__ void topk_kernel(TopkParams p) {
         for (int i = lane; i < E; i += 32) s[i] = expf_glibc(__fsub_rn(lg[i], mx));
         __syncwarp();
         float sum = 0.f;
-        if (lane == 0)
-            for (int i = 0; i < E; i++) sum = __fadd_rn(sum, s[i]);
+        if (lane == 0) {
+            int i = 0;
+            for (; i + 16 <= E; i += 16) {
+                float q[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++) q[u] = s[i + u];
+#pragma unroll
+                for (int u = 0; u < 16; u++) sum = __fadd_rn(sum, q[u]);
+            }
+            for (; i < E; i++) sum = __fadd_rn(sum, s[i]);
+        }
         sum = __shfl_sync(0xffffffffu, sum, 0);
         float inv = __fdiv_rn(1.f, sum);
         for (int i = lane; i < E; i += 32) { float q = __fmul_rn(s[i], inv); s[i] = q; v[i] = q; }
@@ -346,44 +364,58 @@ __global__ void topk_kernel(TopkParams p) {
         }
     }
     __syncwarp();
-    // k rounds of warp argmax under the reference ordering
+    // k rounds of warp argmax under the reference ordering; lane owns i = lane + 32j
+    uint32_t taken = 0;
     int sel[kMaxK];
-    for (int r = 0; r < k; r++) {
-        float bv = 0.f;
-        int bi = -1;
-        for (int i = lane; i < E; i += 32) {
-            float a = v[i];
-            bool used = false;
-            for (int q = 0; q < r; q++) used |= (sel[q] == i);
-            if (used) continue;
-            if (bi < 0 || rank_before(a, i, bv, bi)) { bv = a; bi = i; }
-        }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi >= 0 && (bi < 0 || rank_before(ov, oi, bv, bi))) { bv = ov; bi = oi; }
+    for (int r = 0; r < kMaxK; r++) {
+        if (r < k) {
+            float bv = 0.f;
+            int bi = -1;
+            for (int j = 0, i = lane; i < E; j++, i += 32) {
+                if (taken & (1u << j)) continue;
+                float a = v[i];
+                if (bi < 0 || rank_before(a, i, bv, bi)) { bv = a; bi = i; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi >= 0 && (bi < 0 || rank_before(ov, oi, bv, bi))) { bv = ov; bi = oi; }
+            }
+            sel[r] = bi;
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         }
-        sel[r] = bi;
     }
     if (lane == 0) {
         int32_t* oi = p.topk_idx + (size_t)t * k;
         float* ow = p.topk_w + (size_t)t * k;
         if (!p.sigmoid) {
             float sum = 0.f;
-            for (int r = 0; r < k; r++) sum = __fadd_rn(sum, s[sel[r]]);
+#pragma unroll
+            for (int r = 0; r < kMaxK; r++) if (r < k) sum = __fadd_rn(sum, s[sel[r]]);
             if (sum <= 0.f) sum = 1.f;
-            for (int r = 0; r < k; r++) { oi[r] = sel[r]; ow[r] = __fdiv_rn(s[sel[r]], sum); }
+#pragma unroll
+            for (int r = 0; r < kMaxK; r++) if (r < k) { oi[r] = sel[r]; ow[r] = __fdiv_rn(s[sel[r]], sum); }
         } else {
             float wsum = 0.f;
-            for (int r = 0; r < k; r++) wsum = __fadd_rn(wsum, s[sel[r]]);
+#pragma unroll
+            for (int r = 0; r < kMaxK; r++) if (r < k) wsum = __fadd_rn(wsum, s[sel[r]]);
             float inv2 = __fdiv_rn(1.f, __fadd_rn(wsum, 1e-20f));
-            for (int r = 0; r < k; r++) {
-                oi[r] = sel[r];
-                ow[r] = __fmul_rn(__fmul_rn(s[sel[r]], inv2), p.routed_scale);
-            }
+#pragma unroll
+            for (int r = 0; r < kMaxK; r++)
+                if (r < k) { oi[r] = sel[r]; ow[r] = __fmul_rn(__fmul_rn(s[sel[r]], inv2), p.routed_scale); }
         }
     }
+}
+
+__global__ void topk_kernel(TopkParams p) {
+    __shared__ float sv[4][kMaxE];   // 4 warps per CTA
+    __shared__ float sc[4][kMaxE];
+    const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 4 + wib;
+    if (t >= p.T) return;
+    topk_token(p, t, lane, sv[wib], sc[wib]);
 }
 
 // ---------------------------------------------------------------------------
@@ -410,13 +442,29 @@ struct DispatchParams {
 };
 
 constexpr int kDispatchThreads = 1024;
+constexpr int kFusedTopkMaxT = 32;   // fused top-k + dispatch: one warp per token
 
-__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchParams p) {
-    __shared__ int cnt[kMaxE + 1];
-    __shared__ int base[kMaxE + 1];
-    __shared__ int wcnt[kDispatchThreads / 32][64];  // per-warp counts, experts in 64-wide windows
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+inline size_t dispatch_smem(int E, int T, bool fused) {
+    size_t b = sizeof(int) * ((size_t)2 * (E + 1) + (size_t)32 * E + 64);
+    if (fused) b += sizeof(float) * (size_t)2 * min(T, kFusedTopkMaxT) * E;
+    return b;
+}
+
+// Dispatch, one CTA of 1024 threads.  With `fused` (T <= 32) the CTA first
+// runs the top-k of every token (one warp each).
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchParams p, TopkParams tp, int fused) {
+    extern __shared__ __align__(16) int dsm[];
     const int E = p.E, n = p.T * p.k;
+    int* cnt = dsm;                  // [E+1]
+    int* base = cnt + (E + 1);       // [E+1]
+    int* wc = base + (E + 1);        // [32][E]
+    int* wsum = wc + 32 * E;         // [64] scan scratch
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (fused) {
+        float* tsc = reinterpret_cast<float*>(wsum + 64);
+        if (warp < p.T) topk_token(tp, warp, lane, tsc + (size_t)warp * 2 * E, tsc + (size_t)warp * 2 * E + E);
+        __syncthreads();
+    }
     for (int e = tid; e <= E; e += kDispatchThreads) cnt[e] = 0;
     __syncthreads();
     for (int a = tid; a < n; a += kDispatchThreads) {
@@ -425,47 +473,72 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
         else atomicOr(&p.sched->err, (int)ERR_BOUNDS);
     }
     __syncthreads();
-    if (tid == 0) {
-        int run = 0, na = 0;
-        for (int e = 0; e < E; e++) {
-            base[e] = run;
-            p.offsets[e] = run;
-            if (cnt[e] > 0 && e >= p.first_expert && e < p.first_expert + p.n_local) p.active[na++] = e;
-            run += cnt[e];
+    // exclusive scans of the counts and of the "active local expert" flags:
+    // warp w < 16 scans experts [32w, 32w+32)
+    int c = 0, flag = 0, incl_c = 0, incl_f = 0;
+    const int e_me = tid;
+    if (warp < 16) {
+        if (e_me < E) {
+            c = cnt[e_me];
+            flag = (c > 0 && e_me >= p.first_expert && e_me < p.first_expert + p.n_local) ? 1 : 0;
         }
-        p.offsets[E] = run;
+        incl_c = c;
+        incl_f = flag;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int a = __shfl_up_sync(0xffffffffu, incl_c, o), b = __shfl_up_sync(0xffffffffu, incl_f, o);
+            if (lane >= o) { incl_c += a; incl_f += b; }
+        }
+        if (lane == 31) { wsum[warp] = incl_c; wsum[32 + warp] = incl_f; }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int a = lane < 16 ? wsum[lane] : 0, b = lane < 16 ? wsum[32 + lane] : 0;
+        int ia = a, ib = b;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int x = __shfl_up_sync(0xffffffffu, ia, o), y = __shfl_up_sync(0xffffffffu, ib, o);
+            if (lane >= o) { ia += x; ib += y; }
+        }
+        if (lane < 16) { wsum[lane] = ia - a; wsum[32 + lane] = ib - b; }
+        if (lane == 15) { wsum[48] = ia; wsum[49] = ib; }
+    }
+    __syncthreads();
+    if (warp < 16 && e_me < E) {
+        int ex = wsum[warp] + incl_c - c;
+        base[e_me] = ex;
+        p.offsets[e_me] = ex;
+        if (flag) p.active[wsum[32 + warp] + incl_f - 1] = e_me;
+    }
+    if (tid == 0) {
+        int total = wsum[48], na = wsum[49];
+        p.offsets[E] = total;
         if (p.has_shared) p.active[na] = E;
         p.sched->n_active = na;
-        for (int c = 0; c < 4; c++) p.sched->ctr[c] = 0;
+        for (int q = 0; q < 4; q++) p.sched->ctr[q] = 0;
     }
     __syncthreads();
     // stable scatter, 1024 assignments per round
     for (int r0 = 0; r0 < n; r0 += kDispatchThreads) {
-        int a = r0 + tid;
+        const int a = r0 + tid;
         int e = a < n ? p.topk_idx[a] : -1;
-        if (e >= E) e = -1;
-        unsigned peers = __match_any_sync(0xffffffffu, e);
-        int rank_w = __popc(peers & ((1u << lane) - 1));
-        int leader = __ffs(peers) - 1;
-        // prefix over earlier warps of this round: count assignments to e
-        // in warps w' < warp, via a windowed per-warp histogram
-        int before = 0;
-        for (int w0 = 0; w0 < E; w0 += 64) {
-            for (int i = lane; i < 64; i += 32) wcnt[warp][i] = 0;
-            __syncwarp();
-            if (e >= w0 && e < w0 + 64 && lane == leader) wcnt[warp][e - w0] = __popc(peers);
-            __syncthreads();
-            if (e >= w0 && e < w0 + 64)
-                for (int w = 0; w < warp; w++) before += wcnt[w][e - w0];
-            __syncthreads();
-        }
+        if (e >= E || e < 0) e = -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank_w = __popc(peers & ((1u << lane) - 1));
+        const int leader = __ffs(peers) - 1;
+        int* row = wc + warp * E;
+        for (int i = lane; i < E; i += 32) row[i] = 0;
+        __syncwarp();
+        if (e >= 0 && lane == leader) row[e] = __popc(peers);
+        __syncthreads();
         if (e >= 0) {
-            int pos = base[e] + before + rank_w;
+            int before = 0;
+            for (int w = 0; w < warp; w++) before += wc[w * E + e];
+            const int pos = base[e] + before + rank_w;
             p.perm[pos] = a;
             p.inv_perm[a] = pos;
         }
         __syncthreads();
-        // advance bases by this round's counts
         if (e >= 0 && lane == leader) atomicAdd(&base[e], __popc(peers));
         __syncthreads();
     }
