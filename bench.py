@@ -221,7 +221,7 @@ def build_layer(torch, Q, dev, T, seed=SEED):
 
 def traffic_from_profiles():
     """dram bytes per gate/up launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "gateup_gemv_c5_decode.txt")
+    p = os.path.join(ROOT, "profiles", "expert_gemv_c5_decode.md")
     try:
         with open(p) as fh:
             for line in fh:
