@@ -327,6 +327,12 @@ struct GemvParams {
     int routed_by_token;       // gate/up: routed inputs are token rows (perm/k)
     int mode;                  // 0: routed + shared slots, 1: routed only, 2: shared only
     int has_shared;
+    // quantised activation tables (integer tensor-core kernel): routed rows are
+    // token rows (gate/up, row = perm/k) or assignment rows (down, row = off+i);
+    // shared rows follow at xtab_shared_base
+    const uint8_t* xtab;
+    int xtab_stride;
+    int xtab_shared_base;
 };
 
 __device__ __forceinline__ float swiglu(float g, float u, float limit) {

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
+#include "gemv_imma.cuh"
 #include "layout.cuh"
 #include "route.cuh"
 
@@ -149,7 +150,69 @@ int launch_tma(int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cud
     return launch_tma_r<FMT, M, 8>(nt, p, sm_count, err, s, used);
 }
 
-// gate/up (M=2) or down (M=1) for one format: the bulk-copy staged kernel
+// Integer tensor-core kernel (Q4_K, Q8_0, Q4_0 with 256-multiple rows);
+// needs the activation tables of p.xtab (written by xquant_kernel).
+template <int FMT, int M, int NTK, int RTILES>
+int launch_imma_t(const qrm::GemvParams& p, const qrm::ImmaConfig& cfg, int sm_count, int32_t* err, cudaStream_t s) {
+    // consumer warps: RTILES x (K slices); the slice count divides the
+    // super-blocks evenly where a divisor close to the 16-warp limit exists
+    const int nsb = p.cols / 256, lim = std::min(nsb, 16 / RTILES);
+    int nks = 1;
+    for (int d = lim; d >= 1; d--)
+        if (nsb % d == 0) { nks = d; break; }
+    if (2 * nks <= lim) nks = lim;
+    const int CW = nks * RTILES;
+    auto fn = qrm::expert_gemv_imma_kernel<FMT, M, NTK, RTILES>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+            return fail(QRM_E_CUDA, "expert kernel attribute");
+        attr_set = true;
+    }
+    fn<<<sm_count, (CW + 1) * 32, qrm::imma_smem_bytes(cfg), s>>>(p, cfg, err);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
+}
+
+bool imma_format(int fmt) { return fmt == qrm::Q4_K || fmt == qrm::Q8_0 || fmt == qrm::Q4_0; }
+
+// true when the integer kernel will take this matrix shape
+bool imma_usable(int fmt, int rows, int cols, bool gateup) {
+    if (!imma_format(fmt) || cols % 256) return false;
+    const int rt = gateup ? 8 : 16;
+    return rows % (2 * rt) == 0;
+}
+
+template <int FMT, int M>
+int launch_imma(int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s, bool* used) {
+    *used = false;
+    if (!p.xtab) return QRM_OK;
+    constexpr int RT = qrm::kImmaRows / M;
+    const int nsb = p.cols / 256;
+    const int rtiles = nsb >= 16 ? 1 : 2;
+    if (p.rows % (RT * rtiles)) return QRM_OK;
+    const int ntk = T <= 1 ? 1 : 2;
+    qrm::ImmaConfig cfg;
+    if (!qrm::imma_plan<FMT>(p.cols, qrm::kImmaRows * rtiles, ntk, 227 * 1024, &cfg)) return QRM_OK;
+    qrm::GemvParams q = p;
+    q.tiles = p.rows / (RT * rtiles);
+    *used = true;
+    if (rtiles == 1)
+        return ntk == 1 ? launch_imma_t<FMT, M, 1, 1>(q, cfg, sm_count, err, s) : launch_imma_t<FMT, M, 2, 1>(q, cfg, sm_count, err, s);
+    return ntk == 1 ? launch_imma_t<FMT, M, 1, 2>(q, cfg, sm_count, err, s) : launch_imma_t<FMT, M, 2, 2>(q, cfg, sm_count, err, s);
+}
+
+int launch_xquant(const float* src, int K, int rows, uint8_t* tab, cudaStream_t s) {
+    if (rows <= 0) return QRM_OK;
+    long long warps = (long long)rows * (K / 32);
+    int grid = (int)std::min<long long>((warps + 7) / 8, 148 * 16);
+    qrm::xquant_kernel<<<grid, 256, 0, s>>>(src, K, rows, tab, qrm::xtab_stride(K));
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "xquant launch: %s", cudaGetErrorString(e));
+}
+
+// gate/up (M=2) or down (M=1) for one format: the integer tensor-core kernel
+// for Q4_K / Q8_0 / Q4_0, else the bulk-copy staged kernel
 // when the tile fields are 16-byte multiples, else the register kernel.
 int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s) {
     const int U = p.cols / 32;
@@ -160,6 +223,11 @@ int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_c
     int rc = QRM_OK;
 #define QRM_GEMV_CASE(F)                                                                        \
     case F:                                                                                     \
+        if (F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) {                               \
+            rc = gateup ? launch_imma<(F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) ? F : qrm::Q4_K, 2>(p.T, p, sm_count, err, s, &used) \
+                        : launch_imma<(F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) ? F : qrm::Q4_K, 1>(p.T, p, sm_count, err, s, &used); \
+            if (rc || used) return rc;                                                          \
+        }                                                                                       \
         if (gateup) {                                                                           \
             rc = launch_tma<F, 2>(nt, p, sm_count, err, s, &used);                    \
             if (rc || used) return rc;                                                          \
@@ -217,6 +285,8 @@ struct qrm_layer {
     qrm::Schedule* sched = nullptr;
     uint8_t* staging = nullptr;
     size_t staging_bytes = 0;
+    uint8_t* xtab_gu = nullptr;   // activation tables of the gate/up inputs [T]
+    uint8_t* xtab_dn = nullptr;   // of the down inputs [T*k routed | T shared]
     int last_T = 0;
     const float* last_xn = nullptr;
     // per-stage timing
@@ -240,7 +310,7 @@ static void free_layer(qrm_layer* L) {
     if (L->stream) cudaStreamSynchronize(L->stream);
     void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
-                    L->inv_perm, L->offsets, L->active, L->sched, L->staging};
+                    L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     clear_graphs(L);
@@ -295,6 +365,8 @@ static int alloc_work(qrm_layer* L, int T) {
         QRM_CUDA(cudaMalloc(&L->hs, sizeof(float) * T * f));
         QRM_CUDA(cudaMalloc(&L->ys, sizeof(float) * T * d));
     }
+    QRM_CUDA(cudaMalloc(&L->xtab_gu, (size_t)qrm::xtab_stride(d) * T));
+    QRM_CUDA(cudaMalloc(&L->xtab_dn, (size_t)qrm::xtab_stride(f) * (Tk + T)));
     L->cap_T = T;
     return QRM_OK;
 }
@@ -552,7 +624,24 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
     for (int stage = 0; stage < 2; stage++) {
         const bool gu = stage == 0;
+        // activation tables for the integer tensor-core kernel
+        const int frs = gu ? D.fmt_gate : D.fmt_down, fss = gu ? D.fmt_sh_gate : D.fmt_sh_down;
+        const int rows_s = gu ? f : d, cols_s = gu ? d : f;
+        const bool want_tab = imma_usable(frs, rows_s, cols_s, gu) || (shared && imma_usable(fss, rows_s, cols_s, gu));
+        if (want_tab) {
+            int rc;
+            if (gu) {
+                rc = launch_xquant(xn, d, T, L->xtab_gu, s);
+            } else {
+                rc = launch_xquant(L->h, f, T * k, L->xtab_dn, s);
+                if (!rc && shared) rc = launch_xquant(L->hs, f, T, L->xtab_dn + (size_t)qrm::xtab_stride(f) * T * k, s);
+            }
+            if (rc) return rc;
+        }
         qrm::GemvParams gp{};
+        gp.xtab = want_tab ? (gu ? L->xtab_gu : L->xtab_dn) : nullptr;
+        gp.xtab_stride = qrm::xtab_stride(cols_s);
+        gp.xtab_shared_base = gu ? 0 : T * k;
         gp.mats = L->mats_dev;
         gp.active = L->active;
         gp.offsets = L->offsets;
@@ -743,7 +832,9 @@ struct qrm_matrix {
     qrm::MatDev mat{};
     qrm::MatDev* mats_dev = nullptr;  // [3]; slot 2 is the matrix
     uint8_t* data = nullptr;
-    int32_t* misc = nullptr;          // active[1], offsets[2], n_active, ctr
+    int32_t* misc = nullptr;          // active[1], offsets[2], n_active, ctr, err
+    uint8_t* xtab = nullptr;          // activation tables of the last call's rows
+    int xtab_rows = 0;
 };
 
 extern "C" int qrm_matrix_create(int device, int fmt, int64_t rows, int64_t cols, const void* bytes, size_t nbytes,
@@ -800,6 +891,7 @@ extern "C" void qrm_matrix_destroy(qrm_matrix* M) {
     if (M->data) cudaFree(M->data);
     if (M->mats_dev) cudaFree(M->mats_dev);
     if (M->misc) cudaFree(M->misc);
+    if (M->xtab) cudaFree(M->xtab);
     delete M;
 }
 
@@ -831,6 +923,22 @@ extern "C" int qrm_matrix_gemv(qrm_matrix* M, const float* x_dev, int T, float* 
     gp.routed_by_token = 0;
     gp.mode = 2;
     gp.has_shared = 1;
+    if (imma_usable(M->mat.fmt, M->mat.rows, M->mat.cols, false)) {
+        if (M->xtab_rows < T) {
+            QRM_CUDA(cudaStreamSynchronize(s));
+            if (M->xtab) cudaFree(M->xtab);
+            M->xtab = nullptr;
+            M->xtab_rows = 0;
+            if (cudaMalloc(&M->xtab, (size_t)qrm::xtab_stride(M->mat.cols) * T) != cudaSuccess)
+                return fail(QRM_E_NOMEM, "activation table allocation failed");
+            M->xtab_rows = T;
+        }
+        int rc = launch_xquant(x_dev, M->mat.cols, T, M->xtab, s);
+        if (rc) return rc;
+        gp.xtab = M->xtab;
+        gp.xtab_stride = qrm::xtab_stride(M->mat.cols);
+        gp.xtab_shared_base = 0;
+    }
     return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, M->misc + 5, s);
 }
 
