@@ -162,6 +162,22 @@ int  qrm_matrix_create(int device, int fmt, int64_t rows, int64_t cols,
 void qrm_matrix_destroy(qrm_matrix* m);
 int  qrm_matrix_gemv(qrm_matrix* m, const float* x_dev, int T, float* y_dev, void* stream);
 
+/* qrm_matrix_gemv without any device allocation.  No counterpart in the
+ * reference.  qrm_matrix_gemv grows the matrix's activation-table buffer when
+ * T rises (stream synchronise, cudaFree, cudaMalloc); cudaFree synchronises
+ * the whole device, so a caller that overlaps work on several streams, or one
+ * that has committed all HBM to weights and caches up front, cannot take that
+ * path.  This variant keeps the tables (Q4_K / Q8_0 / Q4_0 matrices) in a
+ * fixed 1 MiB device array per device:
+ *   - T * (2*cols + 8*cols/32, rounded up to 16) must be <= 1048576 bytes,
+ *     else QRM_E_CAPACITY (cols 7168: T <= 65);
+ *   - the array is shared by every call on the device: calls that overlap
+ *     in time (other streams, other threads, other matrices) race on it;
+ *   - the first call on each device looks up the array's address
+ *     (cudaGetSymbolAddress) and must come before any stream capture.
+ * Nothing needs to start at zero: every table byte read is written first. */
+int  qrm_matrix_gemv_static(qrm_matrix* m, const float* x_dev, int T, float* y_dev, void* stream);
+
 /* ---- synthetic weights on the device (the reference's `synthesize`,
  * src/QuantRunner.Cli/Program.cs:247-369) ----
  * qrm_synth_gaussian fills dst_dev[n] with sigma * N(0,1) from a

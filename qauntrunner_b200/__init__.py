@@ -89,6 +89,7 @@ _SIGS = {
     "qrm_matrix_create": (C.c_int, [C.c_int, C.c_int, C.c_int64, C.c_int64, P, C.c_size_t, C.POINTER(P)]),
     "qrm_matrix_destroy": (None, [P]),
     "qrm_matrix_gemv": (C.c_int, [P, P, C.c_int, P, P]),
+    "qrm_matrix_gemv_static": (C.c_int, [P, P, C.c_int, P, P]),
     "qrm_synth_gaussian": (C.c_int, [P, C.c_int64, C.c_uint64, C.c_float, P]),
     "qrm_synth_quantize": (C.c_int, [C.c_int, P, C.c_int64, P, P]),
 }
@@ -251,6 +252,11 @@ class Matrix:
 
     def gemv(self, x_ptr, T, y_ptr, stream=None):
         _check(lib().qrm_matrix_gemv(self._h, x_ptr, T, y_ptr, stream))
+
+    def gemv_static(self, x_ptr, T, y_ptr, stream=None):
+        """gemv with the activation tables in the library's fixed per-device
+        scratch (no allocation; concurrent calls on one device race)."""
+        _check(lib().qrm_matrix_gemv_static(self._h, x_ptr, T, y_ptr, stream))
 
     def close(self):
         if getattr(self, "_h", None):

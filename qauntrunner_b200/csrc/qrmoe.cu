@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <map>
+#include <mutex>
 #include <tuple>
 #include <cstdio>
 #include <cstring>
@@ -936,6 +937,75 @@ extern "C" int qrm_matrix_gemv(qrm_matrix* M, const float* x_dev, int T, float* 
         int rc = launch_xquant(x_dev, M->mat.cols, T, M->xtab, s);
         if (rc) return rc;
         gp.xtab = M->xtab;
+        gp.xtab_stride = qrm::xtab_stride(M->mat.cols);
+        gp.xtab_shared_base = 0;
+    }
+    return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, M->misc + 5, s);
+}
+
+// ---------------------------------------------------------------- matrix operator, no allocation
+// qrm_matrix_gemv_static keeps the activation tables of the integer
+// tensor-core kernel in this fixed device array (one copy per device, shared
+// by every call on that device) instead of the matrix's growable buffer.  The
+// tables need no zeroing: xquant_kernel writes every byte the GEMV reads.
+constexpr size_t kStaticTabBytes = (size_t)1 << 20;
+static __device__ __align__(256) uint8_t g_static_tab[kStaticTabBytes];
+
+namespace {
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+uint8_t* g_static_tab_ptr[kStaticMaxDevices];  // device address of g_static_tab, per device
+}  // namespace
+
+extern "C" int qrm_matrix_gemv_static(qrm_matrix* M, const float* x_dev, int T, float* y_dev, void* stream) {
+    if (!M || !x_dev || !y_dev) return fail(QRM_E_INVALID, "NULL argument");
+    if (T <= 0) return fail(QRM_E_INVALID, "T must be positive");
+    if (M->device < 0 || M->device >= kStaticMaxDevices)
+        return fail(QRM_E_INVALID, "device %d is outside the static scratch table", M->device);
+    QRM_CUDA(cudaSetDevice(M->device));
+    cudaStream_t s = (cudaStream_t)stream;
+    const bool tables = imma_usable(M->mat.fmt, M->mat.rows, M->mat.cols, false);
+    uint8_t* tab = nullptr;
+    if (tables) {
+        const size_t need = (size_t)qrm::xtab_stride(M->mat.cols) * (size_t)T;
+        if (need > kStaticTabBytes)
+            return fail(QRM_E_CAPACITY, "T = %d needs %zu bytes of activation tables; the static scratch holds %zu",
+                        T, need, kStaticTabBytes);
+        std::lock_guard<std::mutex> lock(g_static_mu);
+        if (!g_static_tab_ptr[M->device]) {
+            void* p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_static_tab);
+            if (e != cudaSuccess) return fail(QRM_E_CUDA, "static scratch address: %s", cudaGetErrorString(e));
+            g_static_tab_ptr[M->device] = static_cast<uint8_t*>(p);
+        }
+        tab = g_static_tab_ptr[M->device];
+    }
+    QRM_CUDA(cudaMemsetAsync(M->misc + 4, 0, sizeof(int32_t), s));
+    qrm::GemvParams gp{};
+    gp.mats = M->mats_dev;
+    gp.active = M->misc;
+    gp.offsets = M->misc + 1;
+    gp.perm = M->misc;
+    gp.n_active = M->misc + 3;
+    gp.ctr = M->misc + 4;
+    gp.x_routed = x_dev;
+    gp.x_shared = x_dev;
+    gp.out_routed = y_dev;
+    gp.out_shared = y_dev;
+    gp.T = T;
+    gp.k = 1;
+    gp.E = 0;
+    gp.rows = M->mat.rows;
+    gp.cols = M->mat.cols;
+    gp.tiles = (gp.rows + kRDown - 1) / kRDown;
+    gp.limit = 0.f;
+    gp.routed_by_token = 0;
+    gp.mode = 2;
+    gp.has_shared = 1;
+    if (tables) {
+        int rc = launch_xquant(x_dev, M->mat.cols, T, tab, s);
+        if (rc) return rc;
+        gp.xtab = tab;
         gp.xtab_stride = qrm::xtab_stride(M->mat.cols);
         gp.xtab_shared_base = 0;
     }
