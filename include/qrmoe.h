@@ -169,8 +169,8 @@ int  qrm_matrix_gemv(qrm_matrix* m, const float* x_dev, int T, float* y_dev, voi
  * that has committed all HBM to weights and caches up front, cannot take that
  * path.  This variant keeps the tables (Q4_K / Q8_0 / Q4_0 matrices) in a
  * fixed 1 MiB device array per device:
- *   - T * (2*cols + 8*cols/32, rounded up to 16) must be <= 1048576 bytes,
- *     else QRM_E_CAPACITY (cols 7168: T <= 65);
+ *   - T * (2*cols + 128 + cols/4, rounded up to 16) must be <= 1048576
+ *     bytes, else QRM_E_CAPACITY (cols 7168: T <= 64);
  *   - the array is shared by every call on the device: calls that overlap
  *     in time (other streams, other threads, other matrices) race on it;
  *   - the first call on each device looks up the array's address

@@ -333,6 +333,7 @@ struct GemvParams {
     const uint8_t* xtab;
     int xtab_stride;
     int xtab_shared_base;
+    int xtab_rows;             // table rows written for this launch
 };
 
 __device__ __forceinline__ float swiglu(float g, float u, float limit) {

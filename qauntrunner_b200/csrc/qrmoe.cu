@@ -16,6 +16,7 @@
 #include <mutex>
 #include <tuple>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -153,16 +154,43 @@ int launch_tma(int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cud
 
 // Integer tensor-core kernel (Q4_K, Q8_0, Q4_0 with 256-multiple rows);
 // needs the activation tables of p.xtab (written by xquant_kernel).
-template <int FMT, int M, int NTK, int RTILES>
-int launch_imma_t(const qrm::GemvParams& p, const qrm::ImmaConfig& cfg, int sm_count, int32_t* err, cudaStream_t s) {
-    // consumer warps: RTILES x (K slices); the slice count divides the
-    // super-blocks evenly where a divisor close to the 16-warp limit exists
-    const int nsb = p.cols / 256, lim = std::min(nsb, 16 / RTILES);
+
+// K slices per row tile: a divisor of the super-block count close to the
+// warp limit, else the limit itself (uneven slices)
+int imma_kslices(int nsb, int rtiles) {
+    const int lim = std::min(nsb, qrm::kImmaMaxWarps / rtiles);
     int nks = 1;
     for (int d = lim; d >= 1; d--)
         if (nsb % d == 0) { nks = d; break; }
-    if (2 * nks <= lim) nks = lim;
+    return 2 * nks <= lim ? lim : nks;
+}
+
+// Row tiles per item.  Default: one for long rows (>= 16 super-blocks), two
+// otherwise.  QRM_IMMA_RTILES="<gate/up>,<down>" overrides it for tuning runs
+// (gate/up 1 or 2, down 1, 2 or 4).
+int imma_rtiles(bool gateup, int nsb) {
+    static int env[2] = {-1, -1};
+    static bool read = false;
+    if (!read) {
+        const char* v = getenv("QRM_IMMA_RTILES");
+        if (v) sscanf(v, "%d,%d", &env[0], &env[1]);
+        read = true;
+    }
+    const int e = env[gateup ? 0 : 1];
+    if (e == 1 || e == 2 || (!gateup && e == 4)) return e;
+    return nsb >= 16 ? 1 : 2;
+}
+
+template <int FMT, int M, int NTK, int RTILES>
+int launch_imma_t(const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s, bool* used) {
+    constexpr int RT = qrm::kImmaRows / M;
+    const int nks = imma_kslices(p.cols / 256, RTILES);
     const int CW = nks * RTILES;
+    qrm::ImmaConfig cfg;
+    if (!qrm::imma_plan<FMT>(p.cols, qrm::kImmaRows * RTILES, NTK, CW, p.xtab_rows, 227 * 1024, &cfg)) return QRM_OK;
+    qrm::GemvParams q = p;
+    q.tiles = p.rows / (RT * RTILES);
+    *used = true;
     auto fn = qrm::expert_gemv_imma_kernel<FMT, M, NTK, RTILES>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -170,7 +198,7 @@ int launch_imma_t(const qrm::GemvParams& p, const qrm::ImmaConfig& cfg, int sm_c
             return fail(QRM_E_CUDA, "expert kernel attribute");
         attr_set = true;
     }
-    fn<<<sm_count, (CW + 1) * 32, qrm::imma_smem_bytes(cfg), s>>>(p, cfg, err);
+    fn<<<sm_count, (CW + 1) * 32, qrm::imma_smem_bytes(cfg), s>>>(q, cfg, err);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
 }
@@ -180,8 +208,7 @@ bool imma_format(int fmt) { return fmt == qrm::Q4_K || fmt == qrm::Q8_0 || fmt =
 // true when the integer kernel will take this matrix shape
 bool imma_usable(int fmt, int rows, int cols, bool gateup) {
     if (!imma_format(fmt) || cols % 256) return false;
-    const int rt = gateup ? 8 : 16;
-    return rows % (2 * rt) == 0;
+    return rows % (gateup ? 8 : 16) == 0;
 }
 
 template <int FMT, int M>
@@ -189,18 +216,21 @@ int launch_imma(int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cud
     *used = false;
     if (!p.xtab) return QRM_OK;
     constexpr int RT = qrm::kImmaRows / M;
-    const int nsb = p.cols / 256;
-    const int rtiles = nsb >= 16 ? 1 : 2;
-    if (p.rows % (RT * rtiles)) return QRM_OK;
-    const int ntk = T <= 1 ? 1 : 2;
-    qrm::ImmaConfig cfg;
-    if (!qrm::imma_plan<FMT>(p.cols, qrm::kImmaRows * rtiles, ntk, 227 * 1024, &cfg)) return QRM_OK;
-    qrm::GemvParams q = p;
-    q.tiles = p.rows / (RT * rtiles);
-    *used = true;
-    if (rtiles == 1)
-        return ntk == 1 ? launch_imma_t<FMT, M, 1, 1>(q, cfg, sm_count, err, s) : launch_imma_t<FMT, M, 2, 1>(q, cfg, sm_count, err, s);
-    return ntk == 1 ? launch_imma_t<FMT, M, 1, 2>(q, cfg, sm_count, err, s) : launch_imma_t<FMT, M, 2, 2>(q, cfg, sm_count, err, s);
+    int rtiles = imma_rtiles(M == 2, p.cols / 256);
+    while (rtiles > 1 && p.rows % (RT * rtiles)) rtiles >>= 1;
+    if (p.rows % RT) return QRM_OK;
+    const bool one = T <= 1;
+#define QRM_IMMA_RT(R)                                                                          \
+    if (rtiles == R)                                                                            \
+        return one ? launch_imma_t<FMT, M, 1, R>(p, sm_count, err, s, used)                     \
+                   : launch_imma_t<FMT, M, 2, R>(p, sm_count, err, s, used);
+    QRM_IMMA_RT(1)
+    QRM_IMMA_RT(2)
+    if constexpr (M == 1) {
+        QRM_IMMA_RT(4)
+    }
+#undef QRM_IMMA_RT
+    return QRM_OK;
 }
 
 int launch_xquant(const float* src, int K, int rows, uint8_t* tab, cudaStream_t s) {
@@ -643,6 +673,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.xtab = want_tab ? (gu ? L->xtab_gu : L->xtab_dn) : nullptr;
         gp.xtab_stride = qrm::xtab_stride(cols_s);
         gp.xtab_shared_base = gu ? 0 : T * k;
+        gp.xtab_rows = gu ? T : T * k + (shared ? T : 0);
         gp.mats = L->mats_dev;
         gp.active = L->active;
         gp.offsets = L->offsets;
@@ -939,6 +970,7 @@ extern "C" int qrm_matrix_gemv(qrm_matrix* M, const float* x_dev, int T, float* 
         gp.xtab = M->xtab;
         gp.xtab_stride = qrm::xtab_stride(M->mat.cols);
         gp.xtab_shared_base = 0;
+        gp.xtab_rows = T;
     }
     return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, M->misc + 5, s);
 }
@@ -1008,6 +1040,7 @@ extern "C" int qrm_matrix_gemv_static(qrm_matrix* M, const float* x_dev, int T, 
         gp.xtab = tab;
         gp.xtab_stride = qrm::xtab_stride(M->mat.cols);
         gp.xtab_shared_base = 0;
+        gp.xtab_rows = T;
     }
     return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, M->misc + 5, s);
 }

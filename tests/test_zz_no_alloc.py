@@ -57,7 +57,7 @@ def test_static_scratch_matches_allocating_gemv(torch_cuda, fmt):
 def test_static_scratch_rejects_oversized_batch(torch_cuda):
     torch = torch_cuda
     rows, cols = 256, 1536
-    stride = (2 * cols + 8 * (cols // 32) + 15) // 16 * 16
+    stride = (2 * cols + 128 + 8 * (cols // 32) + 15) // 16 * 16
     T = SCRATCH_BYTES // stride + 1
     m = _matrix(O.Q4_K, rows, cols, 5)
     try:
