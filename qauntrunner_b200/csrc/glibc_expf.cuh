@@ -104,8 +104,9 @@ QRM_HD float to_f32(double y) {
 #endif
 }
 
-// glibc-identical expf.
-QRM_HD float expf_glibc(float x) {
+// glibc-identical expf with the table T[] at tab (device code may pass a
+// shared-memory copy: lanes index it divergently).
+QRM_HD float expf_glibc_t(float x, const uint64_t* tab) {
     const double kInvLn2N = 0x1.71547652b82fep+0 * 32;
     const double kShift = 0x1.8p+52;
     const double kC0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32;
@@ -124,11 +125,7 @@ QRM_HD float expf_glibc(float x) {
     uint64_t ki = f64_bits(kd);
     kd = add64(kd, -kShift);
     double r = fma64(kInvLn2N, xd, -kd);
-#if defined(__CUDA_ARCH__)
-    uint64_t t = kExpfTabDev[ki % 32];
-#else
-    uint64_t t = kExpfTabHost[ki % 32];
-#endif
+    uint64_t t = tab[ki % 32];
     t += ki << (52 - 5);
     double s = f64_from(t);
     double z = fma64(kC0, r, kC1);
@@ -137,6 +134,15 @@ QRM_HD float expf_glibc(float x) {
     y = fma64(z, r2, y);
     y = mul64(y, s);
     return to_f32(y);
+}
+
+// glibc-identical expf.
+QRM_HD float expf_glibc(float x) {
+#if defined(__CUDA_ARCH__)
+    return expf_glibc_t(x, kExpfTabDev);
+#else
+    return expf_glibc_t(x, kExpfTabHost);
+#endif
 }
 
 }  // namespace qrm

@@ -305,6 +305,7 @@ struct qrm_layer {
     std::vector<uint8_t> uploaded;      // (E+1)*3
     float* norm_w = nullptr;
     float* router = nullptr;
+    float* router_lm = nullptr;   // lane-major copy of the router rows (fused router)
     float* router_bias = nullptr;
     float* offset = nullptr;
     bool has_norm = false, has_router = false, has_bias = false, has_offset = false;
@@ -339,7 +340,7 @@ static void free_layer(qrm_layer* L) {
     if (!L) return;
     cudaSetDevice(L->desc.device);
     if (L->stream) cudaStreamSynchronize(L->stream);
-    void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_bias, L->offset, L->x, L->xn,
+    void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_lm, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
                     L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn};
     for (void* p : ptrs)
@@ -459,12 +460,14 @@ extern "C" int qrm_create(const qrm_layer_desc* desc, qrm_layer** out) {
         cudaMemcpy(L->mats_dev, L->mats.data(), sizeof(qrm::MatDev) * L->mats.size(), cudaMemcpyHostToDevice) != cudaSuccess)
         return bail(fail(QRM_E_NOMEM, "matrix table allocation failed"));
     if (cudaMalloc(&L->norm_w, sizeof(float) * d) != cudaSuccess || cudaMalloc(&L->router, sizeof(float) * (size_t)E * d) != cudaSuccess ||
+        cudaMalloc(&L->router_lm, sizeof(float) * (size_t)E * 8 * qrm::route_lane_pitch(d)) != cudaSuccess ||
         cudaMalloc(&L->router_bias, sizeof(float) * E) != cudaSuccess || cudaMalloc(&L->offset, sizeof(float) * E) != cudaSuccess)
         return bail(fail(QRM_E_NOMEM, "router allocation failed"));
     rc = alloc_work(L, desc->max_tokens);
     if (rc) return bail(rc);
     // kernels with large dynamic shared memory
     if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(qrm::route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(qrm::dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
         return bail(fail(QRM_E_CUDA, "kernel attribute"));
     *out = L;
@@ -487,6 +490,8 @@ extern "C" int qrm_upload_router(qrm_layer* L, const float* w, const float* bias
     clear_graphs(L);
     QRM_CUDA(cudaSetDevice(L->desc.device));
     QRM_CUDA(cudaMemcpy(L->router, w, sizeof(float) * (size_t)L->desc.n_experts * L->desc.d_model, cudaMemcpyHostToDevice));
+    qrm::router_lane_major_kernel<<<L->sm_count * 4, 256>>>(L->router, L->router_lm, L->desc.n_experts, L->desc.d_model);
+    QRM_CUDA(cudaDeviceSynchronize());
     if (bias) QRM_CUDA(cudaMemcpy(L->router_bias, bias, sizeof(float) * L->desc.n_experts, cudaMemcpyHostToDevice));
     L->has_bias = bias != nullptr;
     L->has_router = true;
@@ -616,39 +621,50 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const bool prof = L->profiling;
     auto mark = [&](int i) { if (prof) cudaEventRecordWithFlags(L->ev[i], s, cudaEventRecordExternal); };
     mark(0);
-    // 1. RMSNorm + router logits
+    // 1. RMSNorm + router logits, 2. top-k, 3. dispatch
     const float* xn = L->xn;
-    if (T <= qrm::route_small_max_tokens(d)) {
-        qrm::RouteParams rp{x, L->norm_w, L->router, L->has_offset ? L->offset : nullptr, L->xn, L->logits, T, d, E,
-                            (flags & QRM_APPLY_NORM) ? 1 : 0, D.rms_eps};
-        int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
-        qrm::route_small_kernel<<<grid, qrm::kRouteThreads, qrm::route_small_smem(d, T), s>>>(rp);
-    } else {
-        if (flags & QRM_APPLY_NORM) {
-            qrm::rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, L->norm_w, L->xn, T, d, D.rms_eps);
-        } else {
-            xn = x;
-        }
-        dim3 grid((T + qrm::kLT - 1) / qrm::kLT, (E + qrm::kLE - 1) / qrm::kLE);
-        qrm::logits_tiled_kernel<<<grid, 256, 0, s>>>(xn, L->router, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
-    }
-    QRM_CUDA(cudaGetLastError());
-    mark(1);
-    L->last_xn = xn;
-    // 2. top-k and 3. dispatch (fused into one single-CTA kernel for small T)
     qrm::TopkParams tp{L->logits, L->has_bias ? L->router_bias : nullptr, topk_idx, topk_w, T, E, k,
                        D.moe_sigmoid ? 1 : 0, D.routed_scale};
-    const bool fused = T <= qrm::kFusedTopkMaxT;
-    if (!fused) {
-        qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
-        QRM_CUDA(cudaGetLastError());
-    }
-    mark(2);
     qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->offsets, L->active, L->sched, T, k, E,
                            L->first_expert, L->n_local, shared ? 1 : 0};
-    qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, T, fused), s>>>(dp, tp, fused ? 1 : 0);
-    QRM_CUDA(cudaGetLastError());
-    mark(3);
+    qrm::RouteParams rp{x, L->norm_w, L->router, L->has_offset ? L->offset : nullptr, L->xn, L->logits, T, d, E,
+                        (flags & QRM_APPLY_NORM) ? 1 : 0, D.rms_eps};
+    if (T <= qrm::route_fused_max_tokens(d, E) && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+        // one launch: every CTA its experts' logits, the last CTA top-k + dispatch
+        const int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
+        qrm::route_fused_kernel<<<grid, qrm::kRouteThreads, qrm::route_fused_smem(d, T, E), s>>>(
+            qrm::RouteFusedParams{rp, L->router_lm, tp, dp});
+        QRM_CUDA(cudaGetLastError());
+        mark(1);
+        mark(2);
+        mark(3);
+    } else {
+        if (T <= qrm::route_small_max_tokens(d)) {
+            int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
+            qrm::route_small_kernel<<<grid, qrm::kRouteThreads, qrm::route_small_smem(d, T), s>>>(rp);
+        } else {
+            if (flags & QRM_APPLY_NORM) {
+                qrm::rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, L->norm_w, L->xn, T, d, D.rms_eps);
+            } else {
+                xn = x;
+            }
+            dim3 grid((T + qrm::kLT - 1) / qrm::kLT, (E + qrm::kLE - 1) / qrm::kLE);
+            qrm::logits_tiled_kernel<<<grid, 256, 0, s>>>(xn, L->router, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
+        }
+        QRM_CUDA(cudaGetLastError());
+        mark(1);
+        // top-k and dispatch (fused into one single-CTA kernel for T <= 32)
+        const bool fused = T <= qrm::kFusedTopkMaxT;
+        if (!fused) {
+            qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
+            QRM_CUDA(cudaGetLastError());
+        }
+        mark(2);
+        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, T, fused), s>>>(dp, tp, fused ? 1 : 0);
+        QRM_CUDA(cudaGetLastError());
+        mark(3);
+    }
+    L->last_xn = xn;
     // 4. gate/up (+ SwiGLU) and 5. down
     const int nt = pick_nt(T);
     const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU

@@ -15,6 +15,7 @@
 // running the T*E*8 chains side by side.
 #pragma once
 #include "common.cuh"
+#include "gemv_tma.cuh"
 #include "glibc_expf.cuh"
 
 namespace qrm {
@@ -28,15 +29,34 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
 // acc + sum over i = lane, lane+8, ... < n8 of a[i]*b[i], in that order (one
-// Vector256 lane of SimdMath.DotF32 / RmsNorm).  Sixteen products are loaded
-// ahead so the dependent adds run back to back.
+// Vector256 lane of SimdMath.DotF32 / RmsNorm).  The sixteen products of the
+// next block are formed while the current block's dependent adds run.
 __device__ __forceinline__ float lane_chain(const float* __restrict__ a, const float* __restrict__ b, int lane,
                                             int n8, float acc) {
     int i = 0;
-    for (; i + 128 <= n8; i += 128) {
-        float p[16];
+    if (n8 >= 256) {
+        // three-stage pipeline over blocks of 16 steps: the operands of block
+        // i+2 are loaded and the products of block i+1 formed while block i's
+        // dependent adds run, so no add waits on a load
+        float ra[16], rb[16], p[16];
 #pragma unroll
-        for (int u = 0; u < 16; u++) p[u] = __fmul_rn(a[i + 8 * u + lane], b[i + 8 * u + lane]);
+        for (int u = 0; u < 16; u++) p[u] = __fmul_rn(a[8 * u + lane], b[8 * u + lane]);
+#pragma unroll
+        for (int u = 0; u < 16; u++) { ra[u] = a[128 + 8 * u + lane]; rb[u] = b[128 + 8 * u + lane]; }
+        for (i = 256; i + 128 <= n8; i += 128) {
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                acc = __fadd_rn(acc, p[u]);
+                p[u] = __fmul_rn(ra[u], rb[u]);
+                ra[u] = a[i + 8 * u + lane];
+                rb[u] = b[i + 8 * u + lane];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+            acc = __fadd_rn(acc, p[u]);
+            p[u] = __fmul_rn(ra[u], rb[u]);
+        }
 #pragma unroll
         for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, p[u]);
     }
@@ -332,14 +352,14 @@ struct TopkParams {
 // sources) are this warp's shared scratch of kMaxE floats each.
 __device__ __forceinline__ void topk_token(const TopkParams& p, int t, int lane, float* v, float* s) {
     const int E = p.E, k = p.k;
-    const float* lg = p.logits + (size_t)t * E;
+    const float* lg = p.logits + (size_t)t * E;   // read through L2: other CTAs may have written it
     if (!p.sigmoid) {
         // max from float.MinValue; comparisons skip NaN like the reference loop
         float mx = -3.40282347e+38f;
-        for (int i = lane; i < E; i += 32) { float a = lg[i]; if (a > mx) mx = a; }
+        for (int i = lane; i < E; i += 32) { float a = __ldcg(lg + i); if (a > mx) mx = a; }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) { float b = __shfl_xor_sync(0xffffffffu, mx, o); if (b > mx) mx = b; }
-        for (int i = lane; i < E; i += 32) s[i] = expf_glibc(__fsub_rn(lg[i], mx));
+        for (int i = lane; i < E; i += 32) s[i] = expf_glibc(__fsub_rn(__ldcg(lg + i), mx));
         __syncwarp();
         float sum = 0.f;
         if (lane == 0) {
@@ -358,7 +378,7 @@ __device__ __forceinline__ void topk_token(const TopkParams& p, int t, int lane,
         for (int i = lane; i < E; i += 32) { float q = __fmul_rn(s[i], inv); s[i] = q; v[i] = q; }
     } else {
         for (int i = lane; i < E; i += 32) {
-            float sg = __fdiv_rn(1.f, __fadd_rn(1.f, expf_glibc(-lg[i])));
+            float sg = __fdiv_rn(1.f, __fadd_rn(1.f, expf_glibc(-__ldcg(lg + i))));
             s[i] = sg;
             v[i] = p.bias ? __fadd_rn(sg, p.bias[i]) : sg;
         }
@@ -426,7 +446,8 @@ struct Schedule {
     int32_t n_active;         // routed experts (of the local window) with assignments
     int32_t err;              // device error flags (ERR_*)
     int32_t ctr[4];           // work counters: gate/up, gate/up shared, down, down shared
-    int32_t pad[2];
+    int32_t route_arrivals;   // CTAs of the fused router done with their logits (0 between launches)
+    int32_t pad;
 };
 
 struct DispatchParams {
@@ -542,6 +563,420 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
         if (e >= 0 && lane == leader) atomicAdd(&base[e], __popc(peers));
         __syncthreads();
     }
+}
+
+// ---------------------------------------------------------------------------
+// Lane-major router rows for the fused router: row e is stored as 8 lanes of P
+// floats, lane j holding columns j, j+8, j+16, ... (the columns of one
+// Vector256 lane of SimdMath.DotF32) contiguously, zero-padded to P >= d/8
+// with P = 4 mod 32 (16-byte aligned, 8 lanes on distinct banks).
+__host__ __device__ inline int route_lane_pitch(int d) { return (d / 8 + 27) / 32 * 32 + 4; }
+
+__global__ void router_lane_major_kernel(const float* __restrict__ w, float* __restrict__ wp, int E, int d) {
+    const int P = route_lane_pitch(d), m8 = d / 8;
+    const long long total = (long long)E * 8 * P;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int e = (int)(i / (8 * P));
+        const int r = (int)(i - (long long)e * 8 * P), j = r / P, m = r - j * P;
+        wp[i] = m < m8 ? w[(size_t)e * d + 8 * m + j] : 0.f;
+    }
+}
+
+// acc + sum over m < nm of a[m]*b[m], in that order, from lane-major rows
+// (16-byte aligned, nm % 4 == 0): one 128-bit load covers four steps, and the
+// loads of the next 16 steps are in flight while the current adds run.
+__device__ __forceinline__ float lane_chain4(const float* __restrict__ a, const float* __restrict__ b, int nm,
+                                             float acc) {
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    const int n4 = nm / 4;
+    int q = 0;
+    if (n4 >= 8) {
+        float4 A[4], B[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) { A[u] = a4[u]; B[u] = b4[u]; }
+        for (q = 4; q + 4 <= n4; q += 4) {
+            float4 An[4], Bn[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) { An[u] = a4[q + u]; Bn[u] = b4[q + u]; }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                acc = __fadd_rn(acc, __fmul_rn(A[u].x, B[u].x));
+                acc = __fadd_rn(acc, __fmul_rn(A[u].y, B[u].y));
+                acc = __fadd_rn(acc, __fmul_rn(A[u].z, B[u].z));
+                acc = __fadd_rn(acc, __fmul_rn(A[u].w, B[u].w));
+                A[u] = An[u];
+                B[u] = Bn[u];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            acc = __fadd_rn(acc, __fmul_rn(A[u].x, B[u].x));
+            acc = __fadd_rn(acc, __fmul_rn(A[u].y, B[u].y));
+            acc = __fadd_rn(acc, __fmul_rn(A[u].z, B[u].z));
+            acc = __fadd_rn(acc, __fmul_rn(A[u].w, B[u].w));
+        }
+    }
+    for (; q < n4; q++) {
+        const float4 x = a4[q], y = b4[q];
+        acc = __fadd_rn(acc, __fmul_rn(x.x, y.x));
+        acc = __fadd_rn(acc, __fmul_rn(x.y, y.y));
+        acc = __fadd_rn(acc, __fmul_rn(x.z, y.z));
+        acc = __fadd_rn(acc, __fmul_rn(x.w, y.w));
+    }
+    return acc;
+}
+
+// ---------------------------------------------------------------------------
+// Fused small-T router: RMSNorm, router logits, top-k and dispatch in one
+// launch.  CTA b owns experts [kRouteEPC*b, +kRouteEPC).  Thread 0 bulk-copies
+// the token rows, the norm weights and the CTA's router rows into shared
+// memory (one copy per row, each group on its own mbarrier, so the RMSNorm
+// chains start as soon as the token rows land); every CTA recomputes the
+// RMSNorm of its T tokens and writes its slice of the xn columns.  The last
+// CTA to finish its logits (arrival counter in the schedule) ranks every
+// token's logits and dispatches, so routing costs one launch.
+// Shared memory: W[EPC][d + 4] | X[T][d] | NW[d] | red | scl | barriers; the
+// top-k / dispatch scratch of the last CTA reuses W.
+constexpr int kRouteFusedMaxT = 4;   // one warp per token in the tail; T*k <= 32
+
+__host__ __device__ inline size_t route_fused_main_floats(int d, int T, int E) {
+    // W[EPC][8P] | X[T][d] | XP[T][8P] | NW | red | scl (padded to 4) | bias[E] (padded to 4) | exp table
+    const size_t P8 = (size_t)8 * route_lane_pitch(d);
+    return (size_t)kRouteEPC * P8 + (size_t)T * d + (size_t)T * P8 + d + (size_t)T * kRouteEPC * 8 +
+           (size_t)(T + 3) / 4 * 4 + (size_t)(E + 3) / 4 * 4 + 64;
+}
+inline size_t route_tail_smem(int E, int T) {
+    return sizeof(float) * (size_t)2 * T * E + sizeof(int) * 64;
+}
+inline size_t route_fused_smem(int d, int T, int E) {
+    return (sizeof(float) * route_fused_main_floats(d, T, E) + 15) / 16 * 16 + 4 * 8;   // + 3 mbarriers
+}
+inline int route_fused_max_tokens(int d, int E) {
+    int t = kRouteFusedMaxT;
+    while (t > 0 && (route_fused_smem(d, t, E) > 220 * 1024 ||
+                     route_tail_smem(E, t) > sizeof(float) * (size_t)kRouteEPC * 8 * route_lane_pitch(d)))
+        t--;
+    return E <= kMaxE ? t : 0;
+}
+
+struct RouteFusedParams {
+    RouteParams r;             // r.router unused: rows come from router_lm
+    const float* router_lm;    // [E][8][P] lane-major router rows
+    TopkParams tp;
+    DispatchParams dp;
+};
+
+// order-preserving key of a ranking value: larger value -> larger key, NaN
+// lowest, -0 == +0 (Array.Sort with v[b].CompareTo(v[a]), value descending)
+__device__ __forceinline__ uint32_t rank_key(float v) {
+    if (isnan(v)) return 0u;
+    const uint32_t u = __float_as_uint(__fadd_rn(v, 0.f));   // -0 -> +0
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Top-k of every token and the dispatch of the n = T*k <= 32 assignments.
+// Scores: the whole CTA (softmax: StreamingEngine.cs:642-647 with the
+// sequential sum; GLM sigmoid + bias: 730-767).  Selection: one warp per token,
+// k rounds of "largest key, lowest index" over registers.  Dispatch, computed
+// directly: offsets[e] = #assignments with expert < e, pos(a) = offsets[e_a] +
+// #{b < a : e_b == e_a} (stable), active = local experts with assignments,
+// ascending.
+// scratch: sv / key / asg / wred (may alias consumed data); bias: E floats of
+// tp.bias staged in shared memory (or null); tab: the exp table in shared memory
+template <int J>
+__device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_t* scratch, const float* bias,
+                           const uint64_t* tab) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int NW = kRouteThreads / 32;
+    const int E = p.E, T = tp.T, k = tp.k, n = T * k;
+    float* sv = reinterpret_cast<float*>(scratch);                       // [T][E] weight sources
+    uint32_t* key = reinterpret_cast<uint32_t*>(sv + (size_t)T * E);     // [T][E] ranking keys
+    int* asg = reinterpret_cast<int*>(key + (size_t)T * E);              // [32] expert of assignment a
+    float* wred = reinterpret_cast<float*>(asg + 32);                    // [T][NW] max / sum scratch
+    if (!tp.sigmoid) {
+        // max from float.MinValue (comparisons skip NaN like the reference loop)
+        for (int t = 0; t < T; t++) {
+            float mx = -3.40282347e+38f;
+            for (int i = tid; i < E; i += kRouteThreads) {
+                const float a = __ldcg(tp.logits + (size_t)t * E + i);
+                sv[t * E + i] = a;
+                if (a > mx) mx = a;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) { const float b = __shfl_xor_sync(0xffffffffu, mx, o); if (b > mx) mx = b; }
+            if (lane == 0) wred[t * NW + warp] = mx;
+        }
+        __syncthreads();
+        for (int t = 0; t < T; t++) {
+            float mx = wred[t * NW];
+#pragma unroll
+            for (int w = 1; w < NW; w++) if (wred[t * NW + w] > mx) mx = wred[t * NW + w];
+            for (int i = tid; i < E; i += kRouteThreads) sv[t * E + i] = expf_glibc_t(__fsub_rn(sv[t * E + i], mx), tab);
+        }
+        __syncthreads();
+        if (tid < T) {   // sequential sum in index order
+            const float* e = sv + tid * E;
+            float sum = 0.f;
+            int i = 0;
+            for (; i + 16 <= E; i += 16) {
+                float q[16];
+#pragma unroll
+                for (int u = 0; u < 16; u++) q[u] = e[i + u];
+#pragma unroll
+                for (int u = 0; u < 16; u++) sum = __fadd_rn(sum, q[u]);
+            }
+            for (; i < E; i++) sum = __fadd_rn(sum, e[i]);
+            wred[tid * NW] = __fdiv_rn(1.f, sum);
+        }
+        __syncthreads();
+        for (int i = tid; i < T * E; i += kRouteThreads) {
+            const float q = __fmul_rn(sv[i], wred[(i / E) * NW]);
+            sv[i] = q;
+            key[i] = rank_key(q);
+        }
+    } else {
+        for (int i = tid; i < T * E; i += kRouteThreads) {
+            const int e = i - (i / E) * E;
+            const float sg = __fdiv_rn(1.f, __fadd_rn(1.f, expf_glibc_t(-__ldcg(tp.logits + i), tab)));
+            sv[i] = sg;
+            key[i] = rank_key(bias ? __fadd_rn(sg, bias[e]) : sg);
+        }
+    }
+    __syncthreads();
+    if (warp < T) {
+        const int t = warp;
+        uint32_t kr[J];
+#pragma unroll
+        for (int jj = 0; jj < J; jj++) kr[jj] = lane + 32 * jj < E ? key[t * E + lane + 32 * jj] : 0u;
+        uint32_t taken = 0;
+        int sel[kMaxK];
+        float ssel[kMaxK];
+#pragma unroll
+        for (int r = 0; r < kMaxK; r++) {
+            if (r < k) {
+                uint32_t bk = 0;
+                int bj = -1;
+#pragma unroll
+                for (int jj = 0; jj < J; jj++) {
+                    const bool ok = lane + 32 * jj < E && !(taken & (1u << jj));
+                    if (ok && (bj < 0 || kr[jj] > bk)) { bk = kr[jj]; bj = jj; }
+                }
+                const uint32_t m = __reduce_max_sync(0xffffffffu, bj >= 0 ? bk : 0u);
+                // lanes hold indices lane + 32*jj: the lowest index among the maxima
+                const uint32_t cand = (bj >= 0 && bk == m) ? (uint32_t)(bj * 32 + lane) : 0xffffffffu;
+                const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
+                sel[r] = (int)win;
+                ssel[r] = sv[t * E + (int)win];
+                if ((int)(win & 31) == lane) taken |= 1u << (win >> 5);
+            }
+        }
+        if (lane == 0) {
+            int32_t* oi = tp.topk_idx + (size_t)t * k;
+            float* ow = tp.topk_w + (size_t)t * k;
+            if (!tp.sigmoid) {
+                float sum = 0.f;
+#pragma unroll
+                for (int r = 0; r < kMaxK; r++) if (r < k) sum = __fadd_rn(sum, ssel[r]);
+                if (sum <= 0.f) sum = 1.f;
+#pragma unroll
+                for (int r = 0; r < kMaxK; r++)
+                    if (r < k) { oi[r] = sel[r]; ow[r] = __fdiv_rn(ssel[r], sum); asg[t * k + r] = sel[r]; }
+            } else {
+                float wsum = 0.f;
+#pragma unroll
+                for (int r = 0; r < kMaxK; r++) if (r < k) wsum = __fadd_rn(wsum, ssel[r]);
+                const float inv2 = __fdiv_rn(1.f, __fadd_rn(wsum, 1e-20f));
+#pragma unroll
+                for (int r = 0; r < kMaxK; r++)
+                    if (r < k) {
+                        oi[r] = sel[r];
+                        ow[r] = __fmul_rn(__fmul_rn(ssel[r], inv2), tp.routed_scale);
+                        asg[t * k + r] = sel[r];
+                    }
+            }
+        }
+    }
+    for (int a = n + tid; a < 32; a += kRouteThreads) asg[a] = 0x7fffffff;   // padding sorts last
+    __syncthreads();
+    int av[32];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+        const int4 v = reinterpret_cast<const int4*>(asg)[q];
+        av[4 * q] = v.x; av[4 * q + 1] = v.y; av[4 * q + 2] = v.z; av[4 * q + 3] = v.w;
+    }
+    for (int e = tid; e <= E; e += kRouteThreads) {
+        int c = 0;
+#pragma unroll
+        for (int a = 0; a < 32; a++) c += av[a] < e ? 1 : 0;
+        p.offsets[e] = c;
+    }
+    if (warp == 0) {
+        const int a = lane;
+        const int e = asg[lane];   // 0x7fffffff past n
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const bool first = a < n && lane == __ffs(peers) - 1;
+        const bool local = a < n && e >= p.first_expert && e < p.first_expert + p.n_local;
+        const unsigned firsts = __ballot_sync(0xffffffffu, first && local);
+        int below = 0, dbelow = 0;
+#pragma unroll
+        for (int b = 0; b < 32; b++) {
+            below += av[b] < e ? 1 : 0;
+            dbelow += ((firsts >> b) & 1u) && av[b] < e ? 1 : 0;
+        }
+        if (a < n) {
+            const int pos = below + __popc(peers & ((1u << lane) - 1));   // stable inside an expert
+            p.perm[pos] = a;
+            p.inv_perm[a] = pos;
+            if (first && local) p.active[dbelow] = e;
+        }
+        if (lane == 0) {
+            const int nd = __popc(firsts);
+            if (p.has_shared) p.active[nd] = E;
+            p.sched->n_active = nd;
+            for (int q = 0; q < 4; q++) p.sched->ctr[q] = 0;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kRouteThreads, 1)
+route_fused_kernel(RouteFusedParams fp) {
+    extern __shared__ __align__(16) float smem[];
+    const RouteParams& p = fp.r;
+    const int d = p.d, T = p.T;
+    const int P = route_lane_pitch(d), P8 = 8 * P, m8 = d / 8;   // d % 32 == 0 (host check)
+    const int e0 = blockIdx.x * kRouteEPC;
+    const int ne = min(kRouteEPC, p.E - e0);
+    float* W = smem;                        // [EPC][8][P] lane-major router rows
+    float* X = W + kRouteEPC * P8;          // [T][d] token rows as given
+    float* XP = X + T * d;                  // [T][8][P] normalised rows, lane-major
+    float* NW = XP + T * P8;                // [d]
+    float* red = NW + d;                    // [T*EPC*8]
+    float* scl = red + T * kRouteEPC * 8;   // [T]
+    float* sbias = scl + (T + 3) / 4 * 4;   // [E] (GLM router bias, for the last CTA)
+    uint64_t* stab = reinterpret_cast<uint64_t*>(sbias + (p.E + 3) / 4 * 4);   // [32] exp table
+    uint64_t* bar = reinterpret_cast<uint64_t*>(
+        reinterpret_cast<uint8_t*>(smem) + (sizeof(float) * route_fused_main_floats(d, T, p.E) + 15) / 16 * 16);
+    __shared__ int s_flag;                  // bit 0: a wait gave up; bit 1: last CTA
+    const int tid = threadIdx.x;
+    const int d8 = d / 8 * 8;
+    const bool norm = p.apply_norm != 0;
+    const bool has_nw = norm && p.norm_w != nullptr;
+
+    if (tid == 0) {
+        s_flag = 0;
+        for (int i = 0; i < 3; i++) mbar_init(&bar[i], 1);
+        fence_barrier_init();
+        // token rows, then norm weights, then router rows (16-byte aligned rows)
+        const uint32_t rb = (uint32_t)(sizeof(float) * d);
+        mbar_arrive_expect_tx(&bar[0], rb * T);
+        for (int t = 0; t < T; t++) bulk_g2s(X + t * d, p.x + (size_t)t * d, rb, &bar[0]);
+        if (has_nw) {
+            mbar_arrive_expect_tx(&bar[1], rb);
+            bulk_g2s(NW, p.norm_w, rb, &bar[1]);
+        } else {
+            mbar_arrive(&bar[1]);
+        }
+        const uint32_t wb = (uint32_t)(sizeof(float) * P8);
+        mbar_arrive_expect_tx(&bar[2], wb * ne);
+        for (int e = 0; e < ne; e++) bulk_g2s(W + e * P8, fp.router_lm + (size_t)(e0 + e) * P8, wb, &bar[2]);
+    }
+    // what the last CTA's ranking needs, staged while the chains run
+    if (fp.tp.bias) {
+        for (int i = 4 * tid; i + 4 <= p.E; i += 4 * kRouteThreads) cp_async16(sbias + i, fp.tp.bias + i);
+        if (tid < (p.E & 3)) sbias[(p.E & ~3) + tid] = fp.tp.bias[(p.E & ~3) + tid];
+    }
+    cp_async_commit();
+    const uint64_t tabv = kExpfTabDev[tid & 31];   // stored after the chains (hides the load)
+    __syncthreads();
+    // bounded wait on group g by every thread; a timeout is reported through
+    // the schedule's error flags (qrm_sync returns QRM_E_TIMEOUT)
+    auto wait_group = [&](int g) {
+        if (!mbar_wait(&bar[g], 0u)) atomicOr(&s_flag, 1);
+    };
+
+    // RMSNorm chains, thread (t, j) for t < T, j < 8
+    wait_group(0);
+    // chain group g (token or (token, expert)) -> warp g % 4, lanes 8*(g/4)..+7,
+    // so the groups issue from different schedulers
+    const int cg = (tid >> 5) + 4 * ((tid & 31) >> 3), cj = tid & 7;
+    if (norm && cg < T) red[cg * 8 + cj] = lane_chain(X + cg * d, X + cg * d, cj, d8, 0.f);
+    __syncthreads();
+    if (norm) {
+        if (tid < T) {
+            const float* xr = X + tid * d;
+            float ss = 0.f;
+            int i = 0;
+            if (d >= 8) { ss = hsum8_seq(red + tid * 8); i = d8; }
+            for (; i < d; i++) ss = __fadd_rn(ss, __fmul_rn(xr[i], xr[i]));
+            const float v = __fadd_rn(__fdiv_rn(ss, (float)d), p.eps);
+            scl[tid] = __fdiv_rn(1.f, __fsqrt_rn(v));
+        }
+        wait_group(1);
+    } else {
+        wait_group(1);
+    }
+    __syncthreads();
+    // normalise into the lane-major XP and write this CTA's slice of xn
+    {
+        const int d4 = d / 4;
+        const int c0 = (int)((long long)d4 * blockIdx.x / gridDim.x), c1 = (int)((long long)d4 * (blockIdx.x + 1) / gridDim.x);
+        const float4* nw4 = reinterpret_cast<const float4*>(NW);
+        for (int t = 0; t < T; t++) {
+            const float sc = norm ? scl[t] : 1.f;
+            const float4* xr = reinterpret_cast<const float4*>(X + t * d);
+            float* xp = XP + t * P8;
+            for (int c = tid; c < d4; c += kRouteThreads) {
+                float4 v = xr[c];
+                if (norm) {
+                    v.x = __fmul_rn(v.x, sc); v.y = __fmul_rn(v.y, sc); v.z = __fmul_rn(v.z, sc); v.w = __fmul_rn(v.w, sc);
+                    if (has_nw) {
+                        const float4 w = nw4[c];
+                        v.x = __fmul_rn(v.x, w.x); v.y = __fmul_rn(v.y, w.y); v.z = __fmul_rn(v.z, w.z); v.w = __fmul_rn(v.w, w.w);
+                    }
+                }
+                // columns 4c..4c+3 -> lanes (4c & 7) + i, position (4c) >> 3
+                const int j0 = (4 * c) & 7, m = (4 * c) >> 3;
+                xp[(j0 + 0) * P + m] = v.x;
+                xp[(j0 + 1) * P + m] = v.y;
+                xp[(j0 + 2) * P + m] = v.z;
+                xp[(j0 + 3) * P + m] = v.w;
+                if (c >= c0 && c < c1) reinterpret_cast<float4*>(p.xn + (size_t)t * d)[c] = v;
+            }
+        }
+    }
+    wait_group(2);
+    __syncthreads();
+    // logit chains: thread (t, e, j)
+    {
+        const int lt = cg / kRouteEPC, le = cg - lt * kRouteEPC;
+        if (lt < T && le < ne) red[cg * 8 + cj] = lane_chain4(W + le * P8 + cj * P, XP + lt * P8 + cj * P, m8, 0.f);
+    }
+    __syncthreads();
+    if (tid < T * ne) {
+        const int t = tid / ne, e = tid - t * ne;
+        float s = hsum8_seq(red + (t * kRouteEPC + e) * 8);   // no tail columns: d % 8 == 0
+        if (p.offset) s = __fadd_rn(s, p.offset[e0 + e]);
+        p.logits[(size_t)t * p.E + e0 + e] = s;
+        __threadfence();
+    }
+    // the last CTA to arrive ranks and dispatches
+    if (tid < 32) stab[tid] = tabv;
+    __syncthreads();
+    if (tid == 0) {
+        if (s_flag & 1) atomicOr(&fp.dp.sched->err, (int)ERR_TIMEOUT);
+        __threadfence();
+        if (atomicAdd(&fp.dp.sched->route_arrivals, 1) == (int)gridDim.x - 1) s_flag |= 2;
+    }
+    __syncthreads();
+    if (!(s_flag & 2)) return;
+    __threadfence();
+    cp_async_wait<0>();
+    __syncthreads();
+    const float* bias = fp.tp.bias ? sbias : nullptr;
+    if (p.E <= 256) route_tail<8>(fp.tp, fp.dp, reinterpret_cast<uint8_t*>(smem), bias, stab);
+    else route_tail<kMaxE / 32>(fp.tp, fp.dp, reinterpret_cast<uint8_t*>(smem), bias, stab);
+    if (tid == 0) fp.dp.sched->route_arrivals = 0;
 }
 
 }  // namespace qrm
