@@ -364,10 +364,8 @@ def run_ours(args, rank, world, dist):
             cpu = dict(value=v, unit="tokens/s", cores=cores, kind="port", sample=desc)
         except Exception as ex:  # the baseline must never block the GPU number
             cpu = dict(value=None, unit="tokens/s", cores=None, kind="port", sample=f"failed: {ex}")
-    # route, (top-k for T > 32), dispatch, activation tables (gate/up 1, down 2 with a
-    # shared expert), gate/up and down (routed + shared when their formats differ), combine
-    split = WORKLOAD["shared_fmt"] != WORKLOAD["fmt"]
-    launches_per_step = 2 + (1 if T > 32 else 0) + 3 + (4 if split else 2) + 1
+    # the library counts the kernel launches of its forward (one graph replay)
+    launches_per_step = layer.last_launch_count()
     line = dict(
         metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="weak", vs_baseline=None,

@@ -152,6 +152,10 @@ enum { QRM_STAGE_ROUTE = 0, QRM_STAGE_TOPK, QRM_STAGE_DISPATCH, QRM_STAGE_GATEUP
 int qrm_set_profiling(qrm_layer* layer, int on);
 int qrm_last_profile(qrm_layer* layer, float* ms, double* bytes);
 
+/* Number of this library's kernel launches in the last forward (one CUDA
+ * graph replay).  No counterpart in the reference. */
+int qrm_last_launch_count(qrm_layer* layer, int* count);
+
 /* ---- operator API: DotKernels.MatVecParallel / DotKernels.GEMM on the GPU ----
  * (DotKernels.cs:610-660).  A qrm_matrix holds one [rows x cols] matrix in
  * HBM; qrm_matrix_gemv computes y[t] = W x[t] for T tokens

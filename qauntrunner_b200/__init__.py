@@ -86,6 +86,7 @@ _SIGS = {
     "qrm_last_router": (C.c_int, [P, P, P]),
     "qrm_set_profiling": (C.c_int, [P, C.c_int]),
     "qrm_last_profile": (C.c_int, [P, P, P]),
+    "qrm_last_launch_count": (C.c_int, [P, P]),
     "qrm_matrix_create": (C.c_int, [C.c_int, C.c_int, C.c_int64, C.c_int64, P, C.c_size_t, C.POINTER(P)]),
     "qrm_matrix_destroy": (None, [P]),
     "qrm_matrix_gemv": (C.c_int, [P, P, C.c_int, P, P]),
@@ -232,6 +233,12 @@ class MoeLayer:
         by = np.zeros(STAGE_COUNT, np.float64)
         _check(lib().qrm_last_profile(self._h, _ptr(ms), _ptr(by)))
         return ms, by
+
+    def last_launch_count(self):
+        """Kernel launches of this library in the last forward."""
+        n = C.c_int(0)
+        _check(lib().qrm_last_launch_count(self._h, C.byref(n)))
+        return n.value
 
     def last_router(self, T):
         logits = np.zeros((T, self.desc.n_experts), np.float32)

@@ -334,6 +334,11 @@ struct GemvParams {
     int xtab_stride;
     int xtab_shared_base;
     int xtab_rows;             // table rows written for this launch
+    // when set, the kernel builds resident tables itself from these f32 rows
+    // (rows < xq_split from xq_a, the rest from xq_b) instead of copying xtab
+    const float* xq_a;
+    const float* xq_b;
+    int xq_split;
 };
 
 __device__ __forceinline__ float swiglu(float g, float u, float limit) {

@@ -68,32 +68,48 @@ __host__ __device__ inline int xtab_ss(int K) { return 2 * K + 2 * kXtabLo; }
 __host__ __device__ inline int xtab_bytes(int K) { return xtab_ss(K) + 8 * (K / 32); }
 inline int xtab_stride(int K) { return (xtab_bytes(K) + 15) / 16 * 16; }
 
-// Quantises activation rows into tables (global memory), one warp per
-// 32-element group: q = rint(x / s) with s = amax / 32639, hi = floor((q +
-// 128) / 256) in [-127, 127], lo = q - 256 hi in [-128, 127].
+// Quantises four consecutive 32-element groups of one activation row, one
+// warp: lane l holds elements 4(l%8)..+3 of group 4c + l/8 (v), and writes the
+// table row at `row` (global or shared memory): q = rint(x / s) with s = amax /
+// 32639 per group, hi = floor((q + 128) / 256) in [-127, 127], lo = q - 256 hi
+// in [-128, 127], ss = (s, sum of the group's values).
+__device__ __forceinline__ void xquant_quad(float4 v, int lane, int c, int K, uint8_t* row) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    float sum = (v.x + v.y) + (v.z + v.w);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    const float s = amax > 0.f ? amax * (1.f / 32639.f) : 0.f;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t hw = 0, lw = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        int q = amax > 0.f ? __float2int_rn(vv[i] / s) : 0;
+        q = max(-32639, min(32639, q));
+        const int hi = (q + 128) >> 8;   // arithmetic shift: floor
+        hw |= (uint32_t)(uint8_t)(int8_t)hi << (8 * i);
+        lw |= (uint32_t)(uint8_t)(int8_t)(q - 256 * hi) << (8 * i);
+    }
+    const int g = 4 * c + (lane >> 3), off = 32 * g + 4 * (lane & 7);
+    *reinterpret_cast<uint32_t*>(row + off) = hw;
+    *reinterpret_cast<uint32_t*>(row + xtab_lo(K) + off) = lw;
+    if ((lane & 7) == 0) reinterpret_cast<float2*>(row + xtab_ss(K))[g] = make_float2(s, sum);
+}
+
+// Quantises activation rows into tables (global memory), one warp per four
+// groups (K % 128 == 0).
 __global__ void xquant_kernel(const float* __restrict__ src, int K, int rows, uint8_t* __restrict__ tab,
                               int stride) {
     const int lane = threadIdx.x & 31;
-    const int groups = K / 32;
-    const long long total = (long long)rows * groups;
+    const int quads = K / 128;
+    const long long total = (long long)rows * quads;
     for (long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; w < total;
          w += ((long long)gridDim.x * blockDim.x) >> 5) {
-        const int r = (int)(w / groups), gi = (int)(w - (long long)r * groups);
-        const float v = src[(size_t)r * K + gi * 32 + lane];
-        float amax = fabsf(v), sum = v;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        }
-        const float s = amax > 0.f ? amax * (1.f / 32639.f) : 0.f;
-        int q = amax > 0.f ? __float2int_rn(v / s) : 0;
-        q = max(-32639, min(32639, q));
-        const int hi = (q + 128) >> 8;   // arithmetic shift: floor
-        uint8_t* row = tab + (size_t)r * stride;
-        row[gi * 32 + lane] = (uint8_t)(int8_t)hi;
-        row[xtab_lo(K) + gi * 32 + lane] = (uint8_t)(int8_t)(q - 256 * hi);
-        if (lane == 0) reinterpret_cast<float2*>(row + xtab_ss(K))[gi] = make_float2(s, sum);
+        const int r = (int)(w / quads), c = (int)(w - (long long)r * quads);
+        const float4 v = reinterpret_cast<const float4*>(src + (size_t)r * K)[32 * c + lane];
+        xquant_quad(v, lane, c, K, tab + (size_t)r * stride);
     }
 }
 
@@ -486,7 +502,7 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
         // ---------------- producer: lane 0 resolves the item and waits, the
         // lanes issue the row copies in parallel (one thread alone cannot keep
         // enough small copies in flight)
-        if (lane == 0 && res_bytes > 0) {
+        if (lane == 0 && res_bytes > 0 && !p.xq_a) {
             mbar_arrive_expect_tx(tabbar, (uint32_t)res_bytes);
             bulk_g2s(ism + kImmaDataOff, p.xtab, (uint32_t)res_bytes, tabbar);
         }
@@ -552,7 +568,7 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
                 // the stages this warp filled must land before the CTA exits
                 for (int it = max(0, issued - S); it < issued; it++) mbar_wait(&full[it % S], (uint32_t)(it / S) & 1u);
             }
-            if (res_bytes > 0) mbar_wait(tabbar, 0u);
+            if (res_bytes > 0 && !p.xq_a) mbar_wait(tabbar, 0u);
         }
         return;
     }
@@ -565,7 +581,37 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
 #pragma unroll
     for (int g4 = 0; g4 < 4; g4++) bm[g4] = (gid >> 1) == g4 ? 0xFFFFFFFFu : 0u;
     const uint32_t res_u = smem_u32(ism + kImmaDataOff);
-    if (res_bytes > 0 && !warp_wait(tabbar, 0u, abort_flag, err)) return;
+    if (res_bytes > 0 && p.xq_a) {
+        // quantise the resident tables here from the f32 rows (rows < xq_split
+        // from xq_a, the rest from xq_b) while the first stages stream in; no
+        // consumer leaves before this barrier
+        // one float4 per lane covers four groups; each warp issues up to 8 such
+        // loads before it quantises any, so their latencies overlap
+        const int quads = K / 128, total = cfg.res_rows * quads;
+        for (int base = warp; base < total; base += 8 * CW) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int w = base + u * CW;
+                if (w < total) {
+                    const int r = w / quads, c = w - r * quads;
+                    const float* src = r < p.xq_split ? p.xq_a + (size_t)r * K : p.xq_b + (size_t)(r - p.xq_split) * K;
+                    v[u] = __ldcg(reinterpret_cast<const float4*>(src) + 32 * c + lane);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int w = base + u * CW;
+                if (w < total) {
+                    const int r = w / quads, c = w - r * quads;
+                    xquant_quad(v[u], lane, c, K, ism + kImmaDataOff + r * cfg.xtab_bytes);
+                }
+            }
+        }
+        named_barrier(1, CW * 32);
+    } else if (res_bytes > 0 && !warp_wait(tabbar, 0u, abort_flag, err)) {
+        return;
+    }
     for (int it = 0;; it++) {
         const int s = it % S;
         const uint32_t ph = (uint32_t)(it / S) & 1u;

@@ -181,16 +181,45 @@ int imma_rtiles(bool gateup, int nsb) {
     return nsb >= 16 ? 1 : 2;
 }
 
+// The integer kernel's launch shape for one matrix launch.
+struct ImmaSel {
+    int rtiles = 1, ntk = 1, cw = 0;
+    qrm::ImmaConfig cfg{};
+};
+
+bool imma_format(int fmt) { return fmt == qrm::Q4_K || fmt == qrm::Q8_0 || fmt == qrm::Q4_0; }
+
+// true when the integer kernel may take this matrix shape (tables wanted)
+bool imma_usable(int fmt, int rows, int cols, bool gateup) {
+    if (!imma_format(fmt) || cols % 256) return false;
+    return rows % (gateup ? 8 : 16) == 0;
+}
+
+// Chooses row tiles, tokens per pass, consumer warps and the stage plan;
+// false when the integer kernel does not take the launch.
+bool imma_select(int fmt, bool gateup, int T, const qrm::GemvParams& p, ImmaSel* sel) {
+    if (!p.xtab || !imma_usable(fmt, p.rows, p.cols, gateup)) return false;
+    const int RT = qrm::kImmaRows / (gateup ? 2 : 1);
+    int rtiles = imma_rtiles(gateup, p.cols / 256);
+    while (rtiles > 1 && p.rows % (RT * rtiles)) rtiles >>= 1;
+    if (p.rows % RT) return false;
+    sel->rtiles = rtiles;
+    sel->ntk = T <= 1 ? 1 : 2;
+    sel->cw = imma_kslices(p.cols / 256, rtiles) * rtiles;
+    const int rows = qrm::kImmaRows * rtiles;
+    switch (fmt) {
+        case qrm::Q4_K: return qrm::imma_plan<qrm::Q4_K>(p.cols, rows, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg);
+        case qrm::Q8_0: return qrm::imma_plan<qrm::Q8_0>(p.cols, rows, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg);
+        case qrm::Q4_0: return qrm::imma_plan<qrm::Q4_0>(p.cols, rows, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg);
+        default: return false;
+    }
+}
+
 template <int FMT, int M, int NTK, int RTILES>
-int launch_imma_t(const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s, bool* used) {
+int launch_imma_t(const qrm::GemvParams& p, const ImmaSel& sel, int sm_count, int32_t* err, cudaStream_t s) {
     constexpr int RT = qrm::kImmaRows / M;
-    const int nks = imma_kslices(p.cols / 256, RTILES);
-    const int CW = nks * RTILES;
-    qrm::ImmaConfig cfg;
-    if (!qrm::imma_plan<FMT>(p.cols, qrm::kImmaRows * RTILES, NTK, CW, p.xtab_rows, 227 * 1024, &cfg)) return QRM_OK;
     qrm::GemvParams q = p;
     q.tiles = p.rows / (RT * RTILES);
-    *used = true;
     auto fn = qrm::expert_gemv_imma_kernel<FMT, M, NTK, RTILES>;
     static bool attr_set = false;
     if (!attr_set) {
@@ -198,38 +227,30 @@ int launch_imma_t(const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStre
             return fail(QRM_E_CUDA, "expert kernel attribute");
         attr_set = true;
     }
-    fn<<<sm_count, (CW + 1) * 32, qrm::imma_smem_bytes(cfg), s>>>(q, cfg, err);
+    fn<<<sm_count, (sel.cw + 1) * 32, qrm::imma_smem_bytes(sel.cfg), s>>>(q, sel.cfg, err);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
-}
-
-bool imma_format(int fmt) { return fmt == qrm::Q4_K || fmt == qrm::Q8_0 || fmt == qrm::Q4_0; }
-
-// true when the integer kernel will take this matrix shape
-bool imma_usable(int fmt, int rows, int cols, bool gateup) {
-    if (!imma_format(fmt) || cols % 256) return false;
-    return rows % (gateup ? 8 : 16) == 0;
 }
 
 template <int FMT, int M>
 int launch_imma(int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s, bool* used) {
     *used = false;
-    if (!p.xtab) return QRM_OK;
-    constexpr int RT = qrm::kImmaRows / M;
-    int rtiles = imma_rtiles(M == 2, p.cols / 256);
-    while (rtiles > 1 && p.rows % (RT * rtiles)) rtiles >>= 1;
-    if (p.rows % RT) return QRM_OK;
-    const bool one = T <= 1;
+    ImmaSel sel;
+    if (!imma_select(FMT, M == 2, T, p, &sel)) return QRM_OK;
+    // in-kernel tables only with a resident plan (the caller checked)
+    if (p.xq_a && sel.cfg.res_rows == 0) return fail(QRM_E_STATE, "internal: activation tables were not built");
+    *used = true;
 #define QRM_IMMA_RT(R)                                                                          \
-    if (rtiles == R)                                                                            \
-        return one ? launch_imma_t<FMT, M, 1, R>(p, sm_count, err, s, used)                     \
-                   : launch_imma_t<FMT, M, 2, R>(p, sm_count, err, s, used);
+    if (sel.rtiles == R)                                                                        \
+        return sel.ntk == 1 ? launch_imma_t<FMT, M, 1, R>(p, sel, sm_count, err, s)             \
+                            : launch_imma_t<FMT, M, 2, R>(p, sel, sm_count, err, s);
     QRM_IMMA_RT(1)
     QRM_IMMA_RT(2)
     if constexpr (M == 1) {
         QRM_IMMA_RT(4)
     }
 #undef QRM_IMMA_RT
+    *used = false;
     return QRM_OK;
 }
 
@@ -320,6 +341,7 @@ struct qrm_layer {
     uint8_t* xtab_gu = nullptr;   // activation tables of the gate/up inputs [T]
     uint8_t* xtab_dn = nullptr;   // of the down inputs [T*k routed | T shared]
     int last_T = 0;
+    int last_launches = 0;        // kernel launches of the last forward
     const float* last_xn = nullptr;
     // per-stage timing
     bool profiling = false;
@@ -328,11 +350,11 @@ struct qrm_layer {
     bool last_shared = false;
     // CUDA graphs of the forward, keyed by buffers, T, flags and profiling
     using GraphKey = std::tuple<const void*, const void*, const void*, const void*, int, int, int>;
-    std::map<GraphKey, cudaGraphExec_t> graphs;
+    std::map<GraphKey, std::pair<cudaGraphExec_t, int>> graphs;   // graph, kernel launches in it
 };
 
 static void clear_graphs(qrm_layer* L) {
-    for (auto& kv : L->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto& kv : L->graphs) cudaGraphExecDestroy(kv.second.first);
     L->graphs.clear();
 }
 
@@ -619,6 +641,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const int d = D.d_model, E = D.n_experts, f = D.expert_ffn, k = L->k;
     const bool shared = L->shared_enabled && L->uploaded[(size_t)E * 3];
     const bool prof = L->profiling;
+    int nl = 0;   // kernel launches of this forward
     auto mark = [&](int i) { if (prof) cudaEventRecordWithFlags(L->ev[i], s, cudaEventRecordExternal); };
     mark(0);
     // 1. RMSNorm + router logits, 2. top-k, 3. dispatch
@@ -632,6 +655,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     if (T <= qrm::route_fused_max_tokens(d, E) && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         // one launch: every CTA its experts' logits, the last CTA top-k + dispatch
         const int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
+        nl++;
         qrm::route_fused_kernel<<<grid, qrm::kRouteThreads, qrm::route_fused_smem(d, T, E), s>>>(
             qrm::RouteFusedParams{rp, L->router_lm, tp, dp});
         QRM_CUDA(cudaGetLastError());
@@ -641,14 +665,17 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     } else {
         if (T <= qrm::route_small_max_tokens(d)) {
             int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
+            nl++;
             qrm::route_small_kernel<<<grid, qrm::kRouteThreads, qrm::route_small_smem(d, T), s>>>(rp);
         } else {
             if (flags & QRM_APPLY_NORM) {
+                nl++;
                 qrm::rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, L->norm_w, L->xn, T, d, D.rms_eps);
             } else {
                 xn = x;
             }
             dim3 grid((T + qrm::kLT - 1) / qrm::kLT, (E + qrm::kLE - 1) / qrm::kLE);
+            nl++;
             qrm::logits_tiled_kernel<<<grid, 256, 0, s>>>(xn, L->router, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
         }
         QRM_CUDA(cudaGetLastError());
@@ -656,10 +683,12 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         // top-k and dispatch (fused into one single-CTA kernel for T <= 32)
         const bool fused = T <= qrm::kFusedTopkMaxT;
         if (!fused) {
+            nl++;
             qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
             QRM_CUDA(cudaGetLastError());
         }
         mark(2);
+        nl++;
         qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, T, fused), s>>>(dp, tp, fused ? 1 : 0);
         QRM_CUDA(cudaGetLastError());
         mark(3);
@@ -675,16 +704,6 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         const int frs = gu ? D.fmt_gate : D.fmt_down, fss = gu ? D.fmt_sh_gate : D.fmt_sh_down;
         const int rows_s = gu ? f : d, cols_s = gu ? d : f;
         const bool want_tab = imma_usable(frs, rows_s, cols_s, gu) || (shared && imma_usable(fss, rows_s, cols_s, gu));
-        if (want_tab) {
-            int rc;
-            if (gu) {
-                rc = launch_xquant(xn, d, T, L->xtab_gu, s);
-            } else {
-                rc = launch_xquant(L->h, f, T * k, L->xtab_dn, s);
-                if (!rc && shared) rc = launch_xquant(L->hs, f, T, L->xtab_dn + (size_t)qrm::xtab_stride(f) * T * k, s);
-            }
-            if (rc) return rc;
-        }
         qrm::GemvParams gp{};
         gp.xtab = want_tab ? (gu ? L->xtab_gu : L->xtab_dn) : nullptr;
         gp.xtab_stride = qrm::xtab_stride(cols_s);
@@ -708,6 +727,33 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.limit = limit;
         gp.routed_by_token = gu ? 1 : 0;
         gp.has_shared = shared ? 1 : 0;
+        if (want_tab) {
+            // the kernels quantise resident tables themselves when every
+            // integer-kernel launch of this stage keeps them resident
+            ImmaSel sr, ss;
+            const bool ur = imma_select(frs, gu, T, gp, &sr);
+            const bool us = shared && !same_fmt && imma_select(fss, gu, T, gp, &ss);
+            const bool in_kernel = (ur || us) && (!ur || sr.cfg.res_rows > 0) && (!us || ss.cfg.res_rows > 0);
+            if (in_kernel) {
+                gp.xq_a = gu ? xn : L->h;
+                gp.xq_b = gu ? xn : L->hs;
+                gp.xq_split = gu ? T : T * k;
+            } else {
+                int rc;
+                if (gu) {
+                    rc = launch_xquant(xn, d, T, L->xtab_gu, s);
+                    nl++;
+                } else {
+                    rc = launch_xquant(L->h, f, T * k, L->xtab_dn, s);
+                    nl++;
+                    if (!rc && shared) {
+                        rc = launch_xquant(L->hs, f, T, L->xtab_dn + (size_t)qrm::xtab_stride(f) * T * k, s);
+                        nl++;
+                    }
+                }
+                if (rc) return rc;
+            }
+        }
         const int fr = gu ? D.fmt_gate : D.fmt_down;
         const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
         if (same_fmt) {
@@ -715,6 +761,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
             int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, &L->sched->err, s);
             if (rc) return rc;
+            nl++;
         } else {
             gp.mode = 1;
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
@@ -724,6 +771,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             gp.ctr = &L->sched->ctr[gu ? 1 : 3];
             rc = launch_gemv(fs, gu, nt, gp, L->sm_count, &L->sched->err, s);
             if (rc) return rc;
+            nl += 2;
         }
         mark(gu ? 4 : 5);
     }
@@ -733,9 +781,11 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     long long n4 = (long long)T * (d / 4);
     int cgrid = (int)std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 16);
     qrm::combine_kernel<<<cgrid, 256, 0, s>>>(cp);
+    nl++;
     QRM_CUDA(cudaGetLastError());
     mark(6);
     L->last_T = T;
+    L->last_launches = nl;
     L->profiled_last = prof;
     L->last_shared = shared;
     return QRM_OK;
@@ -762,10 +812,11 @@ static int run_forward(qrm_layer* L, const float* x, int T, int flags, float* ou
         ce = cudaGraphInstantiate(&ex, g, 0);
         cudaGraphDestroy(g);
         if (ce != cudaSuccess) return fail(QRM_E_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
-        it = L->graphs.emplace(key, ex).first;
+        it = L->graphs.emplace(key, std::make_pair(ex, L->last_launches)).first;
     }
-    QRM_CUDA(cudaGraphLaunch(it->second, s));
+    QRM_CUDA(cudaGraphLaunch(it->second.first, s));
     L->last_T = T;
+    L->last_launches = it->second.second;
     L->profiled_last = L->profiling;
     L->last_xn = (T > qrm::route_small_max_tokens(L->desc.d_model) && !(flags & QRM_APPLY_NORM)) ? x : L->xn;
     return QRM_OK;
@@ -819,6 +870,13 @@ extern "C" int qrm_last_dispatch(qrm_layer* L, int32_t* perm, int32_t* offsets) 
     QRM_CUDA(cudaDeviceSynchronize());
     if (perm) QRM_CUDA(cudaMemcpy(perm, L->perm, sizeof(int32_t) * L->last_T * L->k, cudaMemcpyDeviceToHost));
     if (offsets) QRM_CUDA(cudaMemcpy(offsets, L->offsets, sizeof(int32_t) * (L->desc.n_experts + 1), cudaMemcpyDeviceToHost));
+    return QRM_OK;
+}
+
+extern "C" int qrm_last_launch_count(qrm_layer* L, int* count) {
+    if (!L || !count) return fail(QRM_E_INVALID, "NULL argument");
+    if (L->last_T <= 0) return fail(QRM_E_STATE, "no forward has run");
+    *count = L->last_launches;
     return QRM_OK;
 }
 
