@@ -23,6 +23,7 @@ struct CombineParams {
 };
 
 __global__ void combine_kernel(CombineParams p) {
+    pdl_wait();   // the expert outputs of the predecessor
     const int d4 = p.d >> 2;
     const long long total = (long long)p.T * d4;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;

@@ -49,6 +49,13 @@ struct MatDev {
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while its predecessor still runs: pdl_wait() blocks
+// until the predecessor grid has completed and its writes are visible (a no-op
+// for an ordinary launch); pdl_trigger() lets the successor be scheduled.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Device-side error flag bits, read back by qrm_sync().
 enum : uint32_t { ERR_TIMEOUT = 1u, ERR_BOUNDS = 2u, ERR_INTERNAL = 4u };
 

@@ -70,8 +70,8 @@ inline int xtab_stride(int K) { return (xtab_bytes(K) + 15) / 16 * 16; }
 
 // Quantises four consecutive 32-element groups of one activation row, one
 // warp: lane l holds elements 4(l%8)..+3 of group 4c + l/8 (v), and writes the
-// table row at `row` (global or shared memory): q = rint(x / s) with s = amax /
-// 32639 per group, hi = floor((q + 128) / 256) in [-127, 127], lo = q - 256 hi
+// table row at `row` (global or shared memory): q = rint(x * 32639 / amax),
+// s = amax / 32639 per group, hi = floor((q + 128) / 256) in [-127, 127], lo = q - 256 hi
 // in [-128, 127], ss = (s, sum of the group's values).
 __device__ __forceinline__ void xquant_quad(float4 v, int lane, int c, int K, uint8_t* row) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
@@ -82,11 +82,12 @@ __device__ __forceinline__ void xquant_quad(float4 v, int lane, int c, int K, ui
         sum += __shfl_xor_sync(0xffffffffu, sum, o);
     }
     const float s = amax > 0.f ? amax * (1.f / 32639.f) : 0.f;
+    const float inv = amax > 0.f ? 32639.f / amax : 0.f;   // one division per group
     const float vv[4] = {v.x, v.y, v.z, v.w};
     uint32_t hw = 0, lw = 0;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        int q = amax > 0.f ? __float2int_rn(vv[i] / s) : 0;
+        int q = __float2int_rn(vv[i] * inv);
         q = max(-32639, min(32639, q));
         const int hi = (q + 128) >> 8;   // arithmetic shift: floor
         hw |= (uint32_t)(uint8_t)(int8_t)hi << (8 * i);
@@ -146,66 +147,117 @@ template <> struct ImmaFmt<Q4_0> {
 
 constexpr int kImmaRows = 16;                 // MMA rows per row tile
 constexpr int kImmaMaxTok = 2;                // most tokens per pass
-constexpr int kImmaMaxWarps = 16;             // consumer warps
-constexpr int kImmaHdrInts = 8;               // item, slot, e, off, n_tok, arrivals, passes done, pad
+constexpr int kImmaMaxWarps = 16;             // consumer warps (one token per pass)
+constexpr int kImmaMaxWarps2 = 15;            // consumer warps (two tokens per pass)
+constexpr int kImmaMaxSplit = 4;              // K parts of a shared-expert item
+// per-stage header: item, slot, e, off, n_tok, arrivals, passes done, segment,
+// part, tile, table rows of the first two tokens
+constexpr int kImmaHdrInts = 12;
 constexpr int kImmaCtlOff = 8 * (2 * kTmaMaxStages + 1);   // after full[], empty[], the table barrier
 constexpr int kImmaHdrOff = 256;
-constexpr int kImmaDataOff = kImmaHdrOff + kTmaMaxStages * kImmaHdrInts * 4;
+constexpr int kImmaDataOff = (kImmaHdrOff + kTmaMaxStages * kImmaHdrInts * 4 + 127) / 128 * 128;
 static_assert(kImmaCtlOff + 16 <= kImmaHdrOff, "imma control area");
-static_assert(kImmaDataOff % 128 == 0, "imma data alignment");
+
+// bytes of field f of a format per super-block of 256 columns
+__host__ __device__ inline int imma_sb_bytes(int fmt, int f) {
+    switch (fmt) {
+        case Q4_K: return f == 0 ? 144 : 0;
+        case Q8_0: return f == 0 ? 256 : 16;
+        case Q4_0: return f == 0 ? 128 : 16;
+        default: return 0;
+    }
+}
+
+// Stage geometry of one segment of a launch (0: routed experts, 1: the shared
+// expert).  An item of the segment is cut into nsplit parts along K.
+struct ImmaSeg {
+    int nsplit;          // K parts per item (1: whole rows)
+    int pitch[2];        // bytes between rows of field f in a stage
+    int field_off[2];    // offset of field f's row 0 in a stage
+    int row_bytes[2];    // bytes of a whole matrix row of field f
+    int part_bytes[2];   // bytes of field f copied per row for one part
+    int nsbp;            // super-blocks per part
+};
 
 struct ImmaConfig {
     int stages;
     int stage_bytes;     // weights (+ per-item tables) + partial sums
-    int pitch[2];        // bytes between rows of field 0 / field 1
-    int field_off[2];    // offset of field f's row 0 inside a stage
-    int row_bytes[2];    // bytes copied per row of field f
+    ImmaSeg seg[2];
     int xtab_bytes;      // per token table (16-byte multiple)
     int xtab_off;        // per-item tables inside a stage (resident: unused)
-    int res_rows;        // > 0: all table rows resident in shared memory, copied once
+    int res_rows;        // > 0: all table rows resident in shared memory
     int red_off;         // partial sums [warps][NTK][16] floats inside a stage
 };
 
-// rows_per_item = 16 * RTILES; cw consumer warps; tab_rows = table rows the
-// launch reads.  Tables are kept resident when that costs no pipeline depth
-// (at least min(4, per-item stages) stages remain).
-template <int FMT>
-__host__ inline bool imma_plan(int cols, int rows_per_item, int ntok, int cw, int tab_rows, int smem_budget,
-                               ImmaConfig* c) {
-    using F = ImmaFmt<FMT>;
-    if (cols % 256) return false;                 // super-blocks of 256 weights
-    const int bpr = cols / F::kBS;
+// Returns the weight bytes of a stage, -1 when a part of a field is not a
+// multiple of 16 bytes (bulk copies).  Row pitch = 32 or 96 mod 128: the
+// 8-byte fragment loads of a half warp (4 rows x 32 bytes) hit distinct banks.
+__host__ inline int imma_seg_geom(int fmt, int cols, int rows, int nsplit, ImmaSeg* g) {
+    const int nsb = cols / 256;
+    if (nsplit < 1 || nsb % nsplit) return -1;
     int off = 0;
-    c->row_bytes[1] = c->pitch[1] = c->field_off[1] = 0;
-    for (int f = 0; f < F::kFields; f++) {
-        const int rb = bpr * F::len(f);
-        if (rb % 16) return false;
-        c->row_bytes[f] = rb;
-        // pitch = 32 or 96 mod 128: the 8-byte fragment loads of a half warp
-        // (4 rows x 32 bytes) then fall on distinct banks
-        const int m = rb % 128;
-        c->pitch[f] = rb + (m <= 32 ? 32 - m : (m <= 96 ? 96 - m : 160 - m));
-        c->field_off[f] = off;
-        off += rows_per_item * c->pitch[f];
+    g->nsplit = nsplit;
+    g->nsbp = nsb / nsplit;
+    for (int f = 0; f < 2; f++) {
+        const int b = imma_sb_bytes(fmt, f);
+        g->row_bytes[f] = nsb * b;
+        g->part_bytes[f] = nsb / nsplit * b;
+        if (g->part_bytes[f] % 16) return -1;
+        const int m = g->part_bytes[f] % 128;
+        g->pitch[f] = b ? g->part_bytes[f] + (m <= 32 ? 32 - m : (m <= 96 ? 96 - m : 160 - m)) : 0;
+        g->field_off[f] = off;
+        off += rows * g->pitch[f];
     }
-    c->xtab_bytes = xtab_stride(cols);
+    return off;
+}
+
+// fmt[0] / fmt[1]: formats of the routed and the shared segment (-1: none in
+// this launch).  Routed items take whole rows; shared items are split along K
+// until their stage is no larger than the routed one (alone: until two stages
+// fit).  tab_rows = table rows the launch reads.  Tables are kept resident
+// when that costs no pipeline depth (at least min(4, per-item stages) stages);
+// split items need them resident.
+__host__ inline bool imma_plan(const int (&fmt)[2], int cols, int rows_per_item, int ntok, int cw, int tab_rows,
+                               int smem_budget, ImmaConfig* c) {
+    if (cols % 256) return false;
+    const int nsb = cols / 256;
     const int red = cw * ntok * 16 * 4;
     const int avail = smem_budget - kImmaDataOff;
+    int wbytes = 0;
+    c->seg[0] = ImmaSeg{};
+    c->seg[1] = ImmaSeg{};
+    c->seg[0].nsplit = c->seg[1].nsplit = 1;
+    if (fmt[0] >= 0) {
+        wbytes = imma_seg_geom(fmt[0], cols, rows_per_item, 1, &c->seg[0]);
+        if (wbytes < 0) return false;
+    }
+    if (fmt[1] >= 0) {
+        const int target = fmt[0] >= 0 ? wbytes : (avail - red) / 2;
+        int b = -1;
+        for (int sp = 1; sp <= kImmaMaxSplit && b < 0; sp++) {
+            b = imma_seg_geom(fmt[1], cols, rows_per_item, sp, &c->seg[1]);
+            if (b > target) b = -1;
+        }
+        if (b < 0) return false;
+        wbytes = std::max(wbytes, b);
+    }
+    const bool split = c->seg[1].nsplit > 1;
+    c->xtab_bytes = xtab_stride(cols);
     const long long res = (long long)tab_rows * c->xtab_bytes;
-    const int stA = off + red;
-    const int sA = res < avail ? std::min<long long>(kTmaMaxStages, (avail - res) / stA) : 0;
-    const int stB = off + ntok * c->xtab_bytes + red;
+    const int stA = wbytes + red;
+    const int sA = res < avail ? (int)std::min<long long>(kTmaMaxStages, (avail - res) / stA) : 0;
+    const int stB = wbytes + ntok * c->xtab_bytes + red;
     const int sB = std::min(kTmaMaxStages, avail / stB);
-    if (tab_rows > 0 && sA >= 2 && sA >= std::min(sB, 4)) {
+    if (tab_rows > 0 && sA >= 2 && (split || sA >= std::min(sB, 4))) {
         c->res_rows = tab_rows;
         c->xtab_off = 0;
-        c->red_off = off;
+        c->red_off = wbytes;
         c->stage_bytes = stA;
         c->stages = sA;
-    } else if (sB >= 2) {
+    } else if (!split && sB >= 2) {
         c->res_rows = 0;
-        c->xtab_off = off;
-        c->red_off = off + ntok * c->xtab_bytes;
+        c->xtab_off = wbytes;
+        c->red_off = wbytes + ntok * c->xtab_bytes;
         c->stage_bytes = stB;
         c->stages = sB;
     } else {
@@ -308,22 +360,24 @@ template <> struct TabLd<false> {
 };
 
 // ------------------------------------------------------------ one pass
-// Accumulates this warp's K slice [sb0, sb1) of rows gid / gid+8 of its row
-// tile for nt <= NTK tokens whose tables start at tq[q].  y[q][0] = row gid,
+// Accumulates this warp's K slice [sb0, sb1) (super-blocks of the stage) of
+// rows gid / gid+8 of its row tile for nt <= NTK tokens whose tables start at
+// tq[q]; stage super-block sb is table super-block sb + sb_tab.  y[q][0] = row gid,
 // y[q][1] = row gid+8 (this lane's two groups t and t+4 only).  r0 / d0: shared
 // addresses of row gid of field 0 / field 1 (row gid+8 is 8 pitches on).
 template <int FMT, int NTK, bool SM>
 __device__ __forceinline__ void imma_pass(uint32_t r0, uint32_t pitch0, uint32_t d0, uint32_t pitch1,
                                           const typename TabLd<SM>::Ptr (&tq)[NTK], int nt, int K, int sb0,
-                                          int sb1, int lane, const uint32_t (&bm)[4], float (&y)[NTK][2]) {
+                                          int sb1, int sb_tab, int lane, const uint32_t (&bm)[4],
+                                          float (&y)[NTK][2]) {
     using L = TabLd<SM>;
     const int gid = lane >> 2, t = lane & 3, j = gid >> 1, hl = gid & 1;
     // Q4_K: odd groups (high nibbles) keep the nibble in place (code * 16)
     const float kq = (FMT == Q4_K && (t & 1)) ? 4.f : 64.f;
     const uint32_t sel = 0x7044u | ((uint32_t)t << 8);   // byte t -> bits 16..23 of 2.0f
     const uint32_t r1 = r0 + 8 * pitch0, d1 = d0 + 8 * pitch1;
-    const int bofs = hl * xtab_lo(K) + 32 * j + (FMT == Q4_0 ? 4 : 8) * t;   // this lane's B bytes
-    const int sofs = xtab_ss(K) + 8 * t;                                        // its ss entry (group t)
+    const int bofs = hl * xtab_lo(K) + 32 * j + (FMT == Q4_0 ? 4 : 8) * t + 256 * sb_tab;   // this lane's B bytes
+    const int sofs = xtab_ss(K) + 8 * t + 64 * sb_tab;                                        // its ss entry
 #pragma unroll
     for (int q = 0; q < NTK; q++) y[q][0] = y[q][1] = 0.f;
     for (int sb = sb0; sb < sb1; sb++) {
@@ -452,21 +506,222 @@ __device__ __forceinline__ void imma_pass(uint32_t r0, uint32_t pitch0, uint32_t
 }
 
 // ------------------------------------------------------------ kernel
-// Item = (slot, tile) with RTILES row tiles of 16 MMA rows.  gate/up (M = 2):
-// a row tile is 8 rows of gate and the same 8 rows of up (a thread holds gate
-// row g and up row g); down (M = 1): 16 consecutive rows.  CW consumer warps
-// (blockDim/32 - 1): warp w takes row tile w % RTILES and K slice w / RTILES.
-// The producer warp resolves each item (expert, token run), copies its weight
-// rows (and, when the tables are not resident, the first NTK tables) into the
-// stage and writes the item header, S stages ahead of the consumers.
-template <int FMT, int M, int NTK, int RTILES>
-__global__ void __launch_bounds__(32 * (kImmaMaxWarps + 1), 1)
-expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
+// Item = (segment, slot, row tile group, K part).  A row tile group is RTILES
+// row tiles of 16 MMA rows: gate/up (M = 2): 8 rows of gate and the same 8
+// rows of up (a thread holds gate row g and up row g); down (M = 1): 16
+// consecutive rows.  CW consumer warps (blockDim/32 - 1): warp w takes row
+// tile w % RTILES and K slice w / RTILES of the part.  The producer warp
+// resolves each item (expert, token run), copies its weight rows (and, when the
+// tables are not resident, the first NTK tables) into the stage and writes the
+// item header, S stages ahead of the consumers.  Routed items use format FA,
+// the shared expert's items FB.
+
+// Producer: this lane's share of the row copies of one item.
+template <int FMT, int M, int RTILES>
+__device__ __forceinline__ void imma_issue(const GemvParams& p, const ImmaSeg& g, const MatDev* md, int tile,
+                                           int part, uint8_t* st, uint64_t* bar, int lane) {
     using F = ImmaFmt<FMT>;
-    static_assert(NTK >= 1 && NTK <= kImmaMaxTok, "tokens per pass");
-    constexpr int RT = kImmaRows / M;          // matrix rows per row tile
-    constexpr int ROWS = kImmaRows * RTILES;   // stage rows
+    constexpr int RT = kImmaRows / M, ROWS = kImmaRows * RTILES;
+    for (int c = lane; c < ROWS * F::kFields; c += 32) {
+        const int f = c / ROWS, r = c - f * ROWS;
+        const int rt = r / kImmaRows, rr = r % kImmaRows;
+        const MatDev mat = md[M == 2 ? rr / RT : 2];
+        const int row = (tile * RTILES + rt) * RT + (rr % RT);
+        const uint8_t* src = mat.base + mat.nb * F::base_mul(f) + (size_t)row * g.row_bytes[f] + (size_t)part * g.part_bytes[f];
+        bulk_g2s(st + g.field_off[f] + r * g.pitch[f], src, (uint32_t)g.part_bytes[f], bar);
+    }
+}
+
+// Fused combine of one finished down item (one warp): counts the item against
+// its row tile; the last of the tile's n_active + shared items writes
+// out[t][tile columns] = x + w_0 y_0 + ... + w_{k-1} y_{k-1} + ys for every
+// token, each term separately rounded in slot order as combine_kernel does.
+template <int OUTS>
+__device__ __forceinline__ void imma_combine_tile(const GemvParams& p, int tile, int n_active, int lane) {
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&p.tile_ctr[tile], 1) == n_active + (p.has_shared ? 1 : 0) - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    const int d = p.rows;
+    for (int o = lane; o < p.T * OUTS; o += 32) {
+        const int t = o / OUTS, col = tile * OUTS + (o - t * OUTS);
+        float acc = p.cmb_x ? __ldcg(p.cmb_x + (size_t)t * d + col) : 0.f;
+        for (int j = 0; j < p.k; j++) {
+            const float w = __ldcg(p.cmb_w + t * p.k + j);
+            const int pos = __ldcg(p.cmb_inv + t * p.k + j);
+            acc = __fadd_rn(acc, __fmul_rn(w, __ldcg(p.out_routed + (size_t)pos * d + col)));
+        }
+        if (p.has_shared) acc = __fadd_rn(acc, __ldcg(p.out_shared + (size_t)t * d + col));
+        p.cmb_out[(size_t)t * d + col] = acc;
+    }
+    __syncwarp();
+    if (lane == 0) p.tile_ctr[tile] = 0;
+}
+
+// Consumers: one item.  Returns false when a wait gave up (the warp leaves).
+template <int FMT, int M, int NTK, int RTILES>
+__device__ __forceinline__ bool imma_item(const GemvParams& p, const ImmaConfig& cfg, const ImmaSeg g, int* h,
+                                          uint8_t* st, uint8_t* ism, int n_active, int warp, int lane, int NKS,
+                                          int sb0, int sb1, const uint32_t (&bm)[4], volatile int* abort_flag,
+                                          int32_t* err) {
+    constexpr int RT = kImmaRows / M;
     constexpr int OUTS = RTILES * RT;          // outputs per item and token
+    const int CW = NKS * RTILES;
+    const int K = p.cols;
+    const int gid = lane >> 2, t = lane & 3;
+    const int rt = warp % RTILES;
+    const int slot = h[1], off = h[3], n_tok = h[4], part = h[8], tile = h[9];
+    const bool shared = slot >= n_active;
+    const int nsbp = g.nsbp;                                 // super-blocks of this part
+    const uint32_t st_u = smem_u32(st);
+    const uint32_t r0 = st_u + g.field_off[0] + (rt * kImmaRows + gid) * g.pitch[0];
+    const uint32_t d0 = st_u + g.field_off[1] + (rt * kImmaRows + gid) * g.pitch[1];
+    const uint32_t res_u = smem_u32(ism + kImmaDataOff);
+    const int res_bytes = cfg.res_rows * cfg.xtab_bytes;
+    float* red = reinterpret_cast<float*>(st + cfg.red_off);
+    for (int t0 = 0, pass = 0; t0 < n_tok; t0 += NTK, pass++) {
+        const int nt = min(NTK, n_tok - t0);
+        // red is reused by each pass: wait until the previous pass was reduced
+        if (pass > 0 && !warp_spin_eq(&h[6], pass, abort_flag, err)) return false;
+        int trow[NTK];
+#pragma unroll
+        for (int q = 0; q < NTK; q++) {
+            const int tk = t0 + min(q, nt - 1);
+            if (pass == 0) trow[q] = h[10 + min(q, nt - 1)];
+            else if (shared) trow[q] = p.xtab_shared_base + tk;
+            else if (p.routed_by_token) trow[q] = p.pos_tok[off + tk];
+            else trow[q] = off + tk;
+        }
+        float y[NTK][2];
+        if (res_bytes > 0 || pass == 0) {
+            uint32_t tq[NTK];
+#pragma unroll
+            for (int q = 0; q < NTK; q++)
+                tq[q] = res_bytes > 0 ? res_u + trow[q] * cfg.xtab_bytes
+                                      : st_u + cfg.xtab_off + min(q, nt - 1) * cfg.xtab_bytes;
+            imma_pass<FMT, NTK, true>(r0, g.pitch[0], d0, g.pitch[1], tq, nt, K, sb0, sb1, part * nsbp, lane, bm, y);
+        } else {
+            const uint8_t* tq[NTK];
+#pragma unroll
+            for (int q = 0; q < NTK; q++) tq[q] = p.xtab + (size_t)trow[q] * p.xtab_stride;
+            imma_pass<FMT, NTK, false>(r0, g.pitch[0], d0, g.pitch[1], tq, nt, K, sb0, sb1, part * nsbp, lane, bm, y);
+        }
+        // reduce over the 4 lanes of a row, publish the warp's partials
+#pragma unroll
+        for (int q = 0; q < NTK; q++)
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                y[q][hh] += __shfl_xor_sync(0xffffffffu, y[q][hh], 1);
+                y[q][hh] += __shfl_xor_sync(0xffffffffu, y[q][hh], 2);
+            }
+        if (t == 0) {
+#pragma unroll
+            for (int q = 0; q < NTK; q++) {
+                red[(warp * NTK + q) * 16 + gid] = y[q][0];
+                red[(warp * NTK + q) * 16 + gid + 8] = y[q][1];
+            }
+        }
+        __threadfence_block();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&h[5], 1) == CW - 1;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        // every warp's partials are in: add the K slices in a fixed order
+        __threadfence_block();
+        bool split_done = false;
+        if (g.nsplit == 1) {
+            for (int o = lane; o < NTK * OUTS; o += 32) {
+                const int q = o / OUTS, rem = o - q * OUTS;
+                const int rtt = rem / RT, rr = rem - rtt * RT;
+                if (q < nt) {
+                    float v[M];
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        float sum = 0.f;
+                        for (int k2 = 0; k2 < NKS; k2++) sum += red[((k2 * RTILES + rtt) * NTK + q) * 16 + m * RT + rr];
+                        v[m] = sum;
+                    }
+                    const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
+                    const int tk = t0 + q;
+                    float* orow = shared ? p.out_shared + (size_t)tk * p.rows : p.out_routed + (size_t)(off + tk) * p.rows;
+                    orow[(tile * RTILES + rtt) * RT + rr] = res;
+                }
+            }
+        } else {
+            // split item (only the shared expert's items are split; rows = its
+            // tokens): publish this part's sums; the last part of the item adds
+            // the parts in order and finishes the outputs
+            const int R = p.part_rows, grow0 = t0;
+            for (int o = lane; o < NTK * OUTS; o += 32) {
+                const int q = o / OUTS, rem = o - q * OUTS;
+                const int rtt = rem / RT, rr = rem - rtt * RT;
+                if (q < nt) {
+                    const int col = (tile * RTILES + rtt) * RT + rr;
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        float sum = 0.f;
+                        for (int k2 = 0; k2 < NKS; k2++) sum += red[((k2 * RTILES + rtt) * NTK + q) * 16 + m * RT + rr];
+                        p.part_buf[(((size_t)part * R + grow0 + q) * M + m) * p.rows + col] = sum;
+                    }
+                }
+            }
+            __threadfence();
+            __syncwarp();
+            int done = 0;
+            if (lane == 0) done = atomicAdd(&p.part_ctr[grow0 * p.tiles + tile], 1) == g.nsplit - 1;
+            done = __shfl_sync(0xffffffffu, done, 0);
+            split_done = done != 0;
+            if (done) {
+                __threadfence();
+                for (int o = lane; o < NTK * OUTS; o += 32) {
+                    const int q = o / OUTS, rem = o - q * OUTS;
+                    const int rtt = rem / RT, rr = rem - rtt * RT;
+                    if (q < nt) {
+                        const int col = (tile * RTILES + rtt) * RT + rr;
+                        float v[M];
+#pragma unroll
+                        for (int m = 0; m < M; m++) {
+                            float sum = 0.f;
+                            for (int pp = 0; pp < g.nsplit; pp++)
+                                sum += __ldcg(p.part_buf + (((size_t)pp * R + grow0 + q) * M + m) * p.rows + col);
+                            v[m] = sum;
+                        }
+                        const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
+                        const int tk = t0 + q;
+                        float* orow = shared ? p.out_shared + (size_t)tk * p.rows : p.out_routed + (size_t)(off + tk) * p.rows;
+                        orow[col] = res;
+                    }
+                }
+                if (lane == 0) p.part_ctr[grow0 * p.tiles + tile] = 0;
+            }
+        }
+        const bool final_pass = t0 + NTK >= n_tok;
+        if (M == 1 && p.fuse_combine && final_pass && (g.nsplit == 1 || split_done))
+            imma_combine_tile<OUTS>(p, tile, n_active, lane);
+        __syncwarp();
+        if (lane == 0) {
+            h[5] = 0;
+            if (p.fuse_combine) __threadfence();   // this pass's outputs, for the tile's combiner
+            else __threadfence_block();
+            *reinterpret_cast<volatile int*>(&h[6]) = pass + 1;
+        }
+    }
+    return true;
+}
+
+// Registers: a sub-partition holds 16K; with 17 warps one holds 5, so a
+// thread gets 96 registers, with 16 warps 128.  One-token variants run up to
+// 16 consumer warps in 96 registers; two-token variants need more and run at
+// most 15 (kImmaMaxWarps2).
+template <int FA, int FB, int M, int NTK, int RTILES>
+__global__ void __launch_bounds__(32 * ((NTK == 1 ? kImmaMaxWarps : kImmaMaxWarps2) + 1), 1)
+expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
+    static_assert(NTK >= 1 && NTK <= kImmaMaxTok, "tokens per pass");
+    constexpr int ROWS = kImmaRows * RTILES;   // stage rows
     extern __shared__ __align__(128) uint8_t ism[];
     const int S = cfg.stages;
     uint64_t* full = reinterpret_cast<uint64_t*>(ism);
@@ -479,13 +734,7 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int CW = (blockDim.x >> 5) - 1;
-    const int NKS = CW / RTILES;
     const int K = p.cols;
-    const int nsb = K / 256;
-    const int n_active = *p.n_active;
-    const int n_items = p.mode == 2 ? (p.has_shared ? p.tiles : 0)
-                                    : (n_active + (p.mode == 0 && p.has_shared ? 1 : 0)) * p.tiles;
-    const int slot_base = p.mode == 2 ? n_active : 0;
 
     if (tid == 0) {
         for (int s = 0; s < S; s++) {
@@ -497,11 +746,23 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
         fence_barrier_init();
     }
     __syncthreads();
+    // the producer of a down launch may stream weights before the predecessor
+    // (gate/up) has finished; everything else waits for it
+    if (p.pdl == 1 || warp != CW) pdl_wait();
+    pdl_trigger();
+    // the schedule of this launch (written by the router: final before a
+    // down launch starts, so its producer may read it without waiting)
+    const int n_active = *p.n_active;
+    const int ns0 = cfg.seg[0].nsplit, ns1 = cfg.seg[1].nsplit;
+    const int nA = p.mode == 2 ? 0 : n_active * p.tiles * ns0;
+    const int nB = (p.mode == 1 || !p.has_shared) ? 0 : p.tiles * ns1;
+    const int n_items = nA + nB;
 
     if (warp == CW) {
         // ---------------- producer: lane 0 resolves the item and waits, the
         // lanes issue the row copies in parallel (one thread alone cannot keep
         // enough small copies in flight)
+        if (p.pdl == 2 && !p.xq_a) pdl_wait();   // tables written by the predecessor
         if (lane == 0 && res_bytes > 0 && !p.xq_a) {
             mbar_arrive_expect_tx(tabbar, (uint32_t)res_bytes);
             bulk_g2s(ism + kImmaDataOff, p.xtab, (uint32_t)res_bytes, tabbar);
@@ -526,38 +787,50 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
                 }
                 break;
             }
-            const int sl = item / p.tiles, tile = item - sl * p.tiles;
-            const int slot = slot_base + sl;
+            int seg, slot, tile, part;
+            if (item < nA) {
+                seg = 0;
+                slot = item / (p.tiles * ns0);
+                const int r = item - slot * p.tiles * ns0;
+                tile = r / ns0;
+                part = r - tile * ns0;
+            } else {
+                seg = 1;
+                slot = n_active;
+                const int j = item - nA;
+                tile = j / ns1;
+                part = j - tile * ns1;
+            }
+            const ImmaSeg g = seg ? cfg.seg[1] : cfg.seg[0];
             const int e = p.active[slot];
-            const bool shared = slot >= n_active;
+            const bool shared = seg == 1;
             int off = 0, n_tok = p.T;
             if (!shared) { off = p.offsets[e]; n_tok = p.offsets[e + 1] - off; }
             const int ntab = res_bytes > 0 ? 0 : min(NTK, n_tok);
             uint8_t* st = data + (size_t)s * cfg.stage_bytes;
             if (lane == 0) {
                 h[0] = item; h[1] = slot; h[2] = e; h[3] = off; h[4] = n_tok; h[5] = 0; h[6] = 0;
-                const uint32_t bytes = (uint32_t)(ROWS * (cfg.row_bytes[0] + cfg.row_bytes[1]) + ntab * cfg.xtab_bytes);
+                h[7] = seg; h[8] = part; h[9] = tile;
+                // table rows of the first pass's tokens, so consumers need no global load
+#pragma unroll
+                for (int q = 0; q < 2; q++) {
+                    const int tk = min(q, n_tok - 1);
+                    h[10 + q] = shared ? p.xtab_shared_base + tk : (p.routed_by_token ? p.pos_tok[off + tk] : off + tk);
+                }
+                const uint32_t bytes = (uint32_t)(ROWS * (g.part_bytes[0] + g.part_bytes[1]) + ntab * cfg.xtab_bytes);
                 mbar_arrive_expect_tx(&full[s], bytes);
             }
             __syncwarp();
             const MatDev* md = p.mats + (size_t)e * 3;
-            for (int c = lane; c < ROWS * F::kFields + ntab; c += 32) {
-                if (c < ROWS * F::kFields) {
-                    const int f = c / ROWS, r = c - f * ROWS;
-                    const int rt = r / kImmaRows, rr = r % kImmaRows;
-                    const MatDev mat = md[M == 2 ? rr / RT : 2];
-                    const int row = (tile * RTILES + rt) * RT + (rr % RT);
-                    const uint8_t* src = mat.base + mat.nb * F::base_mul(f) + (size_t)row * cfg.row_bytes[f];
-                    bulk_g2s(st + cfg.field_off[f] + r * cfg.pitch[f], src, (uint32_t)cfg.row_bytes[f], &full[s]);
-                } else {
-                    const int q = c - ROWS * F::kFields;
-                    int trow;
-                    if (shared) trow = p.xtab_shared_base + q;
-                    else if (p.routed_by_token) trow = p.perm[off + q] / p.k;
-                    else trow = off + q;
-                    bulk_g2s(st + cfg.xtab_off + q * cfg.xtab_bytes, p.xtab + (size_t)trow * p.xtab_stride,
-                             (uint32_t)cfg.xtab_bytes, &full[s]);
-                }
+            if (seg == 0) imma_issue<FA, M, RTILES>(p, g, md, tile, part, st, &full[s], lane);
+            else imma_issue<FB, M, RTILES>(p, g, md, tile, part, st, &full[s], lane);
+            for (int q = lane; q < ntab; q += 32) {
+                int trow;
+                if (shared) trow = p.xtab_shared_base + q;
+                else if (p.routed_by_token) trow = p.pos_tok[off + q];
+                else trow = off + q;
+                bulk_g2s(st + cfg.xtab_off + q * cfg.xtab_bytes, p.xtab + (size_t)trow * p.xtab_stride,
+                         (uint32_t)cfg.xtab_bytes, &full[s]);
             }
             issued = it + 1;
         }
@@ -574,19 +847,19 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
     }
 
     // ---------------- consumers
-    const int gid = lane >> 2, t = lane & 3;
-    const int rt = warp % RTILES, ks = warp / RTILES;
-    const int sb0 = ks * nsb / NKS, sb1 = (ks + 1) * nsb / NKS;
+    const int gid = lane >> 2;
+    const int NKS = CW / RTILES, ks = warp / RTILES;
+    // this warp's K slice of a part, per segment
+    const int s0a = ks * cfg.seg[0].nsbp / NKS, s0b = (ks + 1) * cfg.seg[0].nsbp / NKS;
+    const int s1a = ks * cfg.seg[1].nsbp / NKS, s1b = (ks + 1) * cfg.seg[1].nsbp / NKS;
     uint32_t bm[4];   // B column pair (2j, 2j+1) of group j: lanes gid = 2j, 2j+1 supply it
 #pragma unroll
     for (int g4 = 0; g4 < 4; g4++) bm[g4] = (gid >> 1) == g4 ? 0xFFFFFFFFu : 0u;
-    const uint32_t res_u = smem_u32(ism + kImmaDataOff);
     if (res_bytes > 0 && p.xq_a) {
         // quantise the resident tables here from the f32 rows (rows < xq_split
         // from xq_a, the rest from xq_b) while the first stages stream in; no
-        // consumer leaves before this barrier
-        // one float4 per lane covers four groups; each warp issues up to 8 such
-        // loads before it quantises any, so their latencies overlap
+        // consumer leaves before this barrier.  One float4 per lane covers four
+        // groups; each warp issues up to 8 such loads before it quantises any.
         const int quads = K / 128, total = cfg.res_rows * quads;
         for (int base = warp; base < total; base += 8 * CW) {
             float4 v[8];
@@ -617,92 +890,12 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
         const uint32_t ph = (uint32_t)(it / S) & 1u;
         if (!warp_wait(&full[s], ph, abort_flag, err)) return;
         int* h = hdr + s * kImmaHdrInts;
-        const int item = h[0];
-        if (item >= n_items) break;
-        const int slot = h[1], off = h[3], n_tok = h[4];
-        const bool shared = slot >= n_active;
-        const int tile = item - (item / p.tiles) * p.tiles;
+        if (h[0] >= n_items) break;
         uint8_t* st = data + (size_t)s * cfg.stage_bytes;
-        const uint32_t st_u = smem_u32(st);
-        const uint32_t r0 = st_u + cfg.field_off[0] + (rt * kImmaRows + gid) * cfg.pitch[0];
-        const uint32_t d0 = st_u + cfg.field_off[1] + (rt * kImmaRows + gid) * cfg.pitch[1];
-        float* red = reinterpret_cast<float*>(st + cfg.red_off);
-        for (int t0 = 0, pass = 0; t0 < n_tok; t0 += NTK, pass++) {
-            const int nt = min(NTK, n_tok - t0);
-            // red is reused by each pass: wait until the previous pass was reduced
-            if (pass > 0 && !warp_spin_eq(&h[6], pass, abort_flag, err)) return;
-            int trow[NTK];
-#pragma unroll
-            for (int q = 0; q < NTK; q++) {
-                const int tk = t0 + min(q, nt - 1);
-                if (shared) trow[q] = p.xtab_shared_base + tk;
-                else if (p.routed_by_token) trow[q] = p.perm[off + tk] / p.k;
-                else trow[q] = off + tk;
-            }
-            float y[NTK][2];
-            if (res_bytes > 0 || pass == 0) {
-                uint32_t tq[NTK];
-#pragma unroll
-                for (int q = 0; q < NTK; q++)
-                    tq[q] = res_bytes > 0 ? res_u + trow[q] * cfg.xtab_bytes
-                                          : st_u + cfg.xtab_off + min(q, nt - 1) * cfg.xtab_bytes;
-                imma_pass<FMT, NTK, true>(r0, cfg.pitch[0], d0, cfg.pitch[1], tq, nt, K, sb0, sb1, lane, bm, y);
-            } else {
-                const uint8_t* tq[NTK];
-#pragma unroll
-                for (int q = 0; q < NTK; q++) tq[q] = p.xtab + (size_t)trow[q] * p.xtab_stride;
-                imma_pass<FMT, NTK, false>(r0, cfg.pitch[0], d0, cfg.pitch[1], tq, nt, K, sb0, sb1, lane, bm, y);
-            }
-            // reduce over the 4 lanes of a row, publish the warp's partials
-#pragma unroll
-            for (int q = 0; q < NTK; q++)
-#pragma unroll
-                for (int hh = 0; hh < 2; hh++) {
-                    y[q][hh] += __shfl_xor_sync(0xffffffffu, y[q][hh], 1);
-                    y[q][hh] += __shfl_xor_sync(0xffffffffu, y[q][hh], 2);
-                }
-            if (t == 0) {
-#pragma unroll
-                for (int q = 0; q < NTK; q++) {
-                    red[(warp * NTK + q) * 16 + gid] = y[q][0];
-                    red[(warp * NTK + q) * 16 + gid + 8] = y[q][1];
-                }
-            }
-            __threadfence_block();
-            __syncwarp();
-            int last = 0;
-            if (lane == 0) last = atomicAdd(&h[5], 1) == CW - 1;
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                // every warp's partials are in: add the K slices in a fixed order
-                __threadfence_block();
-                for (int o = lane; o < NTK * OUTS; o += 32) {
-                    const int q = o / OUTS, rem = o - q * OUTS;
-                    const int rtt = rem / RT, rr = rem - rtt * RT;
-                    if (q < nt) {
-                        float v[M];
-#pragma unroll
-                        for (int m = 0; m < M; m++) {
-                            float sum = 0.f;
-                            for (int k2 = 0; k2 < NKS; k2++)
-                                sum += red[((k2 * RTILES + rtt) * NTK + q) * 16 + m * RT + rr];
-                            v[m] = sum;
-                        }
-                        const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
-                        const int tk = t0 + q;
-                        float* orow = shared ? p.out_shared + (size_t)tk * p.rows
-                                             : p.out_routed + (size_t)(off + tk) * p.rows;
-                        orow[(tile * RTILES + rtt) * RT + rr] = res;
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    h[5] = 0;
-                    __threadfence_block();
-                    *reinterpret_cast<volatile int*>(&h[6]) = pass + 1;
-                }
-            }
-        }
+        const bool ok = h[7] == 0
+            ? imma_item<FA, M, NTK, RTILES>(p, cfg, cfg.seg[0], h, st, ism, n_active, warp, lane, NKS, s0a, s0b, bm, abort_flag, err)
+            : imma_item<FB, M, NTK, RTILES>(p, cfg, cfg.seg[1], h, st, ism, n_active, warp, lane, NKS, s1a, s1b, bm, abort_flag, err);
+        if (!ok) return;
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }

@@ -19,6 +19,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/qrmoe.h"
@@ -155,18 +156,60 @@ int launch_tma(int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cud
 // Integer tensor-core kernel (Q4_K, Q8_0, Q4_0 with 256-multiple rows);
 // needs the activation tables of p.xtab (written by xquant_kernel).
 
+// Programmatic dependent launches between the forward's kernels, as a mask:
+// 1 gate/up, 2 down, 4 combine.  On B200 the expert launches ran slower as
+// dependents (measured 7570 -> 6966 / 7234 tokens/s at C5, T = 1), the
+// combine slightly faster, so only the combine is (QRM_PDL overrides the mask
+// for tuning runs).
+int pdl_default() {
+    const char* e = getenv("QRM_PDL");
+    return e ? atoi(e) : 4;
+}
+
+// The down kernel can combine the expert outputs itself (last item of each
+// row tile); measured slower than the separate combine launch on B200, so
+// only on request: QRM_FUSED_COMBINE=1.
+bool fused_combine_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QRM_FUSED_COMBINE");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
+// Launches kern, as a programmatic dependent of the previous launch on s when
+// pdl is set (the kernel then calls pdl_wait before it reads that launch's
+// outputs).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // K slices per row tile: a divisor of the super-block count close to the
 // warp limit, else the limit itself (uneven slices)
-int imma_kslices(int nsb, int rtiles) {
-    const int lim = std::min(nsb, qrm::kImmaMaxWarps / rtiles);
+int imma_kslices(int nsb, int rtiles, int max_warps) {
+    const int lim = std::min(nsb, max_warps / rtiles);
     int nks = 1;
     for (int d = lim; d >= 1; d--)
         if (nsb % d == 0) { nks = d; break; }
     return 2 * nks <= lim ? lim : nks;
 }
 
-// Row tiles per item.  Default: one for long rows (>= 16 super-blocks), two
-// otherwise.  QRM_IMMA_RTILES="<gate/up>,<down>" overrides it for tuning runs
+// Row tiles per item (preferred; fewer when the stage does not fit).
+// Default: one for long rows (>= 16 super-blocks), else two (gate/up) or four
+// (down), so each consumer warp gets at least two super-blocks per item.  QRM_IMMA_RTILES="<gate/up>,<down>" overrides it for tuning runs
 // (gate/up 1 or 2, down 1, 2 or 4).
 int imma_rtiles(bool gateup, int nsb) {
     static int env[2] = {-1, -1};
@@ -178,7 +221,7 @@ int imma_rtiles(bool gateup, int nsb) {
     }
     const int e = env[gateup ? 0 : 1];
     if (e == 1 || e == 2 || (!gateup && e == 4)) return e;
-    return nsb >= 16 ? 1 : 2;
+    return nsb >= 16 ? 1 : (gateup ? 2 : 4);
 }
 
 // The integer kernel's launch shape for one matrix launch.
@@ -195,55 +238,69 @@ bool imma_usable(int fmt, int rows, int cols, bool gateup) {
     return rows % (gateup ? 8 : 16) == 0;
 }
 
-// Chooses row tiles, tokens per pass, consumer warps and the stage plan;
-// false when the integer kernel does not take the launch.
-bool imma_select(int fmt, bool gateup, int T, const qrm::GemvParams& p, ImmaSel* sel) {
-    if (!p.xtab || !imma_usable(fmt, p.rows, p.cols, gateup)) return false;
+// Chooses row tiles, tokens per pass, consumer warps and the stage plan for
+// a launch whose routed items use format fa and shared items format fb (-1:
+// none); false when the integer kernel does not take the launch.
+bool imma_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, ImmaSel* sel) {
+    if (!p.xtab) return false;
+    if (fa >= 0 && !imma_usable(fa, p.rows, p.cols, gateup)) return false;
+    if (fb >= 0 && !imma_usable(fb, p.rows, p.cols, gateup)) return false;
+    if (fa < 0 && fb < 0) return false;
     const int RT = qrm::kImmaRows / (gateup ? 2 : 1);
-    int rtiles = imma_rtiles(gateup, p.cols / 256);
-    while (rtiles > 1 && p.rows % (RT * rtiles)) rtiles >>= 1;
     if (p.rows % RT) return false;
-    sel->rtiles = rtiles;
     sel->ntk = T <= 1 ? 1 : 2;
-    sel->cw = imma_kslices(p.cols / 256, rtiles) * rtiles;
-    const int rows = qrm::kImmaRows * rtiles;
-    switch (fmt) {
-        case qrm::Q4_K: return qrm::imma_plan<qrm::Q4_K>(p.cols, rows, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg);
-        case qrm::Q8_0: return qrm::imma_plan<qrm::Q8_0>(p.cols, rows, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg);
-        case qrm::Q4_0: return qrm::imma_plan<qrm::Q4_0>(p.cols, rows, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg);
-        default: return false;
+    const int fmts[2] = {fa, fb};
+    for (int rtiles = imma_rtiles(gateup, p.cols / 256); rtiles >= 1; rtiles >>= 1) {
+        if (p.rows % (RT * rtiles)) continue;
+        sel->rtiles = rtiles;
+        sel->cw = imma_kslices(p.cols / 256, rtiles, sel->ntk == 1 ? qrm::kImmaMaxWarps : qrm::kImmaMaxWarps2) * rtiles;
+        if (!qrm::imma_plan(fmts, p.cols, qrm::kImmaRows * rtiles, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg))
+            continue;
+        // split shared items need the per-part buffers
+        if (sel->cfg.seg[1].nsplit == 1 || (p.part_buf && p.part_ctr)) return true;
     }
+    return false;
 }
 
-template <int FMT, int M, int NTK, int RTILES>
+// segment formats of a launch of mode p.mode whose matrices are all format fmt
+void imma_seg_fmts(int fmt, const qrm::GemvParams& p, int* fa, int* fb) {
+    *fa = p.mode == 2 ? -1 : fmt;
+    *fb = (p.mode == 1 || !p.has_shared) ? -1 : fmt;
+}
+
+template <int FA, int FB, int M, int NTK, int RTILES>
 int launch_imma_t(const qrm::GemvParams& p, const ImmaSel& sel, int sm_count, int32_t* err, cudaStream_t s) {
     constexpr int RT = qrm::kImmaRows / M;
     qrm::GemvParams q = p;
     q.tiles = p.rows / (RT * RTILES);
-    auto fn = qrm::expert_gemv_imma_kernel<FMT, M, NTK, RTILES>;
+    auto fn = qrm::expert_gemv_imma_kernel<FA, FB, M, NTK, RTILES>;
     static bool attr_set = false;
     if (!attr_set) {
         if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
             return fail(QRM_E_CUDA, "expert kernel attribute");
         attr_set = true;
     }
-    fn<<<sm_count, (sel.cw + 1) * 32, qrm::imma_smem_bytes(sel.cfg), s>>>(q, sel.cfg, err);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_k(p.pdl != 0, fn, dim3(sm_count), dim3((sel.cw + 1) * 32), qrm::imma_smem_bytes(sel.cfg), s,
+                             q, sel.cfg, err);
+    if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
 }
 
-template <int FMT, int M>
-int launch_imma(int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s, bool* used) {
+// launches the integer kernel for segment formats (FA, FB) when it takes the
+// launch (*used), else leaves it to the other kernels
+template <int FA, int FB, int M>
+int launch_imma(int fa, int fb, int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s,
+                bool* used) {
     *used = false;
     ImmaSel sel;
-    if (!imma_select(FMT, M == 2, T, p, &sel)) return QRM_OK;
+    if (!imma_select(fa, fb, M == 2, T, p, &sel)) return QRM_OK;
     // in-kernel tables only with a resident plan (the caller checked)
     if (p.xq_a && sel.cfg.res_rows == 0) return fail(QRM_E_STATE, "internal: activation tables were not built");
     *used = true;
 #define QRM_IMMA_RT(R)                                                                          \
     if (sel.rtiles == R)                                                                        \
-        return sel.ntk == 1 ? launch_imma_t<FMT, M, 1, R>(p, sel, sm_count, err, s)             \
-                            : launch_imma_t<FMT, M, 2, R>(p, sel, sm_count, err, s);
+        return sel.ntk == 1 ? launch_imma_t<FA, FB, M, 1, R>(p, sel, sm_count, err, s)          \
+                            : launch_imma_t<FA, FB, M, 2, R>(p, sel, sm_count, err, s);
     QRM_IMMA_RT(1)
     QRM_IMMA_RT(2)
     if constexpr (M == 1) {
@@ -252,6 +309,16 @@ int launch_imma(int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cud
 #undef QRM_IMMA_RT
     *used = false;
     return QRM_OK;
+}
+
+// routed items in Q4_K and a Q8_0 shared expert in one launch (mode 0)
+bool imma_pair_supported(int fa, int fb) { return fa == qrm::Q4_K && fb == qrm::Q8_0; }
+int launch_imma_pair(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, int sm_count, int32_t* err,
+                     cudaStream_t s, bool* used) {
+    *used = false;
+    if (!imma_pair_supported(fa, fb)) return QRM_OK;
+    return gateup ? launch_imma<qrm::Q4_K, qrm::Q8_0, 2>(fa, fb, T, p, sm_count, err, s, used)
+                  : launch_imma<qrm::Q4_K, qrm::Q8_0, 1>(fa, fb, T, p, sm_count, err, s, used);
 }
 
 int launch_xquant(const float* src, int K, int rows, uint8_t* tab, cudaStream_t s) {
@@ -276,8 +343,11 @@ int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_c
 #define QRM_GEMV_CASE(F)                                                                        \
     case F:                                                                                     \
         if (F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) {                               \
-            rc = gateup ? launch_imma<(F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) ? F : qrm::Q4_K, 2>(p.T, p, sm_count, err, s, &used) \
-                        : launch_imma<(F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) ? F : qrm::Q4_K, 1>(p.T, p, sm_count, err, s, &used); \
+            constexpr int FI = (F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) ? F : qrm::Q4_K;  \
+            int fa, fb;                                                                         \
+            imma_seg_fmts(F, p, &fa, &fb);                                                      \
+            rc = gateup ? launch_imma<FI, FI, 2>(fa, fb, p.T, p, sm_count, err, s, &used)        \
+                        : launch_imma<FI, FI, 1>(fa, fb, p.T, p, sm_count, err, s, &used);       \
             if (rc || used) return rc;                                                          \
         }                                                                                       \
         if (gateup) {                                                                           \
@@ -335,16 +405,21 @@ struct qrm_layer {
     float *x = nullptr, *xn = nullptr, *logits = nullptr, *topk_w = nullptr;
     float *h = nullptr, *hs = nullptr, *y = nullptr, *ys = nullptr, *out = nullptr;
     int32_t *topk_idx = nullptr, *perm = nullptr, *inv_perm = nullptr, *offsets = nullptr, *active = nullptr;
+    int32_t* pos_tok = nullptr;
     qrm::Schedule* sched = nullptr;
     uint8_t* staging = nullptr;
     size_t staging_bytes = 0;
     uint8_t* xtab_gu = nullptr;   // activation tables of the gate/up inputs [T]
     uint8_t* xtab_dn = nullptr;   // of the down inputs [T*k routed | T shared]
+    float* part_buf = nullptr;    // shared-expert items split along K: per-part sums
+    int32_t* part_ctr = nullptr;  // and their arrival counters
+    int32_t* tile_ctr = nullptr;  // finished down items per row tile (fused combine)
     int last_T = 0;
     int last_launches = 0;        // kernel launches of the last forward
     const float* last_xn = nullptr;
     // per-stage timing
     bool profiling = false;
+    int pdl = pdl_default();      // programmatic dependent launches in the forward graph (mask)
     bool profiled_last = false;
     cudaEvent_t ev[QRM_STAGE_COUNT + 1] = {};
     bool last_shared = false;
@@ -364,7 +439,8 @@ static void free_layer(qrm_layer* L) {
     if (L->stream) cudaStreamSynchronize(L->stream);
     void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_lm, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
-                    L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn};
+                    L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn,
+                    L->part_buf, L->part_ctr, L->pos_tok, L->tile_ctr};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     clear_graphs(L);
@@ -409,6 +485,7 @@ static int alloc_work(qrm_layer* L, int T) {
     QRM_CUDA(cudaMalloc(&L->topk_idx, sizeof(int32_t) * Tk));
     QRM_CUDA(cudaMalloc(&L->perm, sizeof(int32_t) * Tk));
     QRM_CUDA(cudaMalloc(&L->inv_perm, sizeof(int32_t) * Tk));
+    QRM_CUDA(cudaMalloc(&L->pos_tok, sizeof(int32_t) * Tk));
     QRM_CUDA(cudaMalloc(&L->offsets, sizeof(int32_t) * (E + 1)));
     QRM_CUDA(cudaMalloc(&L->active, sizeof(int32_t) * (E + 1)));
     QRM_CUDA(cudaMalloc(&L->sched, sizeof(qrm::Schedule)));
@@ -421,6 +498,15 @@ static int alloc_work(qrm_layer* L, int T) {
     }
     QRM_CUDA(cudaMalloc(&L->xtab_gu, (size_t)qrm::xtab_stride(d) * T));
     QRM_CUDA(cudaMalloc(&L->xtab_dn, (size_t)qrm::xtab_stride(f) * (Tk + T)));
+    QRM_CUDA(cudaMalloc(&L->tile_ctr, sizeof(int32_t) * (d / 16)));
+    QRM_CUDA(cudaMemset(L->tile_ctr, 0, sizeof(int32_t) * (d / 16)));
+    if (L->shared_enabled) {
+        // shared-expert items split along K: sums per part, arrival counters
+        const size_t cols = (size_t)std::max(d, f), tiles = (size_t)std::max(f / 8, d / 16);
+        QRM_CUDA(cudaMalloc(&L->part_buf, sizeof(float) * qrm::kImmaMaxSplit * T * 2 * cols));
+        QRM_CUDA(cudaMalloc(&L->part_ctr, sizeof(int32_t) * T * tiles));
+        QRM_CUDA(cudaMemset(L->part_ctr, 0, sizeof(int32_t) * T * tiles));
+    }
     L->cap_T = T;
     return QRM_OK;
 }
@@ -648,7 +734,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const float* xn = L->xn;
     qrm::TopkParams tp{L->logits, L->has_bias ? L->router_bias : nullptr, topk_idx, topk_w, T, E, k,
                        D.moe_sigmoid ? 1 : 0, D.routed_scale};
-    qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->offsets, L->active, L->sched, T, k, E,
+    qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->pos_tok, L->offsets, L->active, L->sched, T, k, E,
                            L->first_expert, L->n_local, shared ? 1 : 0};
     qrm::RouteParams rp{x, L->norm_w, L->router, L->has_offset ? L->offset : nullptr, L->xn, L->logits, T, d, E,
                         (flags & QRM_APPLY_NORM) ? 1 : 0, D.rms_eps};
@@ -698,6 +784,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const int nt = pick_nt(T);
     const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU
     const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
+    bool combined = false;
     for (int stage = 0; stage < 2; stage++) {
         const bool gu = stage == 0;
         // activation tables for the integer tensor-core kernel
@@ -713,6 +800,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.active = L->active;
         gp.offsets = L->offsets;
         gp.perm = L->perm;
+        gp.pos_tok = L->pos_tok;
         gp.n_active = &L->sched->n_active;
         gp.x_routed = gu ? xn : L->h;
         gp.x_shared = gu ? xn : L->hs;
@@ -727,13 +815,28 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.limit = limit;
         gp.routed_by_token = gu ? 1 : 0;
         gp.has_shared = shared ? 1 : 0;
+        const int fr = gu ? D.fmt_gate : D.fmt_down;
+        const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
+        gp.part_buf = L->part_buf;
+        gp.part_ctr = L->part_ctr;
+        gp.part_rows = T;
+        gp.pdl = (!prof && (L->pdl & (gu ? 1 : 2))) ? (gu ? 1 : 2) : 0;   // profiling events sit between the launches
+        // routed + shared expert in one integer-kernel launch when the pair of
+        // formats has one (shared items split along K to fit the stage)
+        ImmaSel sp;
+        const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && imma_select(fr, fs, gu, T, gp, &sp);
         if (want_tab) {
             // the kernels quantise resident tables themselves when every
             // integer-kernel launch of this stage keeps them resident
-            ImmaSel sr, ss;
-            const bool ur = imma_select(frs, gu, T, gp, &sr);
-            const bool us = shared && !same_fmt && imma_select(fss, gu, T, gp, &ss);
-            const bool in_kernel = (ur || us) && (!ur || sr.cfg.res_rows > 0) && (!us || ss.cfg.res_rows > 0);
+            bool in_kernel;
+            if (pair) {
+                in_kernel = sp.cfg.res_rows > 0;
+            } else {
+                ImmaSel sr, ss;
+                const bool ur = imma_select(fr, same_fmt && shared ? fr : -1, gu, T, gp, &sr);
+                const bool us = shared && !same_fmt && imma_select(-1, fs, gu, T, gp, &ss);
+                in_kernel = (ur || us) && (!ur || sr.cfg.res_rows > 0) && (!us || ss.cfg.res_rows > 0);
+            }
             if (in_kernel) {
                 gp.xq_a = gu ? xn : L->h;
                 gp.xq_b = gu ? xn : L->hs;
@@ -754,9 +857,29 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                 if (rc) return rc;
             }
         }
-        const int fr = gu ? D.fmt_gate : D.fmt_down;
-        const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
-        if (same_fmt) {
+        // down in one integer-kernel launch: the kernel also combines
+        if (!gu) {
+            ImmaSel sd;
+            const bool one = pair || (same_fmt && imma_select(fr, shared ? fr : -1, false, T, gp, &sd));
+            if (one && L->n_local == E && fused_combine_enabled()) {
+                gp.fuse_combine = 1;
+                gp.cmb_x = (flags & QRM_ADD_RESIDUAL) ? x : nullptr;
+                gp.cmb_w = topk_w;
+                gp.cmb_inv = L->inv_perm;
+                gp.cmb_out = out;
+                gp.tile_ctr = L->tile_ctr;
+                combined = true;
+            }
+        }
+        if (pair) {
+            gp.mode = 0;
+            gp.ctr = &L->sched->ctr[gu ? 0 : 2];
+            bool used = false;
+            int rc = launch_imma_pair(fr, fs, gu, T, gp, L->sm_count, &L->sched->err, s, &used);
+            if (rc) return rc;
+            if (!used) return fail(QRM_E_STATE, "internal: the paired expert kernel declined the launch");
+            nl++;
+        } else if (same_fmt) {
             gp.mode = 0;
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
             int rc = launch_gemv(fr, gu, nt, gp, L->sm_count, &L->sched->err, s);
@@ -775,14 +898,15 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         }
         mark(gu ? 4 : 5);
     }
-    // 6. combine
-    qrm::CombineParams cp{(flags & QRM_ADD_RESIDUAL) ? x : nullptr, L->y, shared ? L->ys : nullptr, L->inv_perm,
-                          topk_w, out, T, k, d};
-    long long n4 = (long long)T * (d / 4);
-    int cgrid = (int)std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 16);
-    qrm::combine_kernel<<<cgrid, 256, 0, s>>>(cp);
-    nl++;
-    QRM_CUDA(cudaGetLastError());
+    // 6. combine (unless the down kernel did it)
+    if (!combined) {
+        qrm::CombineParams cp{(flags & QRM_ADD_RESIDUAL) ? x : nullptr, L->y, shared ? L->ys : nullptr, L->inv_perm,
+                              topk_w, out, T, k, d};
+        long long n4 = (long long)T * (d / 4);
+        int cgrid = (int)std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 16);
+        QRM_CUDA(launch_k(!prof && (L->pdl & 4), qrm::combine_kernel, dim3(cgrid), dim3(256), 0, s, cp));
+        nl++;
+    }
     mark(6);
     L->last_T = T;
     L->last_launches = nl;

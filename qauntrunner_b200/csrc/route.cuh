@@ -454,6 +454,7 @@ struct DispatchParams {
     const int32_t* topk_idx;  // [T*k]
     int32_t* perm;            // [T*k]
     int32_t* inv_perm;        // [T*k]
+    int32_t* pos_tok;         // [T*k] token of the assignment at each position
     int32_t* offsets;         // [E+1]
     int32_t* active;          // [E+1] slot -> expert (E = shared)
     Schedule* sched;
@@ -558,6 +559,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
             const int pos = base[e] + before + rank_w;
             p.perm[pos] = a;
             p.inv_perm[a] = pos;
+            p.pos_tok[pos] = a / p.k;
         }
         __syncthreads();
         if (e >= 0 && lane == leader) atomicAdd(&base[e], __popc(peers));
@@ -828,6 +830,7 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
             const int pos = below + __popc(peers & ((1u << lane) - 1));   // stable inside an expert
             p.perm[pos] = a;
             p.inv_perm[a] = pos;
+            p.pos_tok[pos] = a / p.k;
             if (first && local) p.active[dbelow] = e;
         }
         if (lane == 0) {
@@ -863,6 +866,7 @@ route_fused_kernel(RouteFusedParams fp) {
     const bool norm = p.apply_norm != 0;
     const bool has_nw = norm && p.norm_w != nullptr;
 
+    pdl_trigger();   // the expert kernel may be scheduled; it waits for this grid
     if (tid == 0) {
         s_flag = 0;
         for (int i = 0; i < 3; i++) mbar_init(&bar[i], 1);
