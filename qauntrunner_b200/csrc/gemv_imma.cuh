@@ -21,6 +21,7 @@
 // order, and apply SwiGLU.  All waits are bounded.
 #pragma once
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "gemv.cuh"
@@ -168,6 +169,18 @@ __host__ __device__ inline int imma_sb_bytes(int fmt, int f) {
     }
 }
 
+// Whole-row items are copied as one bulk copy per run of consecutive rows
+// into unpadded rows (few large copies keep HBM busier than many padded row
+// copies, at the price of bank conflicts); QRM_IMMA_CONTIG=0 pads every row.
+__host__ inline bool imma_contig() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QRM_IMMA_CONTIG");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
 // Stage geometry of one segment of a launch (0: routed experts, 1: the shared
 // expert).  An item of the segment is cut into nsplit parts along K.
 struct ImmaSeg {
@@ -177,6 +190,7 @@ struct ImmaSeg {
     int row_bytes[2];    // bytes of a whole matrix row of field f
     int part_bytes[2];   // bytes of field f copied per row for one part
     int nsbp;            // super-blocks per part
+    int contig;          // whole rows, unpadded: one bulk copy per run of consecutive rows
 };
 
 struct ImmaConfig {
@@ -192,19 +206,21 @@ struct ImmaConfig {
 // Returns the weight bytes of a stage, -1 when a part of a field is not a
 // multiple of 16 bytes (bulk copies).  Row pitch = 32 or 96 mod 128: the
 // 8-byte fragment loads of a half warp (4 rows x 32 bytes) hit distinct banks.
-__host__ inline int imma_seg_geom(int fmt, int cols, int rows, int nsplit, ImmaSeg* g) {
+__host__ inline int imma_seg_geom(int fmt, int cols, int rows, int nsplit, ImmaSeg* g, bool contig) {
     const int nsb = cols / 256;
     if (nsplit < 1 || nsb % nsplit) return -1;
     int off = 0;
     g->nsplit = nsplit;
     g->nsbp = nsb / nsplit;
+    g->contig = contig && nsplit == 1;
     for (int f = 0; f < 2; f++) {
         const int b = imma_sb_bytes(fmt, f);
         g->row_bytes[f] = nsb * b;
         g->part_bytes[f] = nsb / nsplit * b;
         if (g->part_bytes[f] % 16) return -1;
         const int m = g->part_bytes[f] % 128;
-        g->pitch[f] = b ? g->part_bytes[f] + (m <= 32 ? 32 - m : (m <= 96 ? 96 - m : 160 - m)) : 0;
+        g->pitch[f] = !b ? 0 : g->contig ? g->part_bytes[f]
+                                         : g->part_bytes[f] + (m <= 32 ? 32 - m : (m <= 96 ? 96 - m : 160 - m));
         g->field_off[f] = off;
         off += rows * g->pitch[f];
     }
@@ -228,14 +244,14 @@ __host__ inline bool imma_plan(const int (&fmt)[2], int cols, int rows_per_item,
     c->seg[1] = ImmaSeg{};
     c->seg[0].nsplit = c->seg[1].nsplit = 1;
     if (fmt[0] >= 0) {
-        wbytes = imma_seg_geom(fmt[0], cols, rows_per_item, 1, &c->seg[0]);
+        wbytes = imma_seg_geom(fmt[0], cols, rows_per_item, 1, &c->seg[0], imma_contig());
         if (wbytes < 0) return false;
     }
     if (fmt[1] >= 0) {
         const int target = fmt[0] >= 0 ? wbytes : (avail - red) / 2;
         int b = -1;
         for (int sp = 1; sp <= kImmaMaxSplit && b < 0; sp++) {
-            b = imma_seg_geom(fmt[1], cols, rows_per_item, sp, &c->seg[1]);
+            b = imma_seg_geom(fmt[1], cols, rows_per_item, sp, &c->seg[1], imma_contig());
             if (b > target) b = -1;
         }
         if (b < 0) return false;
@@ -522,6 +538,21 @@ __device__ __forceinline__ void imma_issue(const GemvParams& p, const ImmaSeg& g
                                            int part, uint8_t* st, uint64_t* bar, int lane) {
     using F = ImmaFmt<FMT>;
     constexpr int RT = kImmaRows / M, ROWS = kImmaRows * RTILES;
+    if (g.contig) {
+        // runs: down, all ROWS rows of the matrix; gate/up, per row tile the RT
+        // rows of gate and of up
+        constexpr int RUNS = M == 2 ? 2 * RTILES : 1, RUN = M == 2 ? RT : ROWS;
+        for (int c = lane; c < RUNS * F::kFields; c += 32) {
+            const int f = c / RUNS, run = c - f * RUNS;
+            const int m = M == 2 ? run & 1 : 0, rt = M == 2 ? run >> 1 : 0;
+            const MatDev mat = md[M == 2 ? m : 2];
+            const int row = M == 2 ? (tile * RTILES + rt) * RT : tile * ROWS;
+            const int r = M == 2 ? rt * kImmaRows + m * RT : 0;   // first stage row of the run
+            const uint8_t* src = mat.base + mat.nb * F::base_mul(f) + (size_t)row * g.row_bytes[f];
+            bulk_g2s(st + g.field_off[f] + r * g.pitch[f], src, (uint32_t)(RUN * g.row_bytes[f]), bar);
+        }
+        return;
+    }
     for (int c = lane; c < ROWS * F::kFields; c += 32) {
         const int f = c / ROWS, r = c - f * ROWS;
         const int rt = r / kImmaRows, rr = r % kImmaRows;
