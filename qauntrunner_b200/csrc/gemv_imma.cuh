@@ -151,13 +151,13 @@ constexpr int kImmaMaxTok = 2;                // most tokens per pass
 constexpr int kImmaMaxWarps = 16;             // consumer warps (one token per pass)
 constexpr int kImmaMaxWarps2 = 15;            // consumer warps (two tokens per pass)
 constexpr int kImmaMaxSplit = 4;              // K parts of a shared-expert item
-// per-stage header: item, slot, e, off, n_tok, arrivals, passes done, segment,
-// part, tile, table rows of the first two tokens
+// per-stage header: item, slot, e, off, n_tok, (unused x2), segment, part,
+// tile, table rows of the first two tokens
 constexpr int kImmaHdrInts = 12;
 constexpr int kImmaCtlOff = 8 * (2 * kTmaMaxStages + 1);   // after full[], empty[], the table barrier
 constexpr int kImmaHdrOff = 256;
 constexpr int kImmaDataOff = (kImmaHdrOff + kTmaMaxStages * kImmaHdrInts * 4 + 127) / 128 * 128;
-static_assert(kImmaCtlOff + 16 <= kImmaHdrOff, "imma control area");
+static_assert(kImmaCtlOff + 48 + 48 <= kImmaHdrOff, "imma control area: abort flag, arrivals, tickets, next item");
 
 // bytes of field f of a format per super-block of 256 columns
 __host__ __device__ inline int imma_sb_bytes(int fmt, int f) {
@@ -193,14 +193,16 @@ struct ImmaSeg {
     int contig;          // whole rows, unpadded: one bulk copy per run of consecutive rows
 };
 
+constexpr int kImmaRedSlots = 4;              // reduction slots (items in reduction at once)
+
 struct ImmaConfig {
     int stages;
-    int stage_bytes;     // weights (+ per-item tables) + partial sums
+    int stage_bytes;     // weights (+ per-item tables)
     ImmaSeg seg[2];
     int xtab_bytes;      // per token table (16-byte multiple)
     int xtab_off;        // per-item tables inside a stage (resident: unused)
     int res_rows;        // > 0: all table rows resident in shared memory
-    int red_off;         // partial sums [warps][NTK][16] floats inside a stage
+    int red_bytes;       // one reduction slot: partial sums [warps][NTK][16] floats
 };
 
 // Returns the weight bytes of a stage, -1 when a part of a field is not a
@@ -259,21 +261,21 @@ __host__ inline bool imma_plan(const int (&fmt)[2], int cols, int rows_per_item,
     }
     const bool split = c->seg[1].nsplit > 1;
     c->xtab_bytes = xtab_stride(cols);
+    c->red_bytes = red;
+    const int avail2 = avail - kImmaRedSlots * red;
     const long long res = (long long)tab_rows * c->xtab_bytes;
-    const int stA = wbytes + red;
-    const int sA = res < avail ? (int)std::min<long long>(kTmaMaxStages, (avail - res) / stA) : 0;
-    const int stB = wbytes + ntok * c->xtab_bytes + red;
-    const int sB = std::min(kTmaMaxStages, avail / stB);
+    const int stA = wbytes;
+    const int sA = res < avail2 ? (int)std::min<long long>(kTmaMaxStages, (avail2 - res) / stA) : 0;
+    const int stB = wbytes + ntok * c->xtab_bytes;
+    const int sB = std::min(kTmaMaxStages, avail2 / stB);
     if (tab_rows > 0 && sA >= 2 && (split || sA >= std::min(sB, 4))) {
         c->res_rows = tab_rows;
         c->xtab_off = 0;
-        c->red_off = wbytes;
         c->stage_bytes = stA;
         c->stages = sA;
     } else if (!split && sB >= 2) {
         c->res_rows = 0;
         c->xtab_off = wbytes;
-        c->red_off = wbytes + ntok * c->xtab_bytes;
         c->stage_bytes = stB;
         c->stages = sB;
     } else {
@@ -281,8 +283,10 @@ __host__ inline bool imma_plan(const int (&fmt)[2], int cols, int rows_per_item,
     }
     return true;
 }
+// shared memory: control | resident tables | reduction slots | stages
 inline size_t imma_smem_bytes(const ImmaConfig& c) {
-    return (size_t)kImmaDataOff + (size_t)c.res_rows * c.xtab_bytes + (size_t)c.stages * c.stage_bytes;
+    return (size_t)kImmaDataOff + (size_t)c.res_rows * c.xtab_bytes + (size_t)kImmaRedSlots * c.red_bytes +
+           (size_t)c.stages * c.stage_bytes;
 }
 
 // ------------------------------------------------------------ bounded waits
@@ -592,19 +596,143 @@ __device__ __forceinline__ void imma_combine_tile(const GemvParams& p, int tile,
     if (lane == 0) p.tile_ctr[tile] = 0;
 }
 
-// Consumers: one item.  Returns false when a wait gave up (the warp leaves).
-template <int FMT, int M, int NTK, int RTILES>
-__device__ __forceinline__ bool imma_item(const GemvParams& p, const ImmaConfig& cfg, const ImmaSeg g, int* h,
-                                          uint8_t* st, uint8_t* ism, int n_active, int warp, int lane, int NKS,
-                                          int sb0, int sb1, const uint32_t (&bm)[4], volatile int* abort_flag,
-                                          int32_t* err) {
+// Per-CTA reduction state: kImmaRedSlots slots of partial sums; reduction r
+// of the CTA (items, and passes within an item, in order) uses slot r % slots
+// once the slot's ticket shows the reductions before it are done.
+struct ImmaRed {
+    int* arr;     // [slots] warps arrived with their partials
+    int* tick;    // [slots] reductions completed in the slot
+    float* buf;   // [slots][red floats]
+    int floats;   // floats per slot
+};
+
+// What a reduction needs once the stage and its header are gone.
+struct ImmaRedJob {
+    int r;          // reduction number (slot r % kImmaRedSlots); -1: none
+    int seg, part, tile, off, t0, nt;
+    int shared, final_pass;
+};
+
+// The reduction of job j (all CW warps' partials are in its slot): adds the
+// K slices in a fixed order and writes the outputs (split parts: publishes
+// them, the last part finishes); frees the slot.  Run by one warp.
+template <int M, int NTK, int RTILES>
+__device__ __forceinline__ void imma_reduce(const GemvParams& p, const ImmaConfig& cfg, const ImmaRedJob& j,
+                                            const ImmaRed& R, int n_active, int NKS, int lane) {
     constexpr int RT = kImmaRows / M;
     constexpr int OUTS = RTILES * RT;          // outputs per item and token
+    const int sq = j.r % kImmaRedSlots;
+    const float* red = R.buf + (size_t)sq * R.floats;
+    const int nsplit = j.seg ? cfg.seg[1].nsplit : cfg.seg[0].nsplit;
+    __threadfence_block();
+    bool split_done = false;
+    if (nsplit == 1) {
+        for (int o = lane; o < NTK * OUTS; o += 32) {
+            const int q = o / OUTS, rem = o - q * OUTS;
+            const int rtt = rem / RT, rr = rem - rtt * RT;
+            if (q < j.nt) {
+                float v[M];
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    float sum = 0.f;
+                    for (int k2 = 0; k2 < NKS; k2++) sum += red[((k2 * RTILES + rtt) * NTK + q) * 16 + m * RT + rr];
+                    v[m] = sum;
+                }
+                const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
+                const int tk = j.t0 + q;
+                float* orow = j.shared ? p.out_shared + (size_t)tk * p.rows : p.out_routed + (size_t)(j.off + tk) * p.rows;
+                orow[(j.tile * RTILES + rtt) * RT + rr] = res;
+            }
+        }
+    } else {
+        // split item (only the shared expert's items are split; rows = its
+        // tokens): publish this part's sums; the last part of the item adds
+        // the parts in order and finishes the outputs
+        const int PR = p.part_rows, grow0 = j.t0;
+        for (int o = lane; o < NTK * OUTS; o += 32) {
+            const int q = o / OUTS, rem = o - q * OUTS;
+            const int rtt = rem / RT, rr = rem - rtt * RT;
+            if (q < j.nt) {
+                const int col = (j.tile * RTILES + rtt) * RT + rr;
+#pragma unroll
+                for (int m = 0; m < M; m++) {
+                    float sum = 0.f;
+                    for (int k2 = 0; k2 < NKS; k2++) sum += red[((k2 * RTILES + rtt) * NTK + q) * 16 + m * RT + rr];
+                    p.part_buf[(((size_t)j.part * PR + grow0 + q) * M + m) * p.rows + col] = sum;
+                }
+            }
+        }
+        __threadfence();
+        __syncwarp();
+        int done = 0;
+        if (lane == 0) done = atomicAdd(&p.part_ctr[grow0 * p.tiles + j.tile], 1) == nsplit - 1;
+        done = __shfl_sync(0xffffffffu, done, 0);
+        split_done = done != 0;
+        if (done) {
+            __threadfence();
+            for (int o = lane; o < NTK * OUTS; o += 32) {
+                const int q = o / OUTS, rem = o - q * OUTS;
+                const int rtt = rem / RT, rr = rem - rtt * RT;
+                if (q < j.nt) {
+                    const int col = (j.tile * RTILES + rtt) * RT + rr;
+                    float v[M];
+#pragma unroll
+                    for (int m = 0; m < M; m++) {
+                        float sum = 0.f;
+                        for (int pp = 0; pp < nsplit; pp++)
+                            sum += __ldcg(p.part_buf + (((size_t)pp * PR + grow0 + q) * M + m) * p.rows + col);
+                        v[m] = sum;
+                    }
+                    const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
+                    const int tk = j.t0 + q;
+                    float* orow = j.shared ? p.out_shared + (size_t)tk * p.rows : p.out_routed + (size_t)(j.off + tk) * p.rows;
+                    orow[col] = res;
+                }
+            }
+            if (lane == 0) p.part_ctr[grow0 * p.tiles + j.tile] = 0;
+        }
+    }
+    if (M == 1 && p.fuse_combine && j.final_pass && (nsplit == 1 || split_done))
+        imma_combine_tile<OUTS>(p, j.tile, n_active, lane);
+    else if (p.fuse_combine)
+        __threadfence();   // outputs of an earlier pass, for the tile's combiner
+    __syncwarp();
+    if (lane == 0) {
+        R.arr[sq] = 0;
+        __threadfence_block();
+        *reinterpret_cast<volatile int*>(&R.tick[sq]) = j.r / kImmaRedSlots + 1;
+    }
+}
+
+// Runs this warp's pending reduction once all warps' partials are in (a
+// bounded wait; usually they already are).
+template <int M, int NTK, int RTILES>
+__device__ __forceinline__ bool imma_flush(const GemvParams& p, const ImmaConfig& cfg, ImmaRedJob& pend,
+                                           const ImmaRed& R, int n_active, int NKS, int lane, volatile int* abort_flag,
+                                           int32_t* err) {
+    if (pend.r < 0) return true;
+    if (!warp_spin_eq(&R.arr[pend.r % kImmaRedSlots], NKS * RTILES, abort_flag, err)) return false;
+    imma_reduce<M, NTK, RTILES>(p, cfg, pend, R, n_active, NKS, lane);
+    pend.r = -1;
+    return true;
+}
+
+// Consumers: one item.  The stage is released as soon as this warp's MMAs of
+// the item's last pass are done; the partials go to a reduction slot.
+// Reduction r is run by warp r % CW, one reduction later (pend), so the
+// reductions spread over the warps and no warp falls behind the others.
+// Returns false when a wait gave up (the warp leaves).
+template <int FMT, int M, int NTK, int RTILES>
+__device__ __forceinline__ bool imma_item(const GemvParams& p, const ImmaConfig& cfg, const ImmaSeg g, const int* h,
+                                          uint8_t* st, uint64_t* empty_bar, uint8_t* ism, int n_active, int warp,
+                                          int lane, int NKS, int sb0, int sb1, const uint32_t (&bm)[4], int& rseq,
+                                          ImmaRedJob& pend, const ImmaRed& R, volatile int* abort_flag, int32_t* err) {
     const int CW = NKS * RTILES;
     const int K = p.cols;
     const int gid = lane >> 2, t = lane & 3;
     const int rt = warp % RTILES;
-    const int slot = h[1], off = h[3], n_tok = h[4], part = h[8], tile = h[9];
+    // the header is gone once the stage is released: keep what is needed
+    const int seg = h[7], slot = h[1], off = h[3], n_tok = h[4], part = h[8], tile = h[9], tr0 = h[10], tr1 = h[11];
     const bool shared = slot >= n_active;
     const int nsbp = g.nsbp;                                 // super-blocks of this part
     const uint32_t st_u = smem_u32(st);
@@ -612,22 +740,25 @@ __device__ __forceinline__ bool imma_item(const GemvParams& p, const ImmaConfig&
     const uint32_t d0 = st_u + g.field_off[1] + (rt * kImmaRows + gid) * g.pitch[1];
     const uint32_t res_u = smem_u32(ism + kImmaDataOff);
     const int res_bytes = cfg.res_rows * cfg.xtab_bytes;
-    float* red = reinterpret_cast<float*>(st + cfg.red_off);
-    for (int t0 = 0, pass = 0; t0 < n_tok; t0 += NTK, pass++) {
+    if (n_tok <= 0) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar);
+        return true;
+    }
+    for (int t0 = 0; t0 < n_tok; t0 += NTK) {
         const int nt = min(NTK, n_tok - t0);
-        // red is reused by each pass: wait until the previous pass was reduced
-        if (pass > 0 && !warp_spin_eq(&h[6], pass, abort_flag, err)) return false;
+        const bool final_pass = t0 + NTK >= n_tok;
         int trow[NTK];
 #pragma unroll
         for (int q = 0; q < NTK; q++) {
             const int tk = t0 + min(q, nt - 1);
-            if (pass == 0) trow[q] = h[10 + min(q, nt - 1)];
+            if (t0 == 0) trow[q] = min(q, nt - 1) == 0 ? tr0 : tr1;
             else if (shared) trow[q] = p.xtab_shared_base + tk;
             else if (p.routed_by_token) trow[q] = p.pos_tok[off + tk];
             else trow[q] = off + tk;
         }
         float y[NTK][2];
-        if (res_bytes > 0 || pass == 0) {
+        if (res_bytes > 0 || t0 == 0) {
             uint32_t tq[NTK];
 #pragma unroll
             for (int q = 0; q < NTK; q++)
@@ -640,6 +771,10 @@ __device__ __forceinline__ bool imma_item(const GemvParams& p, const ImmaConfig&
             for (int q = 0; q < NTK; q++) tq[q] = p.xtab + (size_t)trow[q] * p.xtab_stride;
             imma_pass<FMT, NTK, false>(r0, g.pitch[0], d0, g.pitch[1], tq, nt, K, sb0, sb1, part * nsbp, lane, bm, y);
         }
+        if (final_pass) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty_bar);   // this warp is done with the stage
+        }
         // reduce over the 4 lanes of a row, publish the warp's partials
 #pragma unroll
         for (int q = 0; q < NTK; q++)
@@ -648,6 +783,10 @@ __device__ __forceinline__ bool imma_item(const GemvParams& p, const ImmaConfig&
                 y[q][hh] += __shfl_xor_sync(0xffffffffu, y[q][hh], 1);
                 y[q][hh] += __shfl_xor_sync(0xffffffffu, y[q][hh], 2);
             }
+        const int r = rseq++;
+        const int sq = r % kImmaRedSlots, ticket = r / kImmaRedSlots;
+        if (!warp_spin_eq(&R.tick[sq], ticket, abort_flag, err)) return false;
+        float* red = R.buf + (size_t)sq * R.floats;
         if (t == 0) {
 #pragma unroll
             for (int q = 0; q < NTK; q++) {
@@ -657,89 +796,10 @@ __device__ __forceinline__ bool imma_item(const GemvParams& p, const ImmaConfig&
         }
         __threadfence_block();
         __syncwarp();
-        int last = 0;
-        if (lane == 0) last = atomicAdd(&h[5], 1) == CW - 1;
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (!last) continue;
-        // every warp's partials are in: add the K slices in a fixed order
-        __threadfence_block();
-        bool split_done = false;
-        if (g.nsplit == 1) {
-            for (int o = lane; o < NTK * OUTS; o += 32) {
-                const int q = o / OUTS, rem = o - q * OUTS;
-                const int rtt = rem / RT, rr = rem - rtt * RT;
-                if (q < nt) {
-                    float v[M];
-#pragma unroll
-                    for (int m = 0; m < M; m++) {
-                        float sum = 0.f;
-                        for (int k2 = 0; k2 < NKS; k2++) sum += red[((k2 * RTILES + rtt) * NTK + q) * 16 + m * RT + rr];
-                        v[m] = sum;
-                    }
-                    const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
-                    const int tk = t0 + q;
-                    float* orow = shared ? p.out_shared + (size_t)tk * p.rows : p.out_routed + (size_t)(off + tk) * p.rows;
-                    orow[(tile * RTILES + rtt) * RT + rr] = res;
-                }
-            }
-        } else {
-            // split item (only the shared expert's items are split; rows = its
-            // tokens): publish this part's sums; the last part of the item adds
-            // the parts in order and finishes the outputs
-            const int R = p.part_rows, grow0 = t0;
-            for (int o = lane; o < NTK * OUTS; o += 32) {
-                const int q = o / OUTS, rem = o - q * OUTS;
-                const int rtt = rem / RT, rr = rem - rtt * RT;
-                if (q < nt) {
-                    const int col = (tile * RTILES + rtt) * RT + rr;
-#pragma unroll
-                    for (int m = 0; m < M; m++) {
-                        float sum = 0.f;
-                        for (int k2 = 0; k2 < NKS; k2++) sum += red[((k2 * RTILES + rtt) * NTK + q) * 16 + m * RT + rr];
-                        p.part_buf[(((size_t)part * R + grow0 + q) * M + m) * p.rows + col] = sum;
-                    }
-                }
-            }
-            __threadfence();
-            __syncwarp();
-            int done = 0;
-            if (lane == 0) done = atomicAdd(&p.part_ctr[grow0 * p.tiles + tile], 1) == g.nsplit - 1;
-            done = __shfl_sync(0xffffffffu, done, 0);
-            split_done = done != 0;
-            if (done) {
-                __threadfence();
-                for (int o = lane; o < NTK * OUTS; o += 32) {
-                    const int q = o / OUTS, rem = o - q * OUTS;
-                    const int rtt = rem / RT, rr = rem - rtt * RT;
-                    if (q < nt) {
-                        const int col = (tile * RTILES + rtt) * RT + rr;
-                        float v[M];
-#pragma unroll
-                        for (int m = 0; m < M; m++) {
-                            float sum = 0.f;
-                            for (int pp = 0; pp < g.nsplit; pp++)
-                                sum += __ldcg(p.part_buf + (((size_t)pp * R + grow0 + q) * M + m) * p.rows + col);
-                            v[m] = sum;
-                        }
-                        const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
-                        const int tk = t0 + q;
-                        float* orow = shared ? p.out_shared + (size_t)tk * p.rows : p.out_routed + (size_t)(off + tk) * p.rows;
-                        orow[col] = res;
-                    }
-                }
-                if (lane == 0) p.part_ctr[grow0 * p.tiles + tile] = 0;
-            }
-        }
-        const bool final_pass = t0 + NTK >= n_tok;
-        if (M == 1 && p.fuse_combine && final_pass && (g.nsplit == 1 || split_done))
-            imma_combine_tile<OUTS>(p, tile, n_active, lane);
-        __syncwarp();
-        if (lane == 0) {
-            h[5] = 0;
-            if (p.fuse_combine) __threadfence();   // this pass's outputs, for the tile's combiner
-            else __threadfence_block();
-            *reinterpret_cast<volatile int*>(&h[6]) = pass + 1;
-        }
+        if (lane == 0) atomicAdd(&R.arr[sq], 1);
+        // the previous reduction of this warp, then this one becomes pending
+        if (!imma_flush<M, NTK, RTILES>(p, cfg, pend, R, n_active, NKS, lane, abort_flag, err)) return false;
+        if (r % CW == warp) pend = ImmaRedJob{r, seg, part, tile, off, t0, nt, shared ? 1 : 0, final_pass ? 1 : 0};
     }
     return true;
 }
@@ -758,10 +818,12 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
     uint64_t* full = reinterpret_cast<uint64_t*>(ism);
     uint64_t* empty = full + kTmaMaxStages;
     uint64_t* tabbar = empty + kTmaMaxStages;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(ism + kImmaCtlOff);
+    int* ctl = reinterpret_cast<int*>(ism + kImmaCtlOff);
+    volatile int* abort_flag = ctl;
     int* hdr = reinterpret_cast<int*>(ism + kImmaHdrOff);     // [stage][kImmaHdrInts]
     const int res_bytes = cfg.res_rows * cfg.xtab_bytes;
-    uint8_t* data = ism + kImmaDataOff + res_bytes;
+    const ImmaRed R{ctl + 4, ctl + 8, reinterpret_cast<float*>(ism + kImmaDataOff + res_bytes), cfg.red_bytes / 4};
+    uint8_t* data = ism + kImmaDataOff + res_bytes + kImmaRedSlots * cfg.red_bytes;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int CW = (blockDim.x >> 5) - 1;
@@ -774,6 +836,7 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
         }
         mbar_init(tabbar, 1);
         *abort_flag = 0;
+        for (int q = 0; q < kImmaRedSlots; q++) R.arr[q] = R.tick[q] = 0;
         fence_barrier_init();
     }
     __syncthreads();
@@ -790,14 +853,44 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
     const int n_items = nA + nB;
 
     if (warp == CW) {
-        // ---------------- producer: lane 0 resolves the item and waits, the
-        // lanes issue the row copies in parallel (one thread alone cannot keep
-        // enough small copies in flight)
+        // ---------------- producer: every lane resolves the next item (expert,
+        // token run, table rows) while the current stage's copies fly; lane 0
+        // waits for free stages; the lanes issue the copies in parallel
         if (p.pdl == 2 && !p.xq_a) pdl_wait();   // tables written by the predecessor
         if (lane == 0 && res_bytes > 0 && !p.xq_a) {
             mbar_arrive_expect_tx(tabbar, (uint32_t)res_bytes);
             bulk_g2s(ism + kImmaDataOff, p.xtab, (uint32_t)res_bytes, tabbar);
         }
+        // the look-ahead item lives in shared memory (control area), not in
+        // registers that the consumers' code would have to give up
+        struct Item { int seg, slot, tile, part, e, off, n_tok, tr0, tr1; };
+        Item* nxt = reinterpret_cast<Item*>(ism + kImmaCtlOff + 48);
+        auto resolve = [&](int item, Item& in) {
+            if (item < nA) {
+                in.seg = 0;
+                in.slot = item / (p.tiles * ns0);
+                const int r = item - in.slot * p.tiles * ns0;
+                in.tile = r / ns0;
+                in.part = r - in.tile * ns0;
+            } else {
+                in.seg = 1;
+                in.slot = n_active;
+                const int j = item - nA;
+                in.tile = j / ns1;
+                in.part = j - in.tile * ns1;
+            }
+            in.e = p.active[in.slot];
+            in.off = 0;
+            in.n_tok = p.T;
+            if (in.seg == 0) { in.off = p.offsets[in.e]; in.n_tok = p.offsets[in.e + 1] - in.off; }
+            // table rows of the first pass's tokens, so consumers need no global load
+            const int t1 = min(1, in.n_tok - 1);
+            if (in.seg == 1) { in.tr0 = p.xtab_shared_base; in.tr1 = p.xtab_shared_base + t1; }
+            else if (p.routed_by_token) { in.tr0 = p.pos_tok[in.off]; in.tr1 = p.pos_tok[in.off + t1]; }
+            else { in.tr0 = in.off; in.tr1 = in.off + t1; }
+        };
+        if (lane == 0 && (int)blockIdx.x < n_items) resolve(blockIdx.x, *nxt);
+        __syncwarp();
         bool ok = true;
         int issued = 0;
         for (int it = 0;; it++) {
@@ -812,58 +905,36 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
             if (item >= n_items) {
                 if (lane == 0) {
                     h[0] = item;
-                    h[5] = 0;
-                    h[6] = 0;
                     mbar_arrive(&full[s]);
                 }
                 break;
             }
-            int seg, slot, tile, part;
-            if (item < nA) {
-                seg = 0;
-                slot = item / (p.tiles * ns0);
-                const int r = item - slot * p.tiles * ns0;
-                tile = r / ns0;
-                part = r - tile * ns0;
-            } else {
-                seg = 1;
-                slot = n_active;
-                const int j = item - nA;
-                tile = j / ns1;
-                part = j - tile * ns1;
-            }
-            const ImmaSeg g = seg ? cfg.seg[1] : cfg.seg[0];
-            const int e = p.active[slot];
-            const bool shared = seg == 1;
-            int off = 0, n_tok = p.T;
-            if (!shared) { off = p.offsets[e]; n_tok = p.offsets[e + 1] - off; }
-            const int ntab = res_bytes > 0 ? 0 : min(NTK, n_tok);
+            const Item cur = *nxt;
+            __syncwarp();
+            const ImmaSeg g = cur.seg ? cfg.seg[1] : cfg.seg[0];
+            const int ntab = res_bytes > 0 ? 0 : min(NTK, cur.n_tok);
             uint8_t* st = data + (size_t)s * cfg.stage_bytes;
             if (lane == 0) {
-                h[0] = item; h[1] = slot; h[2] = e; h[3] = off; h[4] = n_tok; h[5] = 0; h[6] = 0;
-                h[7] = seg; h[8] = part; h[9] = tile;
-                // table rows of the first pass's tokens, so consumers need no global load
-#pragma unroll
-                for (int q = 0; q < 2; q++) {
-                    const int tk = min(q, n_tok - 1);
-                    h[10 + q] = shared ? p.xtab_shared_base + tk : (p.routed_by_token ? p.pos_tok[off + tk] : off + tk);
-                }
+                h[0] = item; h[1] = cur.slot; h[2] = cur.e; h[3] = cur.off; h[4] = cur.n_tok;
+                h[7] = cur.seg; h[8] = cur.part; h[9] = cur.tile; h[10] = cur.tr0; h[11] = cur.tr1;
                 const uint32_t bytes = (uint32_t)(ROWS * (g.part_bytes[0] + g.part_bytes[1]) + ntab * cfg.xtab_bytes);
                 mbar_arrive_expect_tx(&full[s], bytes);
             }
             __syncwarp();
-            const MatDev* md = p.mats + (size_t)e * 3;
-            if (seg == 0) imma_issue<FA, M, RTILES>(p, g, md, tile, part, st, &full[s], lane);
-            else imma_issue<FB, M, RTILES>(p, g, md, tile, part, st, &full[s], lane);
+            const MatDev* md = p.mats + (size_t)cur.e * 3;
+            if (cur.seg == 0) imma_issue<FA, M, RTILES>(p, g, md, cur.tile, cur.part, st, &full[s], lane);
+            else imma_issue<FB, M, RTILES>(p, g, md, cur.tile, cur.part, st, &full[s], lane);
             for (int q = lane; q < ntab; q += 32) {
                 int trow;
-                if (shared) trow = p.xtab_shared_base + q;
-                else if (p.routed_by_token) trow = p.pos_tok[off + q];
-                else trow = off + q;
+                if (cur.seg == 1) trow = p.xtab_shared_base + q;
+                else if (p.routed_by_token) trow = p.pos_tok[cur.off + q];
+                else trow = cur.off + q;
                 bulk_g2s(st + cfg.xtab_off + q * cfg.xtab_bytes, p.xtab + (size_t)trow * p.xtab_stride,
                          (uint32_t)cfg.xtab_bytes, &full[s]);
             }
             issued = it + 1;
+            if (lane == 0 && item + (int)gridDim.x < n_items) resolve(item + gridDim.x, *nxt);
+            __syncwarp();
         }
         if (lane == 0) {
             if (!ok) {
@@ -916,20 +987,24 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
     } else if (res_bytes > 0 && !warp_wait(tabbar, 0u, abort_flag, err)) {
         return;
     }
+    int rseq = 0;   // reductions this warp has taken part in (the same for every warp)
+    ImmaRedJob pend;
+    pend.r = -1;
     for (int it = 0;; it++) {
         const int s = it % S;
         const uint32_t ph = (uint32_t)(it / S) & 1u;
         if (!warp_wait(&full[s], ph, abort_flag, err)) return;
-        int* h = hdr + s * kImmaHdrInts;
+        const int* h = hdr + s * kImmaHdrInts;
         if (h[0] >= n_items) break;
         uint8_t* st = data + (size_t)s * cfg.stage_bytes;
         const bool ok = h[7] == 0
-            ? imma_item<FA, M, NTK, RTILES>(p, cfg, cfg.seg[0], h, st, ism, n_active, warp, lane, NKS, s0a, s0b, bm, abort_flag, err)
-            : imma_item<FB, M, NTK, RTILES>(p, cfg, cfg.seg[1], h, st, ism, n_active, warp, lane, NKS, s1a, s1b, bm, abort_flag, err);
+            ? imma_item<FA, M, NTK, RTILES>(p, cfg, cfg.seg[0], h, st, &empty[s], ism, n_active, warp, lane, NKS, s0a, s0b, bm,
+                                            rseq, pend, R, abort_flag, err)
+            : imma_item<FB, M, NTK, RTILES>(p, cfg, cfg.seg[1], h, st, &empty[s], ism, n_active, warp, lane, NKS, s1a, s1b, bm,
+                                            rseq, pend, R, abort_flag, err);
         if (!ok) return;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
     }
+    imma_flush<M, NTK, RTILES>(p, cfg, pend, R, n_active, NKS, lane, abort_flag, err);
 }
 
 }  // namespace qrm

@@ -199,8 +199,17 @@ cudaError_t launch_k(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, si
 
 // K slices per row tile: a divisor of the super-block count close to the
 // warp limit, else the limit itself (uneven slices)
-int imma_kslices(int nsb, int rtiles, int max_warps) {
-    const int lim = std::min(nsb, max_warps / rtiles);
+int imma_kslices(int nsb, int rtiles, int max_warps, bool gateup) {
+    // tuning runs: QRM_IMMA_NKS="<gate/up>,<down>" caps the K slices
+    static int env[2] = {0, 0};
+    static bool read = false;
+    if (!read) {
+        const char* v = getenv("QRM_IMMA_NKS");
+        if (v) sscanf(v, "%d,%d", &env[0], &env[1]);
+        read = true;
+    }
+    int lim = std::min(nsb, max_warps / rtiles);
+    if (env[gateup ? 0 : 1] > 0) lim = std::min(lim, env[gateup ? 0 : 1]);
     int nks = 1;
     for (int d = lim; d >= 1; d--)
         if (nsb % d == 0) { nks = d; break; }
@@ -253,7 +262,7 @@ bool imma_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, I
     for (int rtiles = imma_rtiles(gateup, p.cols / 256); rtiles >= 1; rtiles >>= 1) {
         if (p.rows % (RT * rtiles)) continue;
         sel->rtiles = rtiles;
-        sel->cw = imma_kslices(p.cols / 256, rtiles, sel->ntk == 1 ? qrm::kImmaMaxWarps : qrm::kImmaMaxWarps2) * rtiles;
+        sel->cw = imma_kslices(p.cols / 256, rtiles, sel->ntk == 1 ? qrm::kImmaMaxWarps : qrm::kImmaMaxWarps2, gateup) * rtiles;
         if (!qrm::imma_plan(fmts, p.cols, qrm::kImmaRows * rtiles, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg))
             continue;
         // split shared items need the per-part buffers
