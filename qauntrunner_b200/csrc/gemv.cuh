@@ -316,6 +316,7 @@ struct GemvParams {
     const int32_t* offsets;    // [E+1]
     const int32_t* perm;       // [T*k]
     const int32_t* pos_tok;    // [T*k] token of the assignment at each position (perm / k)
+    const int4* slot_info;     // [slots] (expert, first position, tokens, first token), or null
     const int32_t* n_active;   // routed slots (written by the dispatch kernel)
     int32_t* ctr;              // work counter of this launch (zeroed before it)
     const float* x_routed;     // gate/up: xn [T x d]; down: h [T*k x f]
@@ -353,6 +354,12 @@ struct GemvParams {
     // routing it reads was final two launches earlier; only the activations
     // come from the predecessor)
     int pdl;
+    // gate/up launches: build the down launch's activation tables as the
+    // outputs complete (one 32-output group of a row once its tiles are all
+    // written; qgrp_ctr counts them, zero between launches)
+    uint8_t* qtab;
+    int qtab_stride;
+    int32_t* qgrp_ctr;
     int fuse_combine;
     const float* cmb_x;        // residual [T x d] or null
     const float* cmb_w;        // top-k weights [T x k]

@@ -100,6 +100,24 @@ __device__ __forceinline__ void xquant_quad(float4 v, int lane, int c, int K, ui
     if ((lane & 7) == 0) reinterpret_cast<float2*>(row + xtab_ss(K))[g] = make_float2(s, sum);
 }
 
+// The same for one 32-element group gi, lane l holding element l.
+__device__ __forceinline__ void xquant_group(float v, int lane, int gi, int K, uint8_t* row) {
+    float amax = fabsf(v), sum = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    const float s = amax > 0.f ? amax * (1.f / 32639.f) : 0.f;
+    const float inv = amax > 0.f ? 32639.f / amax : 0.f;
+    int q = __float2int_rn(v * inv);
+    q = max(-32639, min(32639, q));
+    const int hi = (q + 128) >> 8;
+    row[gi * 32 + lane] = (uint8_t)(int8_t)hi;
+    row[xtab_lo(K) + gi * 32 + lane] = (uint8_t)(int8_t)(q - 256 * hi);
+    if (lane == 0) reinterpret_cast<float2*>(row + xtab_ss(K))[gi] = make_float2(s, sum);
+}
+
 // Quantises activation rows into tables (global memory), one warp per four
 // groups (K % 128 == 0).
 __global__ void xquant_kernel(const float* __restrict__ src, int K, int rows, uint8_t* __restrict__ tab,
@@ -607,11 +625,46 @@ struct ImmaRed {
 };
 
 // What a reduction needs once the stage and its header are gone.
+struct ImmaRedJob;
+template <int OUTS>
+__device__ __forceinline__ void imma_qgroups(const GemvParams& p, const ImmaRedJob& j, int lane);
+
 struct ImmaRedJob {
     int r;          // reduction number (slot r % kImmaRedSlots); -1: none
     int seg, part, tile, off, t0, nt;
     int shared, final_pass;
 };
+
+// Gate/up outputs of job j are written: count them against their 32-output
+// groups (per token row); the writer of a group's last tile quantises the
+// group into the down launch's table row (routed rows = output rows, shared
+// rows after the T*k routed ones).
+template <int OUTS>
+__device__ __forceinline__ void imma_qgroups(const GemvParams& p, const ImmaRedJob& j, int lane) {
+    const int f = p.rows, ng = f / 32;
+    __threadfence();
+    __syncwarp();
+    for (int q = 0; q < j.nt; q++) {
+        const int tk = j.t0 + q;
+        const int trow = j.shared ? p.T * p.k + tk : j.off + tk;
+        const float* hrow = j.shared ? p.out_shared + (size_t)tk * f : p.out_routed + (size_t)(j.off + tk) * f;
+        uint8_t* qrow = p.qtab + (size_t)trow * p.qtab_stride;
+        if (OUTS >= 32) {
+            for (int g = j.tile * (OUTS / 32); g < (j.tile + 1) * (OUTS / 32); g++)
+                xquant_group(__ldcg(hrow + 32 * g + lane), lane, g, f, qrow);
+        } else {
+            const int g = j.tile * OUTS / 32;
+            int last = 0;
+            if (lane == 0) last = atomicAdd(&p.qgrp_ctr[trow * ng + g], 1) == 32 / OUTS - 1;
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                xquant_group(__ldcg(hrow + 32 * g + lane), lane, g, f, qrow);
+                if (lane == 0) p.qgrp_ctr[trow * ng + g] = 0;
+            }
+        }
+    }
+}
 
 // The reduction of job j (all CW warps' partials are in its slot): adds the
 // K slices in a fixed order and writes the outputs (split parts: publishes
@@ -692,6 +745,7 @@ __device__ __forceinline__ void imma_reduce(const GemvParams& p, const ImmaConfi
             if (lane == 0) p.part_ctr[grow0 * p.tiles + j.tile] = 0;
         }
     }
+    if (M == 2 && p.qtab && (nsplit == 1 || split_done)) imma_qgroups<OUTS>(p, j, lane);
     if (M == 1 && p.fuse_combine && j.final_pass && (nsplit == 1 || split_done))
         imma_combine_tile<OUTS>(p, j.tile, n_active, lane);
     else if (p.fuse_combine)
@@ -879,15 +933,24 @@ expert_gemv_imma_kernel(GemvParams p, ImmaConfig cfg, int32_t* err) {
                 in.tile = j / ns1;
                 in.part = j - in.tile * ns1;
             }
-            in.e = p.active[in.slot];
-            in.off = 0;
-            in.n_tok = p.T;
-            if (in.seg == 0) { in.off = p.offsets[in.e]; in.n_tok = p.offsets[in.e + 1] - in.off; }
+            int tok0 = -1;
+            if (p.slot_info && in.seg == 0) {
+                // one load: expert, first position, tokens, first token
+                const int4 si = p.slot_info[in.slot];
+                in.e = si.x; in.off = si.y; in.n_tok = si.z; tok0 = si.w;
+            } else {
+                in.e = p.active[in.slot];
+                in.off = 0;
+                in.n_tok = p.T;
+                if (in.seg == 0) { in.off = p.offsets[in.e]; in.n_tok = p.offsets[in.e + 1] - in.off; }
+            }
             // table rows of the first pass's tokens, so consumers need no global load
             const int t1 = min(1, in.n_tok - 1);
             if (in.seg == 1) { in.tr0 = p.xtab_shared_base; in.tr1 = p.xtab_shared_base + t1; }
-            else if (p.routed_by_token) { in.tr0 = p.pos_tok[in.off]; in.tr1 = p.pos_tok[in.off + t1]; }
-            else { in.tr0 = in.off; in.tr1 = in.off + t1; }
+            else if (p.routed_by_token) {
+                in.tr0 = tok0 >= 0 ? tok0 : p.pos_tok[in.off];
+                in.tr1 = t1 ? p.pos_tok[in.off + t1] : in.tr0;
+            } else { in.tr0 = in.off; in.tr1 = in.off + t1; }
         };
         if (lane == 0 && (int)blockIdx.x < n_items) resolve(blockIdx.x, *nxt);
         __syncwarp();

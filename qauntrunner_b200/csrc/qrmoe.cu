@@ -156,6 +156,15 @@ int launch_tma(int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cud
 // Integer tensor-core kernel (Q4_K, Q8_0, Q4_0 with 256-multiple rows);
 // needs the activation tables of p.xtab (written by xquant_kernel).
 
+bool gu_tables_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QRM_GU_TABLES");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
 // Programmatic dependent launches between the forward's kernels, as a mask:
 // 1 gate/up, 2 down, 4 combine.  On B200 the expert launches ran slower as
 // dependents (measured 7570 -> 6966 / 7234 tokens/s at C5, T = 1), the
@@ -415,6 +424,8 @@ struct qrm_layer {
     float *h = nullptr, *hs = nullptr, *y = nullptr, *ys = nullptr, *out = nullptr;
     int32_t *topk_idx = nullptr, *perm = nullptr, *inv_perm = nullptr, *offsets = nullptr, *active = nullptr;
     int32_t* pos_tok = nullptr;
+    int4* slot_info = nullptr;    // per active slot: expert, first position, tokens, first token
+    int32_t* qgrp_ctr = nullptr;  // gate/up outputs per (down table row, 32-group), zero between launches
     qrm::Schedule* sched = nullptr;
     uint8_t* staging = nullptr;
     size_t staging_bytes = 0;
@@ -449,7 +460,7 @@ static void free_layer(qrm_layer* L) {
     void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_lm, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
                     L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn,
-                    L->part_buf, L->part_ctr, L->pos_tok, L->tile_ctr};
+                    L->part_buf, L->part_ctr, L->pos_tok, L->tile_ctr, L->slot_info, L->qgrp_ctr};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     clear_graphs(L);
@@ -495,6 +506,9 @@ static int alloc_work(qrm_layer* L, int T) {
     QRM_CUDA(cudaMalloc(&L->perm, sizeof(int32_t) * Tk));
     QRM_CUDA(cudaMalloc(&L->inv_perm, sizeof(int32_t) * Tk));
     QRM_CUDA(cudaMalloc(&L->pos_tok, sizeof(int32_t) * Tk));
+    QRM_CUDA(cudaMalloc(&L->slot_info, sizeof(int4) * (E + 1)));
+    QRM_CUDA(cudaMalloc(&L->qgrp_ctr, sizeof(int32_t) * (Tk + T) * (f / 32)));
+    QRM_CUDA(cudaMemset(L->qgrp_ctr, 0, sizeof(int32_t) * (Tk + T) * (f / 32)));
     QRM_CUDA(cudaMalloc(&L->offsets, sizeof(int32_t) * (E + 1)));
     QRM_CUDA(cudaMalloc(&L->active, sizeof(int32_t) * (E + 1)));
     QRM_CUDA(cudaMalloc(&L->sched, sizeof(qrm::Schedule)));
@@ -743,7 +757,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const float* xn = L->xn;
     qrm::TopkParams tp{L->logits, L->has_bias ? L->router_bias : nullptr, topk_idx, topk_w, T, E, k,
                        D.moe_sigmoid ? 1 : 0, D.routed_scale};
-    qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->pos_tok, L->offsets, L->active, L->sched, T, k, E,
+    qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched, T, k, E,
                            L->first_expert, L->n_local, shared ? 1 : 0};
     qrm::RouteParams rp{x, L->norm_w, L->router, L->has_offset ? L->offset : nullptr, L->xn, L->logits, T, d, E,
                         (flags & QRM_APPLY_NORM) ? 1 : 0, D.rms_eps};
@@ -794,6 +808,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU
     const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
     bool combined = false;
+    bool dn_tables_built = false;
     for (int stage = 0; stage < 2; stage++) {
         const bool gu = stage == 0;
         // activation tables for the integer tensor-core kernel
@@ -810,6 +825,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.offsets = L->offsets;
         gp.perm = L->perm;
         gp.pos_tok = L->pos_tok;
+        gp.slot_info = L->slot_info;
         gp.n_active = &L->sched->n_active;
         gp.x_routed = gu ? xn : L->h;
         gp.x_shared = gu ? xn : L->hs;
@@ -834,7 +850,23 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         // formats has one (shared items split along K to fit the stage)
         ImmaSel sp;
         const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && imma_select(fr, fs, gu, T, gp, &sp);
-        if (want_tab) {
+        // gate/up in one integer-kernel launch can build the down tables as its
+        // outputs complete (QRM_GU_TABLES=1; measured slower on B200 at C5,
+        // T = 1: 61 -> 85 us gate/up for 43 -> 40 us down)
+        if (gu && gu_tables_enabled() && imma_usable(D.fmt_down, d, f, false) &&
+            (!shared || imma_usable(D.fmt_sh_down, d, f, false) || same_fmt)) {
+            ImmaSel sg;
+            gp.mode = 0;
+            if (pair || (same_fmt && imma_select(fr, shared ? fr : -1, true, T, gp, &sg))) {
+                gp.qtab = L->xtab_dn;
+                gp.qtab_stride = qrm::xtab_stride(f);
+                gp.qgrp_ctr = L->qgrp_ctr;
+                dn_tables_built = true;
+            }
+        }
+        if (want_tab && !gu && dn_tables_built) {
+            // nothing to build: the gate/up launch wrote the tables
+        } else if (want_tab) {
             // the kernels quantise resident tables themselves when every
             // integer-kernel launch of this stage keeps them resident
             bool in_kernel;

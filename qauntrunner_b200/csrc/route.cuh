@@ -455,6 +455,7 @@ struct DispatchParams {
     int32_t* perm;            // [T*k]
     int32_t* inv_perm;        // [T*k]
     int32_t* pos_tok;         // [T*k] token of the assignment at each position
+    int4* slot_info;          // [E+1] per active slot: expert, first position, tokens, first token
     int32_t* offsets;         // [E+1]
     int32_t* active;          // [E+1] slot -> expert (E = shared)
     Schedule* sched;
@@ -565,6 +566,13 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
         if (e >= 0 && lane == leader) atomicAdd(&base[e], __popc(peers));
         __syncthreads();
     }
+    // per active slot: expert, first position, tokens, first token
+    const int na = p.sched->n_active;
+    for (int sl = tid; sl < na; sl += kDispatchThreads) {
+        const int e = p.active[sl], off = p.offsets[e];
+        p.slot_info[sl] = make_int4(e, off, p.offsets[e + 1] - off, p.perm[off] / p.k);
+    }
+    if (tid == 0 && p.has_shared) p.slot_info[na] = make_int4(E, 0, p.T, 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -831,11 +839,17 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
             p.perm[pos] = a;
             p.inv_perm[a] = pos;
             p.pos_tok[pos] = a / p.k;
-            if (first && local) p.active[dbelow] = e;
+            if (first && local) {
+                p.active[dbelow] = e;
+                p.slot_info[dbelow] = make_int4(e, below, __popc(peers), a / p.k);
+            }
         }
         if (lane == 0) {
             const int nd = __popc(firsts);
-            if (p.has_shared) p.active[nd] = E;
+            if (p.has_shared) {
+                p.active[nd] = E;
+                p.slot_info[nd] = make_int4(E, 0, p.T, 0);
+            }
             p.sched->n_active = nd;
             for (int q = 0; q < 4; q++) p.sched->ctr[q] = 0;
         }
