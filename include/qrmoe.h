@@ -182,6 +182,25 @@ int  qrm_matrix_gemv(qrm_matrix* m, const float* x_dev, int T, float* y_dev, voi
  * Nothing needs to start at zero: every table byte read is written first. */
 int  qrm_matrix_gemv_static(qrm_matrix* m, const float* x_dev, int T, float* y_dev, void* stream);
 
+/* ---- expert parallelism (no counterpart in the reference, whose MoE layer
+ * runs in one process) ----
+ * world ranks, one process and GPU each; rank r holds the routed experts
+ * [r*E/world, (r+1)*E/world) (qrm_expert_range; uploads of other experts fail
+ * with QRM_E_INVALID) and replicas of norm, router and shared expert.  Every
+ * rank calls qrm_forward / qrm_forward_device with the same T for its own
+ * tokens; the forward routes them (bit-identical on every rank), all-gathers
+ * the normalised tokens with their top-k over NCCL, runs the local experts for
+ * all ranks' tokens, returns the expert outputs to the token owners (grouped
+ * send/recv) and combines on the owner in slot order, so the output equals the
+ * single-GPU forward bit for bit.  The id comes from qrm_nccl_unique_id on one
+ * rank and is passed to every rank by the host (128 bytes); qrm_create_ep
+ * returns once all ranks have joined.  Per-stage profiling is single-GPU
+ * only. */
+#define QRM_NCCL_ID_BYTES 128
+int qrm_nccl_unique_id(void* id_out);
+int qrm_create_ep(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out);
+int qrm_expert_range(qrm_layer* layer, int* first, int* count);
+
 /* ---- synthetic weights on the device (the reference's `synthesize`,
  * src/QuantRunner.Cli/Program.cs:247-369) ----
  * qrm_synth_gaussian fills dst_dev[n] with sigma * N(0,1) from a

@@ -44,6 +44,17 @@ ERRORS = {-1: "QRM_E_INVALID", -2: "QRM_E_FORMAT", -3: "QRM_E_SIZE", -4: "QRM_E_
           -6: "QRM_E_NCCL", -7: "QRM_E_TIMEOUT", -8: "QRM_E_NOMEM", -9: "QRM_E_CAPACITY"}
 
 
+NCCL_ID_BYTES = 128
+
+
+def nccl_unique_id():
+    """A new NCCL unique id (128 bytes) for qrm_create_ep; made on one rank and
+    passed to all of them by the host."""
+    buf = C.create_string_buffer(NCCL_ID_BYTES)
+    _check(lib().qrm_nccl_unique_id(buf))
+    return buf.raw
+
+
 class QrmError(RuntimeError):
     def __init__(self, code, msg):
         super().__init__(f"{ERRORS.get(code, code)}: {msg}")
@@ -91,6 +102,9 @@ _SIGS = {
     "qrm_matrix_destroy": (None, [P]),
     "qrm_matrix_gemv": (C.c_int, [P, P, C.c_int, P, P]),
     "qrm_matrix_gemv_static": (C.c_int, [P, P, C.c_int, P, P]),
+    "qrm_nccl_unique_id": (C.c_int, [P]),
+    "qrm_create_ep": (C.c_int, [C.POINTER(LayerDesc), C.c_int, C.c_int, P, C.POINTER(P)]),
+    "qrm_expert_range": (C.c_int, [P, P, P]),
     "qrm_synth_gaussian": (C.c_int, [P, C.c_int64, C.c_uint64, C.c_float, P]),
     "qrm_synth_quantize": (C.c_int, [C.c_int, P, C.c_int64, P, P]),
 }
@@ -148,15 +162,30 @@ class MoeLayer:
 
     def __init__(self, d_model, n_experts, n_active, expert_ffn, moe_sigmoid=False, routed_scale=1.0,
                  n_shared=0, swiglu_limit=0.0, rms_eps=1e-5, fmt=(6, 6, 6), shared_fmt=None, device=0,
-                 max_tokens=1):
+                 max_tokens=1, rank=0, world=1, nccl_id=None):
+        """rank / world / nccl_id (bytes from nccl_unique_id() on one rank): an
+        expert-parallel layer holding the routed experts of expert_range()."""
         shared_fmt = shared_fmt or fmt
         self.desc = LayerDesc(d_model, n_experts, n_active, expert_ffn, int(bool(moe_sigmoid)), routed_scale,
                               n_shared, swiglu_limit, rms_eps, int(fmt[0]), int(fmt[1]), int(fmt[2]),
                               int(shared_fmt[0]), int(shared_fmt[1]), int(shared_fmt[2]), device, max_tokens)
         self.k = min(n_active, 8)
+        self.rank, self.world = rank, world
         h = P()
-        _check(lib().qrm_create(C.byref(self.desc), C.byref(h)))
+        if world > 1:
+            if nccl_id is None or len(nccl_id) != NCCL_ID_BYTES:
+                raise ValueError("an expert-parallel layer needs the 128-byte NCCL id of nccl_unique_id()")
+            buf = C.create_string_buffer(bytes(nccl_id), NCCL_ID_BYTES)
+            _check(lib().qrm_create_ep(C.byref(self.desc), rank, world, buf, C.byref(h)))
+        else:
+            _check(lib().qrm_create(C.byref(self.desc), C.byref(h)))
         self._h = h
+
+    def expert_range(self):
+        """(first, count) of the routed experts this layer holds."""
+        a, b = C.c_int(0), C.c_int(0)
+        _check(lib().qrm_expert_range(self._h, C.byref(a), C.byref(b)))
+        return a.value, b.value
 
     def close(self):
         if getattr(self, "_h", None):

@@ -55,7 +55,9 @@ def build(ptxas_verbose=False, force=False, quiet=False):
                 print(" ".join(cmd), flush=True)
             subprocess.run(cmd, check=True)
     if force or sources_newer(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lpthread"]
+        # NCCL (expert parallelism): libnccl.so.2 resolves at load time; in a
+        # process that imported torch it is the copy torch already loaded
+        cmd = [nvcc()] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-lnccl", "-lpthread"]
         if not quiet:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

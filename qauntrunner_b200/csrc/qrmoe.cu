@@ -23,7 +23,10 @@
 #include <vector>
 
 #include "../../include/qrmoe.h"
+#include <nccl.h>
+
 #include "combine.cuh"
+#include "ep.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
@@ -48,6 +51,11 @@ int fail(int code, const char* fmt, ...) {
     return code;
 }
 
+#define QRM_NCCL(expr)                                                                          \
+    do {                                                                                        \
+        ncclResult_t r_ = (expr);                                                               \
+        if (r_ != ncclSuccess) return fail(QRM_E_NCCL, "%s: %s", #expr, ncclGetErrorString(r_)); \
+    } while (0)
 #define QRM_CUDA(expr)                                                                          \
     do {                                                                                        \
         cudaError_t e_ = (expr);                                                                \
@@ -403,6 +411,15 @@ struct qrm_layer {
     qrm_layer_desc desc{};
     int k = 0;
     int first_expert = 0, n_local = 0;  // routed experts held by this layer
+    // expert parallelism: rank of world, one NCCL communicator per layer
+    int world = 1, rank = 0;
+    ncclComm_t comm = nullptr;
+    float* rec_own = nullptr;     // [T][d + 2k] this rank's (xn, top-k idx, top-k w) records
+    float* rec_all = nullptr;     // [world*T][d + 2k] gathered records
+    float* xn_all = nullptr;      // [world*T][d]
+    int32_t* idx_all = nullptr;   // [world*T][k]
+    float* ysend = nullptr;       // [world][T*k][d] output rows per owner
+    float* yrecv = nullptr;       // [world][T*k][d] rows of this rank's tokens, per holder
     bool shared_enabled = false;        // GLM layer with n_shared > 0
     int sm_count = 0;
     cudaStream_t stream = nullptr;
@@ -460,13 +477,15 @@ static void free_layer(qrm_layer* L) {
     void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_lm, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
                     L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn,
-                    L->part_buf, L->part_ctr, L->pos_tok, L->tile_ctr, L->slot_info, L->qgrp_ctr};
+                    L->part_buf, L->part_ctr, L->pos_tok, L->tile_ctr, L->slot_info, L->qgrp_ctr,
+                    L->rec_own, L->rec_all, L->xn_all, L->idx_all, L->ysend, L->yrecv};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     clear_graphs(L);
     for (cudaEvent_t e : L->ev)
         if (e) cudaEventDestroy(e);
     if (L->stream) cudaStreamDestroy(L->stream);
+    if (L->comm) ncclCommDestroy(L->comm);
     delete L;
 }
 
@@ -537,11 +556,40 @@ static int alloc_work(qrm_layer* L, int T) {
 extern "C" int qrm_version(void) { return QRM_ABI_VERSION; }
 extern "C" const char* qrm_last_error(void) { return g_err.c_str(); }
 
+static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out);
+
 extern "C" int qrm_create(const qrm_layer_desc* desc, qrm_layer** out) {
+    return create_layer(desc, 0, 1, nullptr, out);
+}
+
+extern "C" int qrm_nccl_unique_id(void* id_out) {
+    if (!id_out) return fail(QRM_E_INVALID, "NULL argument");
+    ncclUniqueId id;
+    QRM_NCCL(ncclGetUniqueId(&id));
+    static_assert(sizeof(ncclUniqueId) == QRM_NCCL_ID_BYTES, "NCCL unique id size");
+    memcpy(id_out, &id, sizeof id);
+    return QRM_OK;
+}
+
+extern "C" int qrm_create_ep(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out) {
+    if (!nccl_id) return fail(QRM_E_INVALID, "NULL NCCL id");
+    return create_layer(desc, rank, world, nccl_id, out);
+}
+
+extern "C" int qrm_expert_range(qrm_layer* L, int* first, int* count) {
+    if (!L || !first || !count) return fail(QRM_E_INVALID, "NULL argument");
+    *first = L->first_expert;
+    *count = L->n_local;
+    return QRM_OK;
+}
+
+static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out) {
     if (!out) return fail(QRM_E_INVALID, "out is NULL");
     *out = nullptr;
     int rc = check_desc(desc);
     if (rc) return rc;
+    if (world < 1 || rank < 0 || rank >= world) return fail(QRM_E_INVALID, "rank %d of world %d", rank, world);
+    if (desc->n_experts % world) return fail(QRM_E_INVALID, "n_experts %d is not a multiple of world %d", desc->n_experts, world);
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(QRM_E_CUDA, "no CUDA device");
     if (desc->device < 0 || desc->device >= ndev) return fail(QRM_E_INVALID, "device %d out of range", desc->device);
@@ -552,8 +600,10 @@ extern "C" int qrm_create(const qrm_layer_desc* desc, qrm_layer** out) {
     qrm_layer* L = new qrm_layer();
     L->desc = *desc;
     L->k = std::min(desc->n_active, 8);
-    L->first_expert = 0;
-    L->n_local = desc->n_experts;
+    L->world = world;
+    L->rank = rank;
+    L->n_local = desc->n_experts / world;
+    L->first_expert = rank * L->n_local;
     L->shared_enabled = desc->moe_sigmoid && desc->n_shared > 0;
     L->sm_count = prop.multiProcessorCount;
     auto bail = [&](int code) { free_layer(L); return code; };
@@ -594,8 +644,24 @@ extern "C" int qrm_create(const qrm_layer_desc* desc, qrm_layer** out) {
         cudaMalloc(&L->router_lm, sizeof(float) * (size_t)E * 8 * qrm::route_lane_pitch(d)) != cudaSuccess ||
         cudaMalloc(&L->router_bias, sizeof(float) * E) != cudaSuccess || cudaMalloc(&L->offset, sizeof(float) * E) != cudaSuccess)
         return bail(fail(QRM_E_NOMEM, "router allocation failed"));
-    rc = alloc_work(L, desc->max_tokens);
+    // the expert stages of an expert-parallel layer run over every rank's tokens
+    rc = alloc_work(L, desc->max_tokens * world);
     if (rc) return bail(rc);
+    L->cap_T = desc->max_tokens;
+    if (world > 1) {
+        const size_t T = desc->max_tokens, G = world, k = L->k;
+        if (cudaMalloc(&L->rec_own, sizeof(float) * T * (d + 2 * k)) != cudaSuccess ||
+            cudaMalloc(&L->rec_all, sizeof(float) * G * T * (d + 2 * k)) != cudaSuccess ||
+            cudaMalloc(&L->xn_all, sizeof(float) * G * T * d) != cudaSuccess ||
+            cudaMalloc(&L->idx_all, sizeof(int32_t) * G * T * k) != cudaSuccess ||
+            cudaMalloc(&L->ysend, sizeof(float) * G * T * k * d) != cudaSuccess ||
+            cudaMalloc(&L->yrecv, sizeof(float) * G * T * k * d) != cudaSuccess)
+            return bail(fail(QRM_E_NOMEM, "expert-parallel buffers"));
+        ncclUniqueId id;
+        memcpy(&id, nccl_id, sizeof id);
+        ncclResult_t nr = ncclCommInitRank(&L->comm, world, id, rank);
+        if (nr != ncclSuccess) return bail(fail(QRM_E_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(nr)));
+    }
     // kernels with large dynamic shared memory
     if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(qrm::route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess ||
@@ -803,8 +869,35 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         mark(3);
     }
     L->last_xn = xn;
+    // expert parallelism: the expert stages run over every rank's tokens
+    const bool ep = L->world > 1;
+    const int G = L->world;
+    int Tx = T;
+    const float* xs = xn;
+    if (ep) {
+        if (prof) return fail(QRM_E_STATE, "per-stage profiling is single-GPU only");
+        // (normalised token, top-k) records of every rank
+        const int W = d + 2 * k;
+        const long long nrec = (long long)T * W;
+        int grid = (int)std::min<long long>((nrec + 255) / 256, (long long)L->sm_count * 8);
+        qrm::ep_pack_records_kernel<<<grid, 256, 0, s>>>(xn, topk_idx, topk_w, T, d, k, L->rec_own);
+        QRM_CUDA(cudaGetLastError());
+        QRM_NCCL(ncclAllGather(L->rec_own, L->rec_all, (size_t)nrec, ncclFloat32, L->comm, s));
+        Tx = G * T;
+        grid = (int)std::min<long long>(((long long)Tx * (d + k) + 255) / 256, (long long)L->sm_count * 8);
+        qrm::ep_unpack_records_kernel<<<grid, 256, 0, s>>>(L->rec_all, Tx, d, k, L->xn_all, L->idx_all);
+        QRM_CUDA(cudaGetLastError());
+        // dispatch of all ranks' assignments; the active list holds this rank's experts
+        qrm::TopkParams tpx{L->logits, nullptr, L->idx_all, nullptr, Tx, E, k, 0, 1.f};
+        qrm::DispatchParams dpx{L->idx_all, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched,
+                                Tx, k, E, L->first_expert, L->n_local, shared ? 1 : 0};
+        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, Tx, false), s>>>(dpx, tpx, 0);
+        QRM_CUDA(cudaGetLastError());
+        nl += 3;
+        xs = L->xn_all;
+    }
     // 4. gate/up (+ SwiGLU) and 5. down
-    const int nt = pick_nt(T);
+    const int nt = pick_nt(Tx);
     const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU
     const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
     bool combined = false;
@@ -818,8 +911,8 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         qrm::GemvParams gp{};
         gp.xtab = want_tab ? (gu ? L->xtab_gu : L->xtab_dn) : nullptr;
         gp.xtab_stride = qrm::xtab_stride(cols_s);
-        gp.xtab_shared_base = gu ? 0 : T * k;
-        gp.xtab_rows = gu ? T : T * k + (shared ? T : 0);
+        gp.xtab_shared_base = gu ? 0 : Tx * k;
+        gp.xtab_rows = gu ? Tx : Tx * k + (shared ? Tx : 0);
         gp.mats = L->mats_dev;
         gp.active = L->active;
         gp.offsets = L->offsets;
@@ -827,11 +920,11 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.pos_tok = L->pos_tok;
         gp.slot_info = L->slot_info;
         gp.n_active = &L->sched->n_active;
-        gp.x_routed = gu ? xn : L->h;
-        gp.x_shared = gu ? xn : L->hs;
+        gp.x_routed = gu ? xs : L->h;
+        gp.x_shared = gu ? xs : L->hs;
         gp.out_routed = gu ? L->h : L->y;
         gp.out_shared = gu ? L->hs : L->ys;
-        gp.T = T;
+        gp.T = Tx;
         gp.k = k;
         gp.E = E;
         gp.rows = gu ? f : d;
@@ -844,20 +937,20 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
         gp.part_buf = L->part_buf;
         gp.part_ctr = L->part_ctr;
-        gp.part_rows = T;
+        gp.part_rows = Tx;
         gp.pdl = (!prof && (L->pdl & (gu ? 1 : 2))) ? (gu ? 1 : 2) : 0;   // profiling events sit between the launches
         // routed + shared expert in one integer-kernel launch when the pair of
         // formats has one (shared items split along K to fit the stage)
         ImmaSel sp;
-        const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && imma_select(fr, fs, gu, T, gp, &sp);
+        const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && imma_select(fr, fs, gu, Tx, gp, &sp);
         // gate/up in one integer-kernel launch can build the down tables as its
         // outputs complete (QRM_GU_TABLES=1; measured slower on B200 at C5,
-        // T = 1: 61 -> 85 us gate/up for 43 -> 40 us down)
+        // Tx = 1: 61 -> 85 us gate/up for 43 -> 40 us down)
         if (gu && gu_tables_enabled() && imma_usable(D.fmt_down, d, f, false) &&
             (!shared || imma_usable(D.fmt_sh_down, d, f, false) || same_fmt)) {
             ImmaSel sg;
             gp.mode = 0;
-            if (pair || (same_fmt && imma_select(fr, shared ? fr : -1, true, T, gp, &sg))) {
+            if (pair || (same_fmt && imma_select(fr, shared ? fr : -1, true, Tx, gp, &sg))) {
                 gp.qtab = L->xtab_dn;
                 gp.qtab_stride = qrm::xtab_stride(f);
                 gp.qgrp_ctr = L->qgrp_ctr;
@@ -874,24 +967,24 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                 in_kernel = sp.cfg.res_rows > 0;
             } else {
                 ImmaSel sr, ss;
-                const bool ur = imma_select(fr, same_fmt && shared ? fr : -1, gu, T, gp, &sr);
-                const bool us = shared && !same_fmt && imma_select(-1, fs, gu, T, gp, &ss);
+                const bool ur = imma_select(fr, same_fmt && shared ? fr : -1, gu, Tx, gp, &sr);
+                const bool us = shared && !same_fmt && imma_select(-1, fs, gu, Tx, gp, &ss);
                 in_kernel = (ur || us) && (!ur || sr.cfg.res_rows > 0) && (!us || ss.cfg.res_rows > 0);
             }
             if (in_kernel) {
-                gp.xq_a = gu ? xn : L->h;
-                gp.xq_b = gu ? xn : L->hs;
-                gp.xq_split = gu ? T : T * k;
+                gp.xq_a = gu ? xs : L->h;
+                gp.xq_b = gu ? xs : L->hs;
+                gp.xq_split = gu ? Tx : Tx * k;
             } else {
                 int rc;
                 if (gu) {
-                    rc = launch_xquant(xn, d, T, L->xtab_gu, s);
+                    rc = launch_xquant(xs, d, Tx, L->xtab_gu, s);
                     nl++;
                 } else {
-                    rc = launch_xquant(L->h, f, T * k, L->xtab_dn, s);
+                    rc = launch_xquant(L->h, f, Tx * k, L->xtab_dn, s);
                     nl++;
                     if (!rc && shared) {
-                        rc = launch_xquant(L->hs, f, T, L->xtab_dn + (size_t)qrm::xtab_stride(f) * T * k, s);
+                        rc = launch_xquant(L->hs, f, Tx, L->xtab_dn + (size_t)qrm::xtab_stride(f) * Tx * k, s);
                         nl++;
                     }
                 }
@@ -901,8 +994,8 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         // down in one integer-kernel launch: the kernel also combines
         if (!gu) {
             ImmaSel sd;
-            const bool one = pair || (same_fmt && imma_select(fr, shared ? fr : -1, false, T, gp, &sd));
-            if (one && L->n_local == E && fused_combine_enabled()) {
+            const bool one = pair || (same_fmt && imma_select(fr, shared ? fr : -1, false, Tx, gp, &sd));
+            if (one && !ep && L->n_local == E && fused_combine_enabled()) {
                 gp.fuse_combine = 1;
                 gp.cmb_x = (flags & QRM_ADD_RESIDUAL) ? x : nullptr;
                 gp.cmb_w = topk_w;
@@ -916,7 +1009,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             gp.mode = 0;
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
             bool used = false;
-            int rc = launch_imma_pair(fr, fs, gu, T, gp, L->sm_count, &L->sched->err, s, &used);
+            int rc = launch_imma_pair(fr, fs, gu, Tx, gp, L->sm_count, &L->sched->err, s, &used);
             if (rc) return rc;
             if (!used) return fail(QRM_E_STATE, "internal: the paired expert kernel declined the launch");
             nl++;
@@ -939,6 +1032,29 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         }
         mark(gu ? 4 : 5);
     }
+    if (ep) {
+        // expert output rows back to the token owners; the owner combines in slot order
+        const long long n4 = (long long)Tx * k * (d / 4);
+        int grid = (int)std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 16);
+        qrm::ep_pack_outputs_kernel<<<grid, 256, 0, s>>>(L->y, L->inv_perm, L->idx_all, G, T, k, d, L->first_expert,
+                                                         L->n_local, L->ysend);
+        QRM_CUDA(cudaGetLastError());
+        const size_t blk = (size_t)T * k * d;
+        QRM_NCCL(ncclGroupStart());
+        for (int q = 0; q < G; q++) {
+            QRM_NCCL(ncclSend(L->ysend + q * blk, blk, ncclFloat32, q, L->comm, s));
+            QRM_NCCL(ncclRecv(L->yrecv + q * blk, blk, ncclFloat32, q, L->comm, s));
+        }
+        QRM_NCCL(ncclGroupEnd());
+        const long long m4 = (long long)T * (d / 4);
+        grid = (int)std::min<long long>((m4 + 255) / 256, (long long)L->sm_count * 16);
+        qrm::ep_combine_kernel<<<grid, 256, 0, s>>>((flags & QRM_ADD_RESIDUAL) ? x : nullptr, topk_w, topk_idx, L->yrecv,
+                                                    shared ? L->ys + (size_t)L->rank * T * d : nullptr, T, k, d,
+                                                    E / G, out);
+        QRM_CUDA(cudaGetLastError());
+        nl += 2;
+        combined = true;
+    }
     // 6. combine (unless the down kernel did it)
     if (!combined) {
         qrm::CombineParams cp{(flags & QRM_ADD_RESIDUAL) ? x : nullptr, L->y, shared ? L->ys : nullptr, L->inv_perm,
@@ -960,6 +1076,15 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
 // and profiling state; uploads invalidate the cache) launched on `s`.
 static int run_forward(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* idx, float* w,
                        cudaStream_t s) {
+    if (L->world > 1) {
+        // expert-parallel forwards launch directly (their NCCL calls are not captured)
+        int rc = launch_forward(L, x, T, flags, out, idx, w, s);
+        if (rc) return rc;
+        L->last_T = T;
+        L->profiled_last = false;
+        L->last_xn = L->xn;
+        return QRM_OK;
+    }
     qrm_layer::GraphKey key{x, out, idx, w, T, flags, L->profiling ? 1 : 0};
     auto it = L->graphs.find(key);
     if (it == L->graphs.end()) {

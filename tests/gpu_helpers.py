@@ -12,19 +12,23 @@ from tests import oracle_api as O
 OUT_TOL = 1e-3
 
 
-def make_layer(case, max_tokens):
+def make_layer(case, max_tokens, device=0, rank=0, world=1, nccl_id=None):
+    """The case's layer on `device`; an expert-parallel one (world > 1) gets
+    only its own block of routed experts."""
     cfg = case.cfg
     shared_fmt = case.fmt_sh if case.shared else None
     fmt = (case.fmt_gate, case.fmt_up, case.fmt_down)
     L = Q.MoeLayer(cfg["d_model"], cfg["n_experts"], cfg["n_active"], cfg["expert_ffn"],
                    moe_sigmoid=bool(cfg["moe_sigmoid"]), routed_scale=cfg["routed_scale"],
                    n_shared=cfg["n_shared"], swiglu_limit=cfg["swiglu_limit"], rms_eps=cfg["rms_eps"],
-                   fmt=fmt, shared_fmt=shared_fmt or fmt, max_tokens=max_tokens)
+                   fmt=fmt, shared_fmt=shared_fmt or fmt, max_tokens=max_tokens, device=device,
+                   rank=rank, world=world, nccl_id=nccl_id)
     L.upload_norm(case.norm_w)
     L.upload_router(case.router, case.router_bias)
     if case.logit_offset is not None:
         L.upload_logit_offset(case.logit_offset)
-    for e in range(cfg["n_experts"]):
+    first, count = L.expert_range()
+    for e in range(first, first + count):
         L.upload_expert(e, Q.GATE, case.fmt_gate, case.gate[e])
         L.upload_expert(e, Q.UP, case.fmt_up, case.up[e])
         L.upload_expert(e, Q.DOWN, case.fmt_down, case.down[e])

@@ -98,6 +98,14 @@ def matvec(fmt, w, rows, cols, x, threads=1):
     return y
 
 
+def swiglu(g, u, limit):
+    """TransformerOps.SiluMulInPlace / Glm5Ops.LimitedSwiglu (limit > 0) of g and u."""
+    g = np.array(g, dtype=np.float32, copy=True)
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    lib().orc_swiglu(ptr(g), ptr(u), g.size, limit)
+    return g
+
+
 def expf(x):
     x = np.ascontiguousarray(x, dtype=np.float32)
     y = np.empty_like(x)
