@@ -184,12 +184,16 @@ def run_reference(args, rank, world):
 
 # ------------------------------------------------------------------ GPU leg
 
-def build_layer(torch, Q, dev, T, seed=SEED):
+def build_layer(torch, Q, dev, T, seed=SEED, rank=0, world=1, nccl_id=None):
+    """The workload's layer; with world > 1 an expert-parallel layer holding
+    this rank's block of routed experts (the weights are the same on every
+    rank: each expert is generated from its own seed)."""
     W = WORKLOAD
     d, f, E = W["d_model"], W["expert_ffn"], W["n_experts"]
     layer = Q.MoeLayer(d, E, W["n_active"], f, moe_sigmoid=True, routed_scale=W["routed_scale"],
                        n_shared=W["n_shared"], swiglu_limit=W["swiglu_limit"], rms_eps=W["rms_eps"],
-                       fmt=W["fmt"], shared_fmt=W["shared_fmt"], device=dev, max_tokens=T)
+                       fmt=W["fmt"], shared_fmt=W["shared_fmt"], device=dev, max_tokens=T,
+                       rank=rank, world=world, nccl_id=nccl_id)
     n = f * d
     tmp = torch.empty(n, dtype=torch.float32, device=f"cuda:{dev}")
     qbuf = torch.empty(Q.tensor_bytes(n, 4), dtype=torch.uint8, device=f"cuda:{dev}")
@@ -200,7 +204,8 @@ def build_layer(torch, Q, dev, T, seed=SEED):
         Q.synth_quantize(fmt, tmp.data_ptr(), n, qbuf.data_ptr())
         layer.upload_expert_device(expert, which, fmt, qbuf.data_ptr(), nb)
 
-    for e in range(E):
+    first, count = layer.expert_range()
+    for e in range(first, first + count):
         for w in range(3):
             synth(e, w, W["fmt"][w], seed * 4096 + e * 3 + w)
     for w in range(3):
@@ -241,7 +246,15 @@ def run_ours(args, rank, world, dist):
     W = WORKLOAD
     d = W["d_model"]
     t_build = time.perf_counter()
-    layer = build_layer(torch, Q, dev, T, seed=SEED)
+    nccl_id = None
+    if world > 1:
+        # expert parallelism: one NCCL id, made on rank 0, for the library's communicator
+        idt = torch.zeros(Q.NCCL_ID_BYTES, dtype=torch.uint8, device=f"cuda:{dev}")
+        if rank == 0:
+            idt.copy_(torch.frombuffer(bytearray(Q.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(idt, 0)
+        nccl_id = bytes(idt.cpu().numpy().tobytes())
+    layer = build_layer(torch, Q, dev, T, seed=SEED, rank=rank, world=world, nccl_id=nccl_id)
     log(f"[rank {rank}] layer built in {time.perf_counter() - t_build:.1f}s")
     nsteps = args.warmup + args.steps
     g = torch.Generator(device=f"cuda:{dev}")
@@ -259,7 +272,7 @@ def run_ours(args, rank, world, dist):
         layer.forward_device(xs[i].data_ptr(), T, out.data_ptr(), flags, idx.data_ptr(), wts.data_ptr(), sp)
 
     with torch.cuda.stream(stream):
-        for prof in (False, True):   # capture both forward graphs before timing
+        for prof in ((False, True) if world == 1 else (False,)):   # capture the forward graphs before timing
             layer.set_profiling(prof)
             for i in range(args.warmup):
                 flush.fill_(float(i))
@@ -298,17 +311,18 @@ def run_ours(args, rank, world, dist):
     stage_ms = np.zeros(Q.STAGE_COUNT)
     stage_bytes = np.zeros(Q.STAGE_COUNT)
     nprof = min(args.steps, 64)
-    layer.set_profiling(True)
-    with torch.cuda.stream(stream):
-        for i in range(nprof):
-            flush.fill_(float(i))
-            step(args.warmup + i)
-            ms, by = layer.last_profile()
-            stage_ms += ms
-            stage_bytes += by
-    layer.set_profiling(False)
-    torch.cuda.synchronize()
-    layer.sync()
+    if world == 1:
+        layer.set_profiling(True)
+        with torch.cuda.stream(stream):
+            for i in range(nprof):
+                flush.fill_(float(i))
+                step(args.warmup + i)
+                ms, by = layer.last_profile()
+                stage_ms += ms
+                stage_bytes += by
+        layer.set_profiling(False)
+        torch.cuda.synchronize()
+        layer.sync()
 
     # ---- e2e: host (pinned) buffers through the C ABI, copies inside the timed region
     xh = xs.cpu().pin_memory()
@@ -351,7 +365,23 @@ def run_ours(args, rank, world, dist):
     gu_ms, gu_bytes = stage_ms[3], stage_bytes[3]   # over the nprof breakdown steps
     achieved = gu_bytes / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else 0.0
     traffic = traffic_from_profiles()
-    layer_bytes = (stage_bytes[3] + stage_bytes[4]) / nprof + (W["n_experts"] * d * 4 + T * d * 4 * 2)
+    if world == 1:
+        layer_bytes = (stage_bytes[3] + stage_bytes[4]) / nprof + (W["n_experts"] * d * 4 + T * d * 4 * 2)
+        roof_kernel = "expert gate/up fused dequant GEMV + SwiGLU"
+    else:
+        # expert parallelism (no per-stage events): compressed bytes this rank streamed in
+        # the last step (its experts that the gathered batch selected + shared expert +
+        # router) over the step time of the timed region
+        _, off = layer.last_dispatch(T)
+        first, count = layer.expert_range()
+        used = int(np.count_nonzero(np.diff(off)[first:first + count]))
+        f = W["expert_ffn"]
+        ebytes = 3 * Q.tensor_bytes(d * f, W["fmt"][0])
+        sbytes = 3 * Q.tensor_bytes(d * f, W["shared_fmt"][0])
+        layer_bytes = used * ebytes + sbytes + W["n_experts"] * d * 4
+        achieved = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
+        traffic = None
+        roof_kernel = "whole layer step per rank (expert parallel: no per-stage events)"
     layer_gbs = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
 
     if rank != 0:
@@ -373,8 +403,8 @@ def run_ours(args, rank, world, dist):
         config=dict(workload=WORKLOAD["name"], tokens_per_rank=T, d_model=d, n_experts=W["n_experts"],
                     top_k=W["n_active"], expert_ffn=W["expert_ffn"], formats="routed Q4_K, shared Q8_0",
                     l2="flushed before every step (256 MiB write, outside the timed events)",
-                    parallelism="single GPU" if world == 1 else f"{world} independent replicas"),
-        roofline=dict(bound="hbm", kernel="expert gate/up fused dequant GEMV + SwiGLU", achieved=achieved,
+                    parallelism="single GPU" if world == 1 else f"ep{world} (expert parallel, NCCL)"),
+        roofline=dict(bound="hbm", kernel=roof_kernel, achieved=achieved,
                       peak=peak, unit="GB/s", frac=achieved / peak if peak else None, peak_kind=peak_kind,
                       traffic=traffic),
         layer_hbm=dict(achieved_gbs=layer_gbs, frac_of_8tbs=layer_gbs / NOMINAL_HBM_GBS,

@@ -164,6 +164,17 @@ int launch_tma(int nt, const qrm::GemvParams& p, int sm_count, int32_t* err, cud
 // Integer tensor-core kernel (Q4_K, Q8_0, Q4_0 with 256-multiple rows);
 // needs the activation tables of p.xtab (written by xquant_kernel).
 
+// Expert-parallel forwards are captured into CUDA graphs with their NCCL
+// calls (QRM_EP_GRAPH=0 launches them directly).
+bool ep_graphs_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QRM_EP_GRAPH");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
 bool gu_tables_enabled() {
     static int v = -1;
     if (v < 0) {
@@ -461,12 +472,19 @@ struct qrm_layer {
     cudaEvent_t ev[QRM_STAGE_COUNT + 1] = {};
     bool last_shared = false;
     // CUDA graphs of the forward, keyed by buffers, T, flags and profiling
-    using GraphKey = std::tuple<const void*, const void*, const void*, const void*, int, int, int>;
-    std::map<GraphKey, std::pair<cudaGraphExec_t, int>> graphs;   // graph, kernel launches in it
+    // one instantiated graph per (T, flags, profiling); a call with other buffers
+    // re-captures and updates it in place (cudaGraphExecUpdate)
+    using GraphKey = std::tuple<int, int, int>;
+    struct Graph {
+        cudaGraphExec_t exec = nullptr;
+        int launches = 0;                // kernel launches in it
+        const void* ptrs[4] = {};        // x, out, top-k idx, top-k w it was captured with
+    };
+    std::map<GraphKey, Graph> graphs;
 };
 
 static void clear_graphs(qrm_layer* L) {
-    for (auto& kv : L->graphs) cudaGraphExecDestroy(kv.second.first);
+    for (auto& kv : L->graphs) cudaGraphExecDestroy(kv.second.exec);
     L->graphs.clear();
 }
 
@@ -1076,8 +1094,8 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
 // and profiling state; uploads invalidate the cache) launched on `s`.
 static int run_forward(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* idx, float* w,
                        cudaStream_t s) {
-    if (L->world > 1) {
-        // expert-parallel forwards launch directly (their NCCL calls are not captured)
+    if (L->world > 1 && !ep_graphs_enabled()) {
+        // expert-parallel forwards launched directly (QRM_EP_GRAPH=0)
         int rc = launch_forward(L, x, T, flags, out, idx, w, s);
         if (rc) return rc;
         L->last_T = T;
@@ -1085,10 +1103,25 @@ static int run_forward(qrm_layer* L, const float* x, int T, int flags, float* ou
         L->last_xn = L->xn;
         return QRM_OK;
     }
-    qrm_layer::GraphKey key{x, out, idx, w, T, flags, L->profiling ? 1 : 0};
+    // expert-parallel graphs hold NCCL calls: they always run on the layer's own
+    // buffers (user buffers are copied in and out) so one graph serves every call
+    float* user_out = out;
+    int32_t* user_idx = idx;
+    float* user_w = w;
+    const bool ep_bufs = L->world > 1;
+    if (ep_bufs) {
+        const size_t xb = sizeof(float) * (size_t)T * L->desc.d_model;
+        if (x != L->x) QRM_CUDA(cudaMemcpyAsync(L->x, x, xb, cudaMemcpyDeviceToDevice, s));
+        x = L->x;
+        out = L->out;
+        idx = L->topk_idx;
+        w = L->topk_w;
+    }
+    qrm_layer::GraphKey key{T, flags, L->profiling ? 1 : 0};
+    const void* ptrs[4] = {x, out, idx, w};
     auto it = L->graphs.find(key);
-    if (it == L->graphs.end()) {
-        if (L->graphs.size() >= 32) clear_graphs(L);
+    const bool same = it != L->graphs.end() && std::equal(ptrs, ptrs + 4, it->second.ptrs);
+    if (!same) {
         QRM_CUDA(cudaStreamBeginCapture(L->stream, cudaStreamCaptureModeThreadLocal));
         int rc = launch_forward(L, x, T, flags, out, idx, w, L->stream);
         cudaGraph_t g = nullptr;
@@ -1098,15 +1131,41 @@ static int run_forward(qrm_layer* L, const float* x, int T, int flags, float* ou
             return rc;
         }
         if (ce != cudaSuccess) return fail(QRM_E_CUDA, "graph capture: %s", cudaGetErrorString(ce));
-        cudaGraphExec_t ex = nullptr;
-        ce = cudaGraphInstantiate(&ex, g, 0);
+        bool updated = false;
+        if (it != L->graphs.end()) {
+            cudaGraphExecUpdateResultInfo info;
+            updated = cudaGraphExecUpdate(it->second.exec, g, &info) == cudaSuccess;
+            if (!updated) {
+                cudaGetLastError();   // clear the update failure; instantiate instead
+                cudaGraphExecDestroy(it->second.exec);
+                L->graphs.erase(it);
+                it = L->graphs.end();
+            }
+        }
+        if (!updated) {
+            if (L->graphs.size() >= 32) clear_graphs(L);
+            cudaGraphExec_t ex = nullptr;
+            ce = cudaGraphInstantiate(&ex, g, 0);
+            if (ce != cudaSuccess) {
+                cudaGraphDestroy(g);
+                return fail(QRM_E_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
+            }
+            it = L->graphs.emplace(key, qrm_layer::Graph{}).first;
+            it->second.exec = ex;
+        }
         cudaGraphDestroy(g);
-        if (ce != cudaSuccess) return fail(QRM_E_CUDA, "graph instantiate: %s", cudaGetErrorString(ce));
-        it = L->graphs.emplace(key, std::make_pair(ex, L->last_launches)).first;
+        it->second.launches = L->last_launches;
+        std::copy(ptrs, ptrs + 4, it->second.ptrs);
     }
-    QRM_CUDA(cudaGraphLaunch(it->second.first, s));
+    QRM_CUDA(cudaGraphLaunch(it->second.exec, s));
+    if (ep_bufs) {
+        const size_t xb = sizeof(float) * (size_t)T * L->desc.d_model, kb = (size_t)T * L->k;
+        if (user_out != out) QRM_CUDA(cudaMemcpyAsync(user_out, out, xb, cudaMemcpyDeviceToDevice, s));
+        if (user_idx != idx) QRM_CUDA(cudaMemcpyAsync(user_idx, idx, sizeof(int32_t) * kb, cudaMemcpyDeviceToDevice, s));
+        if (user_w != w) QRM_CUDA(cudaMemcpyAsync(user_w, w, sizeof(float) * kb, cudaMemcpyDeviceToDevice, s));
+    }
     L->last_T = T;
-    L->last_launches = it->second.second;
+    L->last_launches = it->second.launches;
     L->profiled_last = L->profiling;
     L->last_xn = (T > qrm::route_small_max_tokens(L->desc.d_model) && !(flags & QRM_APPLY_NORM)) ? x : L->xn;
     return QRM_OK;
