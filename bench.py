@@ -384,8 +384,12 @@ def run_ours(args, rank, world, dist):
         roof_kernel = "whole layer step per rank (expert parallel: no per-stage events)"
     layer_gbs = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
 
+    # the library counts the kernel launches of its forward (one graph replay)
+    launches_per_step = layer.last_launch_count()
+    transport = layer.ep_transport()
+    # an expert-parallel layer's close is collective: every rank closes here
+    layer.close()
     if rank != 0:
-        layer.close()
         return 0
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -394,8 +398,6 @@ def run_ours(args, rank, world, dist):
             cpu = dict(value=v, unit="tokens/s", cores=cores, kind="port", sample=desc)
         except Exception as ex:  # the baseline must never block the GPU number
             cpu = dict(value=None, unit="tokens/s", cores=None, kind="port", sample=f"failed: {ex}")
-    # the library counts the kernel launches of its forward (one graph replay)
-    launches_per_step = layer.last_launch_count()
     line = dict(
         metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
@@ -403,7 +405,7 @@ def run_ours(args, rank, world, dist):
         config=dict(workload=WORKLOAD["name"], tokens_per_rank=T, d_model=d, n_experts=W["n_experts"],
                     top_k=W["n_active"], expert_ffn=W["expert_ffn"], formats="routed Q4_K, shared Q8_0",
                     l2="flushed before every step (256 MiB write, outside the timed events)",
-                    parallelism="single GPU" if world == 1 else f"ep{world} (expert parallel, NCCL)"),
+                    parallelism="single GPU" if world == 1 else f"ep{world} (expert parallel, {transport} exchanges)"),
         roofline=dict(bound="hbm", kernel=roof_kernel, achieved=achieved,
                       peak=peak, unit="GB/s", frac=achieved / peak if peak else None, peak_kind=peak_kind,
                       traffic=traffic),

@@ -188,18 +188,30 @@ int  qrm_matrix_gemv_static(qrm_matrix* m, const float* x_dev, int T, float* y_d
  * [r*E/world, (r+1)*E/world) (qrm_expert_range; uploads of other experts fail
  * with QRM_E_INVALID) and replicas of norm, router and shared expert.  Every
  * rank calls qrm_forward / qrm_forward_device with the same T for its own
- * tokens; the forward routes them (bit-identical on every rank), all-gathers
- * the normalised tokens with their top-k over NCCL, runs the local experts for
- * all ranks' tokens, returns the expert outputs to the token owners (grouped
- * send/recv) and combines on the owner in slot order, so the output equals the
- * single-GPU forward bit for bit.  The id comes from qrm_nccl_unique_id on one
- * rank and is passed to every rank by the host (128 bytes); qrm_create_ep
- * returns once all ranks have joined.  Per-stage profiling is single-GPU
- * only. */
+ * tokens, the same number of times; the forward routes them (bit-identical on
+ * every rank), gathers the normalised tokens with their top-k on every rank,
+ * runs the local experts for all ranks' tokens, returns the expert outputs to
+ * the token owners and combines on the owner in slot order, so the output
+ * equals the single-GPU forward bit for bit.  The exchanges are stores into
+ * the peers' memory over NVLink (CUDA IPC mappings made at creation) when
+ * every rank can map every other rank's memory, else NCCL all-gather and
+ * grouped send/recv (QRM_EP_P2P=0 in the environment forces NCCL); a peer
+ * that does not deliver within about a second makes qrm_sync return
+ * QRM_E_TIMEOUT, after which the layer should be destroyed.  The id comes
+ * from qrm_nccl_unique_id on one rank and is passed to every rank by the host
+ * (128 bytes); qrm_create_ep returns once all ranks have joined, and
+ * qrm_destroy of an expert-parallel layer is collective (it waits up to ~10 s
+ * for the other ranks).  Per-stage profiling is single-GPU only. */
 #define QRM_NCCL_ID_BYTES 128
 int qrm_nccl_unique_id(void* id_out);
 int qrm_create_ep(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out);
 int qrm_expert_range(qrm_layer* layer, int* first, int* count);
+/* How the layer exchanges tokens and outputs: 0 single GPU, 1 NCCL, 2 peer
+ * memory (NVLink stores). */
+#define QRM_EP_SINGLE 0
+#define QRM_EP_NCCL 1
+#define QRM_EP_PEER 2
+int qrm_ep_transport(qrm_layer* layer, int* transport);
 
 /* ---- synthetic weights on the device (the reference's `synthesize`,
  * src/QuantRunner.Cli/Program.cs:247-369) ----

@@ -105,6 +105,7 @@ _SIGS = {
     "qrm_nccl_unique_id": (C.c_int, [P]),
     "qrm_create_ep": (C.c_int, [C.POINTER(LayerDesc), C.c_int, C.c_int, P, C.POINTER(P)]),
     "qrm_expert_range": (C.c_int, [P, P, P]),
+    "qrm_ep_transport": (C.c_int, [P, P]),
     "qrm_synth_gaussian": (C.c_int, [P, C.c_int64, C.c_uint64, C.c_float, P]),
     "qrm_synth_quantize": (C.c_int, [C.c_int, P, C.c_int64, P, P]),
 }
@@ -186,6 +187,12 @@ class MoeLayer:
         a, b = C.c_int(0), C.c_int(0)
         _check(lib().qrm_expert_range(self._h, C.byref(a), C.byref(b)))
         return a.value, b.value
+
+    def ep_transport(self):
+        """"single", "nccl" or "peer" (NVLink stores into the peers' memory)."""
+        v = C.c_int(0)
+        _check(lib().qrm_ep_transport(self._h, C.byref(v)))
+        return ("single", "nccl", "peer")[v.value]
 
     def close(self):
         if getattr(self, "_h", None):

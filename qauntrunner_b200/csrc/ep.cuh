@@ -14,10 +14,133 @@
 //   output block for owner q: [T*k][d] rows, row t*k+j = expert output of q's
 //   token t, slot j (only the rows whose expert this rank holds are written;
 //   the owner reads exactly those).
+//
+// Peer-memory mode (NVLink through NVSwitch, the default when every rank can
+// map every other rank's memory): each rank owns one "mailbox" allocation,
+// mapped into every peer's address space.  A sender stores its normalised
+// tokens and top-k indices straight into the gathered-token arrays of every
+// peer, and its expert output rows straight into each owner's receive blocks,
+// then raises a per-sender flag in the receiver's mailbox to the forward's
+// epoch; the receiving kernels (dispatch, combine) wait for the flags of all
+// senders.  The epoch is a per-rank counter in device memory (dispatch
+// advances it), so captured CUDA graphs replay correctly.  Every wait is
+// bounded: on expiry the kernel sets ERR_TIMEOUT and carries on over the
+// stale (in-bounds) contents; qrm_sync reports the error.
+//
+// Buffer reuse needs no extra handshake: a sender writes forward N+1's
+// records into a peer only after its combine of forward N has seen that
+// peer's outputs of forward N, which the peer pushed after its expert kernels
+// finished reading forward N's records; and it writes forward N+1's outputs
+// only after its dispatch has seen the owner's forward N+1 records, which the
+// owner sent after its combine of forward N was done with the receive blocks.
 #pragma once
 #include "common.cuh"
 
 namespace qrm {
+
+// Byte offsets inside every rank's mailbox (identical on all ranks).
+struct EpMailbox {
+    long long rec_flag;   // u32 [G]: epoch of the records received from rank q
+    long long out_flag;   // u32 [G]: epoch of the output rows received from rank q
+    long long xn;         // f32 [G*T][d] gathered normalised tokens
+    long long idx;        // i32 [G*T][k] gathered top-k indices
+    long long y;          // f32 [G][T*k][d] output rows of this rank's tokens, per holder
+};
+
+struct EpPeers {
+    const unsigned long long* base;  // [G] mailbox of each rank, mapped here (own: local)
+    EpMailbox mb;
+    uint32_t* epoch;      // this rank's forward counter
+    uint32_t* cnt;        // [2][G] finished sender blocks per destination (zero between launches)
+    int32_t* err;         // ERR_* flags
+    int G, rank;
+};
+
+constexpr long long kEpSpinLimit = 1ll << 22;   // polls; with the back-off below about 1-2 s
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Waits until *flag has reached `want` (epochs only grow; wrap-safe compare).
+// Returns false when the wait gave up.
+__device__ inline bool ep_wait_flag(const uint32_t* flag, uint32_t want) {
+    for (long long i = 0; i < kEpSpinLimit; i++) {
+        if ((int32_t)(ld_acquire_sys(flag) - want) >= 0) return true;
+        if (i >= 256) __nanosleep(256);
+    }
+    return false;
+}
+
+// The calling block's stores to rank q are complete: the last of the `nb`
+// blocks writing to q raises q's flag `which` (0 records, 1 outputs) for
+// this rank to `epoch`.  Cumulative fences order the other blocks' stores
+// (observed through the counter) before the flag.
+__device__ inline void ep_signal(const EpPeers& p, int which, int q, uint32_t epoch, int nb) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        bool last = true;
+        if (nb > 1) {
+            uint32_t* c = p.cnt + which * p.G + q;
+            last = atomicAdd(c, 1u) == (uint32_t)(nb - 1);
+            if (last) {
+                *c = 0;
+                __threadfence_system();
+            }
+        }
+        if (last) {
+            char* mb = reinterpret_cast<char*>(p.base[q]);
+            uint32_t* flags = reinterpret_cast<uint32_t*>(mb + (which ? p.mb.out_flag : p.mb.rec_flag));
+            st_release_sys(flags + p.rank, epoch);
+        }
+    }
+}
+
+// Records of this rank's T tokens into every rank's gathered arrays, rows
+// [rank*T, rank*T + T).  Grid: G*nb blocks, nb per destination.
+__global__ void ep_push_records_kernel(const float* __restrict__ xn, const int32_t* __restrict__ idx, int T, int d,
+                                       int k, EpPeers p) {
+    const int nb = gridDim.x / p.G, q = blockIdx.x / nb, part = blockIdx.x - q * nb;
+    const uint32_t epoch = *p.epoch + 1;
+    char* mb = reinterpret_cast<char*>(p.base[q]);
+    const int d4 = d / 4;
+    float4* dx = reinterpret_cast<float4*>(mb + p.mb.xn) + (size_t)p.rank * T * d4;
+    const float4* sx = reinterpret_cast<const float4*>(xn);
+    for (int i = part * blockDim.x + threadIdx.x; i < T * d4; i += nb * blockDim.x) dx[i] = sx[i];
+    int32_t* di = reinterpret_cast<int32_t*>(mb + p.mb.idx) + (size_t)p.rank * T * k;
+    for (int i = part * blockDim.x + threadIdx.x; i < T * k; i += nb * blockDim.x) di[i] = idx[i];
+    ep_signal(p, 0, q, epoch, nb);
+}
+
+// Output rows of the local experts straight into the owners' receive blocks:
+// gathered assignment a = (owner q, local assignment i) -> owner q's block of
+// holder `rank`, row i.  Grid: G*nb blocks, nb per owner.
+__global__ void ep_push_outputs_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm,
+                                       const int32_t* __restrict__ idx_all, int T, int k, int d, int first,
+                                       int n_local, EpPeers p) {
+    const int nb = gridDim.x / p.G, q = blockIdx.x / nb, part = blockIdx.x - q * nb;
+    const uint32_t epoch = *p.epoch;   // advanced by this forward's dispatch
+    char* mb = reinterpret_cast<char*>(p.base[q]);
+    const int d4 = d / 4, rows = T * k;
+    float4* dst = reinterpret_cast<float4*>(mb + p.mb.y) + (size_t)p.rank * rows * d4;
+    const float4* src = reinterpret_cast<const float4*>(y);
+    const int32_t* ia = idx_all + (size_t)q * rows;
+    const int32_t* pa = inv_perm + (size_t)q * rows;
+    for (int i = part * blockDim.x + threadIdx.x; i < rows * d4; i += nb * blockDim.x) {
+        const int r = i / d4, c = i - r * d4;
+        const int e = ia[r];
+        if (e < first || e >= first + n_local) continue;
+        dst[i] = src[(size_t)pa[r] * d4 + c];
+    }
+    ep_signal(p, 1, q, epoch, nb);
+}
 
 __global__ void ep_pack_records_kernel(const float* __restrict__ xn, const int32_t* __restrict__ idx,
                                        const float* __restrict__ w, int T, int d, int k, float* __restrict__ rec) {
@@ -67,9 +190,17 @@ __global__ void ep_pack_outputs_kernel(const float* __restrict__ y, const int32_
 // w_{k-1} y_{k-1} (+ shared), each product and sum rounded separately
 // (combine_kernel's arithmetic); y_j comes from the block of the rank that
 // holds expert idx[t][j] (experts per rank: epr).
+// In peer-memory mode (`wait_flags` set) every block first waits for the
+// output flags of all G holders.
 __global__ void ep_combine_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                   const int32_t* __restrict__ idx, const float* __restrict__ recv,
-                                  const float* __restrict__ ys, int T, int k, int d, int epr, float* __restrict__ out) {
+                                  const float* __restrict__ ys, int T, int k, int d, int epr, float* __restrict__ out,
+                                  const uint32_t* wait_flags, const uint32_t* epoch, int G, int32_t* err) {
+    if (wait_flags) {
+        const uint32_t want = *epoch;
+        if ((int)threadIdx.x < G && !ep_wait_flag(wait_flags + threadIdx.x, want)) atomicOr(err, (int32_t)ERR_TIMEOUT);
+        __syncthreads();
+    }
     const int d4 = d / 4;
     const long long total = (long long)T * d4;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;

@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <ctime>
 #include <string>
 #include <utility>
 #include <vector>
@@ -431,6 +432,15 @@ struct qrm_layer {
     int32_t* idx_all = nullptr;   // [world*T][k]
     float* ysend = nullptr;       // [world][T*k][d] output rows per owner
     float* yrecv = nullptr;       // [world][T*k][d] rows of this rank's tokens, per holder
+    // xn_all, idx_all and yrecv live in this rank's mailbox; in peer-memory
+    // mode every rank maps every other rank's mailbox and writes into it
+    char* mbox = nullptr;
+    qrm::EpMailbox mb{};
+    bool p2p = false;
+    std::vector<void*> peer_open;             // mapped peer mailboxes
+    unsigned long long* peer_base = nullptr;  // device [world]: mailbox of each rank
+    uint32_t* ep_state = nullptr;             // device: epoch, block counters [2][world]
+    char* xch = nullptr;                      // device [world][128]: set-up exchange, barrier
     bool shared_enabled = false;        // GLM layer with n_shared > 0
     int sm_count = 0;
     cudaStream_t stream = nullptr;
@@ -488,22 +498,51 @@ static void clear_graphs(qrm_layer* L) {
     L->graphs.clear();
 }
 
+// All ranks of an expert-parallel layer meet here (qrm_destroy is collective).
+// Bounded: false when a rank did not arrive within ~10 s.
+static bool ep_barrier(qrm_layer* L) {
+    if (ncclAllReduce(L->xch, L->xch, 1, ncclInt32, ncclSum, L->comm, L->stream) != ncclSuccess) return false;
+    for (int i = 0; i < 10000; i++) {
+        cudaError_t e = cudaStreamQuery(L->stream);
+        if (e == cudaSuccess) return true;
+        if (e != cudaErrorNotReady) return false;
+        struct timespec ts{0, 1000000};
+        nanosleep(&ts, nullptr);
+    }
+    return false;
+}
+
 static void free_layer(qrm_layer* L) {
     if (!L) return;
     cudaSetDevice(L->desc.device);
     if (L->stream) cudaStreamSynchronize(L->stream);
+    bool met = true;
+    if (L->p2p) {
+        // no peer writes into this mailbox once every rank is here
+        met = ep_barrier(L);
+        for (void* p : L->peer_open) cudaIpcCloseMemHandle(p);
+        L->peer_open.clear();
+    }
+    // a peer that may still write into it keeps the mailbox (leaked, not freed)
+    if (L->mbox && met) cudaFree(L->mbox);
+    L->xn_all = nullptr;
+    L->idx_all = nullptr;
+    L->yrecv = nullptr;
     void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_lm, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
                     L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn,
                     L->part_buf, L->part_ctr, L->pos_tok, L->tile_ctr, L->slot_info, L->qgrp_ctr,
-                    L->rec_own, L->rec_all, L->xn_all, L->idx_all, L->ysend, L->yrecv};
+                    L->rec_own, L->rec_all, L->ysend, L->peer_base, L->ep_state, L->xch};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     clear_graphs(L);
     for (cudaEvent_t e : L->ev)
         if (e) cudaEventDestroy(e);
     if (L->stream) cudaStreamDestroy(L->stream);
-    if (L->comm) ncclCommDestroy(L->comm);
+    if (L->comm) {
+        if (met) ncclCommDestroy(L->comm);
+        else ncclCommAbort(L->comm);
+    }
     delete L;
 }
 
@@ -594,10 +633,94 @@ extern "C" int qrm_create_ep(const qrm_layer_desc* desc, int rank, int world, co
     return create_layer(desc, rank, world, nccl_id, out);
 }
 
+extern "C" int qrm_ep_transport(qrm_layer* L, int* transport) {
+    if (!L || !transport) return fail(QRM_E_INVALID, "NULL argument");
+    *transport = L->world == 1 ? QRM_EP_SINGLE : (L->p2p ? QRM_EP_PEER : QRM_EP_NCCL);
+    return QRM_OK;
+}
+
 extern "C" int qrm_expert_range(qrm_layer* L, int* first, int* count) {
     if (!L || !first || !count) return fail(QRM_E_INVALID, "NULL argument");
     *first = L->first_expert;
     *count = L->n_local;
+    return QRM_OK;
+}
+
+bool ep_p2p_requested() {
+    const char* v = getenv("QRM_EP_P2P");
+    return !(v && v[0] == '0');
+}
+
+// Every rank gathers every rank's 128-byte record through the layer's NCCL
+// communicator (in place in L->xch) and copies the records to `all`.
+static int ep_allgather128(qrm_layer* L, const void* mine, std::vector<char>& all) {
+    const int G = L->world;
+    QRM_CUDA(cudaMemcpy(L->xch + 128 * L->rank, mine, 128, cudaMemcpyHostToDevice));
+    QRM_NCCL(ncclAllGather(L->xch + 128 * L->rank, L->xch, 128, ncclUint8, L->comm, L->stream));
+    QRM_CUDA(cudaStreamSynchronize(L->stream));
+    all.resize((size_t)128 * G);
+    QRM_CUDA(cudaMemcpy(all.data(), L->xch, (size_t)128 * G, cudaMemcpyDeviceToHost));
+    return QRM_OK;
+}
+
+// Peer-memory mode: map every other rank's mailbox (CUDA IPC; NVLink peer
+// access) when all ranks can, else keep the NCCL exchanges.  All ranks take
+// the same decision.
+static int ep_open_peers(qrm_layer* L) {
+    const int G = L->world;
+    char mine[128] = {};
+    int ok = ep_p2p_requested() ? 1 : 0;
+    cudaIpcMemHandle_t h{};
+    static_assert(sizeof(cudaIpcMemHandle_t) <= 120, "IPC handle size");
+    if (ok && cudaIpcGetMemHandle(&h, L->mbox) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+    }
+    memcpy(mine, &h, sizeof h);
+    memcpy(mine + 120, &ok, sizeof ok);
+    std::vector<char> all;
+    int rc = ep_allgather128(L, mine, all);
+    if (rc) return rc;
+    int all_ok = 1;
+    for (int q = 0; q < G; q++) {
+        int v;
+        memcpy(&v, all.data() + 128 * q + 120, sizeof v);
+        all_ok &= v;
+    }
+    std::vector<unsigned long long> base(G, 0);
+    base[L->rank] = (unsigned long long)L->mbox;
+    int opened = all_ok;
+    for (int q = 0; q < G && opened; q++) {
+        if (q == L->rank) continue;
+        cudaIpcMemHandle_t hq;
+        memcpy(&hq, all.data() + 128 * q, sizeof hq);
+        void* ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, hq, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            opened = 0;
+            break;
+        }
+        L->peer_open.push_back(ptr);
+        base[q] = (unsigned long long)ptr;
+    }
+    // second round: every rank mapped every peer
+    memset(mine, 0, sizeof mine);
+    memcpy(mine, &opened, sizeof opened);
+    rc = ep_allgather128(L, mine, all);
+    if (rc) return rc;
+    int every = 1;
+    for (int q = 0; q < G; q++) {
+        int v;
+        memcpy(&v, all.data() + 128 * q, sizeof v);
+        every &= v;
+    }
+    if (!every) {
+        for (void* p : L->peer_open) cudaIpcCloseMemHandle(p);
+        L->peer_open.clear();
+        return QRM_OK;
+    }
+    QRM_CUDA(cudaMemcpy(L->peer_base, base.data(), sizeof(unsigned long long) * G, cudaMemcpyHostToDevice));
+    L->p2p = true;
     return QRM_OK;
 }
 
@@ -668,17 +791,35 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
     L->cap_T = desc->max_tokens;
     if (world > 1) {
         const size_t T = desc->max_tokens, G = world, k = L->k;
+        auto up = [](size_t b) { return (b + 255) / 256 * 256; };
+        L->mb.rec_flag = 0;
+        L->mb.out_flag = (long long)(4 * G);
+        L->mb.xn = (long long)up(8 * G);
+        L->mb.idx = L->mb.xn + (long long)up(sizeof(float) * G * T * d);
+        L->mb.y = L->mb.idx + (long long)up(sizeof(int32_t) * G * T * k);
+        const size_t mbox_bytes = (size_t)L->mb.y + sizeof(float) * G * T * k * d;
         if (cudaMalloc(&L->rec_own, sizeof(float) * T * (d + 2 * k)) != cudaSuccess ||
             cudaMalloc(&L->rec_all, sizeof(float) * G * T * (d + 2 * k)) != cudaSuccess ||
-            cudaMalloc(&L->xn_all, sizeof(float) * G * T * d) != cudaSuccess ||
-            cudaMalloc(&L->idx_all, sizeof(int32_t) * G * T * k) != cudaSuccess ||
             cudaMalloc(&L->ysend, sizeof(float) * G * T * k * d) != cudaSuccess ||
-            cudaMalloc(&L->yrecv, sizeof(float) * G * T * k * d) != cudaSuccess)
+            cudaMalloc(&L->mbox, mbox_bytes) != cudaSuccess ||
+            cudaMalloc(&L->peer_base, sizeof(unsigned long long) * G) != cudaSuccess ||
+            cudaMalloc(&L->ep_state, sizeof(uint32_t) * (1 + 2 * G)) != cudaSuccess ||
+            cudaMalloc(&L->xch, 128 * G) != cudaSuccess)
             return bail(fail(QRM_E_NOMEM, "expert-parallel buffers"));
+        L->xn_all = reinterpret_cast<float*>(L->mbox + L->mb.xn);
+        L->idx_all = reinterpret_cast<int32_t*>(L->mbox + L->mb.idx);
+        L->yrecv = reinterpret_cast<float*>(L->mbox + L->mb.y);
+        // flags and counters start at zero before any peer can see the mailbox
+        if (cudaMemset(L->mbox, 0, mbox_bytes) != cudaSuccess ||
+            cudaMemset(L->ep_state, 0, sizeof(uint32_t) * (1 + 2 * G)) != cudaSuccess ||
+            cudaMemset(L->xch, 0, 128 * G) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
+            return bail(fail(QRM_E_CUDA, "expert-parallel buffer initialisation"));
         ncclUniqueId id;
         memcpy(&id, nccl_id, sizeof id);
         ncclResult_t nr = ncclCommInitRank(&L->comm, world, id, rank);
         if (nr != ncclSuccess) return bail(fail(QRM_E_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(nr)));
+        rc = ep_open_peers(L);
+        if (rc) return bail(rc);
     }
     // kernels with large dynamic shared memory
     if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
@@ -828,6 +969,18 @@ static int forward_checks(qrm_layer* L, int T, int flags) {
     return QRM_OK;
 }
 
+static qrm::EpPeers ep_peers(const qrm_layer* L) {
+    qrm::EpPeers p{};
+    p.base = L->peer_base;
+    p.mb = L->mb;
+    p.epoch = L->ep_state;
+    p.cnt = L->ep_state + 1;
+    p.err = &L->sched->err;
+    p.G = L->world;
+    p.rank = L->rank;
+    return p;
+}
+
 static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* topk_idx,
                           float* topk_w, cudaStream_t s) {
     const qrm_layer_desc& D = L->desc;
@@ -894,6 +1047,23 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const float* xs = xn;
     if (ep) {
         if (prof) return fail(QRM_E_STATE, "per-stage profiling is single-GPU only");
+        Tx = G * T;
+        xs = L->xn_all;
+    }
+    if (ep && L->p2p) {
+        // records straight into every rank's mailbox; the dispatch waits for all of them
+        const qrm::EpPeers pe = ep_peers(L);
+        const int nb = (int)std::min<long long>(((long long)T * d / 4 + 1023) / 1024, 16);
+        qrm::ep_push_records_kernel<<<G * nb, 256, 0, s>>>(xn, topk_idx, T, d, k, pe);
+        QRM_CUDA(cudaGetLastError());
+        qrm::TopkParams tpx{L->logits, nullptr, L->idx_all, nullptr, Tx, E, k, 0, 1.f};
+        qrm::DispatchParams dpx{L->idx_all, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched,
+                                Tx, k, E, L->first_expert, L->n_local, shared ? 1 : 0,
+                                reinterpret_cast<const uint32_t*>(L->mbox + L->mb.rec_flag), L->ep_state, G};
+        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, Tx, false), s>>>(dpx, tpx, 0);
+        QRM_CUDA(cudaGetLastError());
+        nl += 2;
+    } else if (ep) {
         // (normalised token, top-k) records of every rank
         const int W = d + 2 * k;
         const long long nrec = (long long)T * W;
@@ -901,7 +1071,6 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         qrm::ep_pack_records_kernel<<<grid, 256, 0, s>>>(xn, topk_idx, topk_w, T, d, k, L->rec_own);
         QRM_CUDA(cudaGetLastError());
         QRM_NCCL(ncclAllGather(L->rec_own, L->rec_all, (size_t)nrec, ncclFloat32, L->comm, s));
-        Tx = G * T;
         grid = (int)std::min<long long>(((long long)Tx * (d + k) + 255) / 256, (long long)L->sm_count * 8);
         qrm::ep_unpack_records_kernel<<<grid, 256, 0, s>>>(L->rec_all, Tx, d, k, L->xn_all, L->idx_all);
         QRM_CUDA(cudaGetLastError());
@@ -912,7 +1081,6 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, Tx, false), s>>>(dpx, tpx, 0);
         QRM_CUDA(cudaGetLastError());
         nl += 3;
-        xs = L->xn_all;
     }
     // 4. gate/up (+ SwiGLU) and 5. down
     const int nt = pick_nt(Tx);
@@ -1050,7 +1218,25 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         }
         mark(gu ? 4 : 5);
     }
-    if (ep) {
+    if (ep && L->p2p) {
+        // expert output rows straight into the owners' mailboxes; the owner
+        // combines in slot order once every holder's rows are in
+        const qrm::EpPeers pe = ep_peers(L);
+        const int nb = (int)std::min<long long>(((long long)T * k * d / 4 + 2047) / 2048, 32);
+        qrm::ep_push_outputs_kernel<<<G * nb, 256, 0, s>>>(L->y, L->inv_perm, L->idx_all, T, k, d, L->first_expert,
+                                                           L->n_local, pe);
+        QRM_CUDA(cudaGetLastError());
+        const long long m4 = (long long)T * (d / 4);
+        const int grid = (int)std::min<long long>((m4 + 255) / 256, (long long)L->sm_count * 16);
+        qrm::ep_combine_kernel<<<grid, 256, 0, s>>>((flags & QRM_ADD_RESIDUAL) ? x : nullptr, topk_w, topk_idx, L->yrecv,
+                                                    shared ? L->ys + (size_t)L->rank * T * d : nullptr, T, k, d,
+                                                    E / G, out,
+                                                    reinterpret_cast<const uint32_t*>(L->mbox + L->mb.out_flag),
+                                                    L->ep_state, G, &L->sched->err);
+        QRM_CUDA(cudaGetLastError());
+        nl += 2;
+        combined = true;
+    } else if (ep) {
         // expert output rows back to the token owners; the owner combines in slot order
         const long long n4 = (long long)Tx * k * (d / 4);
         int grid = (int)std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 16);
@@ -1068,7 +1254,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         grid = (int)std::min<long long>((m4 + 255) / 256, (long long)L->sm_count * 16);
         qrm::ep_combine_kernel<<<grid, 256, 0, s>>>((flags & QRM_ADD_RESIDUAL) ? x : nullptr, topk_w, topk_idx, L->yrecv,
                                                     shared ? L->ys + (size_t)L->rank * T * d : nullptr, T, k, d,
-                                                    E / G, out);
+                                                    E / G, out, nullptr, nullptr, 0, nullptr);
         QRM_CUDA(cudaGetLastError());
         nl += 2;
         combined = true;

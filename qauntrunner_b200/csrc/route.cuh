@@ -16,6 +16,7 @@
 #pragma once
 #include "common.cuh"
 #include "gemv_tma.cuh"
+#include "ep.cuh"
 #include "glibc_expf.cuh"
 
 namespace qrm {
@@ -462,6 +463,11 @@ struct DispatchParams {
     int T, k, E;
     int first_expert, n_local;  // local expert window (EP); full range otherwise
     int has_shared;
+    // expert parallelism over peer memory: wait for the records of all ep_G
+    // ranks (flags reach this rank's epoch + 1), then advance the epoch
+    const uint32_t* ep_flags; // [ep_G] or null
+    uint32_t* ep_epoch;
+    int ep_G;
 };
 
 constexpr int kDispatchThreads = 1024;
@@ -477,7 +483,19 @@ inline size_t dispatch_smem(int E, int T, bool fused) {
 // runs the top-k of every token (one warp each).
 __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchParams p, TopkParams tp, int fused) {
     extern __shared__ __align__(16) int dsm[];
-    const int E = p.E, n = p.T * p.k;
+    const int E = p.E;
+    int n = p.T * p.k;
+    if (p.ep_flags) {
+        const uint32_t want = *p.ep_epoch + 1;
+        bool ok = true;
+        if ((int)threadIdx.x < p.ep_G) ok = ep_wait_flag(p.ep_flags + threadIdx.x, want);
+        // a rank that never delivered: no routed assignments (error flagged)
+        if (__syncthreads_or(!ok)) {
+            if (threadIdx.x == 0) atomicOr(&p.sched->err, (int)ERR_TIMEOUT);
+            n = 0;
+        }
+        if (threadIdx.x == 0) *p.ep_epoch = want;
+    }
     int* cnt = dsm;                  // [E+1]
     int* base = cnt + (E + 1);       // [E+1]
     int* wc = base + (E + 1);        // [32][E]

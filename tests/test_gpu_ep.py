@@ -1,7 +1,9 @@
 """Expert parallelism on 2 GPUs: each rank holds half of the routed experts;
-its forward (own tokens; NCCL all-gather and send/recv inside the library)
-must equal a single-GPU layer holding every expert on the same tokens, bit for
-bit, and the routing must be identical.  Skipped with fewer than 2 GPUs."""
+its forward (own tokens; the exchanges inside the library, as NVLink stores
+into the peer's memory or as NCCL all-gather and send/recv) must equal a
+single-GPU layer holding every expert on the same tokens, bit for bit, and the
+routing must be identical, over several consecutive forwards (the peer-memory
+flags advance per forward).  Skipped with fewer than 2 GPUs."""
 import numpy as np
 import pytest
 
@@ -17,8 +19,10 @@ def _gpus():
     return torch.cuda.device_count()
 
 
-def _rank(rank, nccl_id, cfgname, over, T, q):
+def _rank(rank, nccl_id, cfgname, over, T, transport, q):
+    import os
     import torch
+    os.environ["QRM_EP_P2P"] = "1" if transport == "peer" else "0"
     from tests.gpu_helpers import make_layer
     from tests.moe_case import make_case, make_input
     try:
@@ -28,13 +32,15 @@ def _rank(rank, nccl_id, cfgname, over, T, q):
         x = np.ascontiguousarray(x_all[rank * T:(rank + 1) * T])
         ep = make_layer(case, max_tokens=T, device=rank, rank=rank, world=WORLD, nccl_id=nccl_id)
         single = make_layer(case, max_tokens=WORLD * T, device=rank)
+        assert ep.ep_transport() == transport, ep.ep_transport()
         res = []
-        for flags in (Q.APPLY_NORM, Q.APPLY_NORM | Q.ADD_RESIDUAL):
+        for flags in (Q.APPLY_NORM, Q.APPLY_NORM | Q.ADD_RESIDUAL, Q.APPLY_NORM, Q.APPLY_NORM):
             out, idx, w = ep.forward(x, apply_norm=True, add_residual=bool(flags & Q.ADD_RESIDUAL))
             ro, ri, rw = single.forward(x_all, apply_norm=True, add_residual=bool(flags & Q.ADD_RESIDUAL))
             sl = slice(rank * T, (rank + 1) * T)
             res.append((bool(np.array_equal(idx, ri[sl])), bool(np.array_equal(w, rw[sl])),
                         bool(np.array_equal(out, ro[sl])), float(np.max(np.abs(out - ro[sl])))))
+        ep.sync()
         ep.close()
         single.close()
         q.put((rank, res, None))
@@ -42,12 +48,13 @@ def _rank(rank, nccl_id, cfgname, over, T, q):
         q.put((rank, None, repr(ex)))
 
 
+@pytest.mark.parametrize("transport", ["peer", "nccl"])
 @pytest.mark.parametrize("cfgname,over,T", [
     ("c5", dict(d_model=1024, expert_ffn=512, n_experts=16, n_active=4), 1),
     ("c5", dict(d_model=1024, expert_ffn=512, n_experts=16, n_active=4), 3),
     ("c1", dict(n_experts=8), 2),
 ])
-def test_ep_equals_single_gpu(cfgname, over, T):
+def test_ep_equals_single_gpu(cfgname, over, T, transport):
     if _gpus() < WORLD:
         pytest.skip("needs 2 GPUs")
     import queue
@@ -56,7 +63,7 @@ def test_ep_equals_single_gpu(cfgname, over, T):
     nid = Q.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, nid, cfgname, over, T, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_rank, args=(r, nid, cfgname, over, T, transport, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res, t0 = [], time.time()
