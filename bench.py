@@ -271,11 +271,21 @@ def run_ours(args, rank, world, dist):
     def step(i):
         layer.forward_device(xs[i].data_ptr(), T, out.data_ptr(), flags, idx.data_ptr(), wts.data_ptr(), sp)
 
+    # expert parallel: the ranks' forwards wait for one another, so every rank
+    # leaves the L2 flush together (a one-element all-reduce on the stream,
+    # outside the timed events) and no rank's step absorbs another's flush
+    sync_buf = torch.zeros(1, device=f"cuda:{dev}") if world > 1 else None
+
+    def flush_l2(i):
+        flush.fill_(float(i))
+        if sync_buf is not None:
+            dist.all_reduce(sync_buf)
+
     with torch.cuda.stream(stream):
         for prof in ((False, True) if world == 1 else (False,)):   # capture the forward graphs before timing
             layer.set_profiling(prof)
             for i in range(args.warmup):
-                flush.fill_(float(i))
+                flush_l2(i)
                 step(i)
     torch.cuda.synchronize()
     layer.sync()
@@ -295,7 +305,7 @@ def run_ours(args, rank, world, dist):
     clocks.start()
     with torch.cuda.stream(stream):
         for i in range(args.steps):
-            flush.fill_(float(i))
+            flush_l2(i)
             ev0[i].record(stream)
             step(args.warmup + i)
             ev1[i].record(stream)
@@ -339,7 +349,7 @@ def run_ours(args, rank, world, dist):
         if dist:
             dist.barrier()
         for i in range(args.steps):
-            flush.fill_(float(i))
+            flush_l2(i)
             e0[i].record(stream)
             xd.copy_(xh[args.warmup + i], non_blocking=True)
             layer.forward_device(xd.data_ptr(), T, out.data_ptr(), flags, None, None, sp)

@@ -341,31 +341,11 @@ struct GemvParams {
     const float* xq_a;
     const float* xq_b;
     int xq_split;
-    // shared-expert items split along K: per-part sums [part][T][M][rows] and
-    // per-(first token of the pass, tile) arrival counters (zero between launches)
-    float* part_buf;
-    int32_t* part_ctr;
-    int part_rows;
-    // down launches holding every expert of the layer: the last item to finish
-    // a row tile also combines it (out = x + sum_j w_j y_j + ys, reference
-    // order); tile_ctr counts finished items per tile (zero between launches)
     // launched as a programmatic dependent: 1 = wait for the predecessor
     // before anything, 2 = the producer streams weights before the wait (the
     // routing it reads was final two launches earlier; only the activations
     // come from the predecessor)
     int pdl;
-    // gate/up launches: build the down launch's activation tables as the
-    // outputs complete (one 32-output group of a row once its tiles are all
-    // written; qgrp_ctr counts them, zero between launches)
-    uint8_t* qtab;
-    int qtab_stride;
-    int32_t* qgrp_ctr;
-    int fuse_combine;
-    const float* cmb_x;        // residual [T x d] or null
-    const float* cmb_w;        // top-k weights [T x k]
-    const int32_t* cmb_inv;    // inv_perm [T*k]
-    float* cmb_out;            // [T x d]
-    int32_t* tile_ctr;
 };
 
 __device__ __forceinline__ float swiglu(float g, float u, float limit) {

@@ -32,6 +32,7 @@
 #include "gemv.cuh"
 #include "gemv_tma.cuh"
 #include "gemv_imma.cuh"
+#include "gemv_stream.cuh"
 #include "layout.cuh"
 #include "route.cuh"
 
@@ -176,15 +177,6 @@ bool ep_graphs_enabled() {
     return v == 1;
 }
 
-bool gu_tables_enabled() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("QRM_GU_TABLES");
-        v = (e && e[0] == '1') ? 1 : 0;
-    }
-    return v == 1;
-}
-
 // Programmatic dependent launches between the forward's kernels, as a mask:
 // 1 gate/up, 2 down, 4 combine.  On B200 the expert launches ran slower as
 // dependents (measured 7570 -> 6966 / 7234 tokens/s at C5, T = 1), the
@@ -193,18 +185,6 @@ bool gu_tables_enabled() {
 int pdl_default() {
     const char* e = getenv("QRM_PDL");
     return e ? atoi(e) : 4;
-}
-
-// The down kernel can combine the expert outputs itself (last item of each
-// row tile); measured slower than the separate combine launch on B200, so
-// only on request: QRM_FUSED_COMBINE=1.
-bool fused_combine_enabled() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("QRM_FUSED_COMBINE");
-        v = (e && e[0] == '1') ? 1 : 0;
-    }
-    return v == 1;
 }
 
 // Launches kern, as a programmatic dependent of the previous launch on s when
@@ -226,78 +206,31 @@ cudaError_t launch_k(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-// K slices per row tile: a divisor of the super-block count close to the
-// warp limit, else the limit itself (uneven slices)
-int imma_kslices(int nsb, int rtiles, int max_warps, bool gateup) {
-    // tuning runs: QRM_IMMA_NKS="<gate/up>,<down>" caps the K slices
-    static int env[2] = {0, 0};
-    static bool read = false;
-    if (!read) {
-        const char* v = getenv("QRM_IMMA_NKS");
-        if (v) sscanf(v, "%d,%d", &env[0], &env[1]);
-        read = true;
-    }
-    int lim = std::min(nsb, max_warps / rtiles);
-    if (env[gateup ? 0 : 1] > 0) lim = std::min(lim, env[gateup ? 0 : 1]);
-    int nks = 1;
-    for (int d = lim; d >= 1; d--)
-        if (nsb % d == 0) { nks = d; break; }
-    return 2 * nks <= lim ? lim : nks;
-}
-
-// Row tiles per item (preferred; fewer when the stage does not fit).
-// Default: one for long rows (>= 16 super-blocks), else two (gate/up) or four
-// (down), so each consumer warp gets at least two super-blocks per item.  QRM_IMMA_RTILES="<gate/up>,<down>" overrides it for tuning runs
-// (gate/up 1 or 2, down 1, 2 or 4).
-int imma_rtiles(bool gateup, int nsb) {
-    static int env[2] = {-1, -1};
-    static bool read = false;
-    if (!read) {
-        const char* v = getenv("QRM_IMMA_RTILES");
-        if (v) sscanf(v, "%d,%d", &env[0], &env[1]);
-        read = true;
-    }
-    const int e = env[gateup ? 0 : 1];
-    if (e == 1 || e == 2 || (!gateup && e == 4)) return e;
-    return nsb >= 16 ? 1 : (gateup ? 2 : 4);
-}
-
-// The integer kernel's launch shape for one matrix launch.
-struct ImmaSel {
-    int rtiles = 1, ntk = 1, cw = 0;
-    qrm::ImmaConfig cfg{};
+// The streaming integer kernel's launch shape for one matrix launch.
+struct StreamSel {
+    int ntk = 1;
+    qrm::StreamConfig cfg{};
 };
 
 bool imma_format(int fmt) { return fmt == qrm::Q4_K || fmt == qrm::Q8_0 || fmt == qrm::Q4_0; }
 
-// true when the integer kernel may take this matrix shape (tables wanted)
+// true when a matrix of this shape is stored in the tiled layout and taken by
+// the streaming integer kernel (tables wanted); gate/up pairs 8-row tiles of
+// the two matrices, down takes 16 rows per MMA tile
 bool imma_usable(int fmt, int rows, int cols, bool gateup) {
     if (!imma_format(fmt) || cols % 256) return false;
     return rows % (gateup ? 8 : 16) == 0;
 }
 
-// Chooses row tiles, tokens per pass, consumer warps and the stage plan for
-// a launch whose routed items use format fa and shared items format fb (-1:
-// none); false when the integer kernel does not take the launch.
-bool imma_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, ImmaSel* sel) {
+// Plans a launch whose routed items use format fa and shared items format fb
+// (-1: none); false when no plan fits (the caller reports it).
+bool stream_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, StreamSel* sel) {
     if (!p.xtab) return false;
     if (fa >= 0 && !imma_usable(fa, p.rows, p.cols, gateup)) return false;
     if (fb >= 0 && !imma_usable(fb, p.rows, p.cols, gateup)) return false;
-    if (fa < 0 && fb < 0) return false;
-    const int RT = qrm::kImmaRows / (gateup ? 2 : 1);
-    if (p.rows % RT) return false;
     sel->ntk = T <= 1 ? 1 : 2;
     const int fmts[2] = {fa, fb};
-    for (int rtiles = imma_rtiles(gateup, p.cols / 256); rtiles >= 1; rtiles >>= 1) {
-        if (p.rows % (RT * rtiles)) continue;
-        sel->rtiles = rtiles;
-        sel->cw = imma_kslices(p.cols / 256, rtiles, sel->ntk == 1 ? qrm::kImmaMaxWarps : qrm::kImmaMaxWarps2, gateup) * rtiles;
-        if (!qrm::imma_plan(fmts, p.cols, qrm::kImmaRows * rtiles, sel->ntk, sel->cw, p.xtab_rows, 227 * 1024, &sel->cfg))
-            continue;
-        // split shared items need the per-part buffers
-        if (sel->cfg.seg[1].nsplit == 1 || (p.part_buf && p.part_ctr)) return true;
-    }
-    return false;
+    return qrm::stream_plan(fmts, gateup ? 2 : 1, p.rows, p.cols, sel->ntk, p.xtab_rows, 227 * 1024, &sel->cfg);
 }
 
 // segment formats of a launch of mode p.mode whose matrices are all format fmt
@@ -306,57 +239,39 @@ void imma_seg_fmts(int fmt, const qrm::GemvParams& p, int* fa, int* fb) {
     *fb = (p.mode == 1 || !p.has_shared) ? -1 : fmt;
 }
 
-template <int FA, int FB, int M, int NTK, int RTILES>
-int launch_imma_t(const qrm::GemvParams& p, const ImmaSel& sel, int sm_count, int32_t* err, cudaStream_t s) {
-    constexpr int RT = qrm::kImmaRows / M;
-    qrm::GemvParams q = p;
-    q.tiles = p.rows / (RT * RTILES);
-    auto fn = qrm::expert_gemv_imma_kernel<FA, FB, M, NTK, RTILES>;
+template <int FA, int FB, int M, int NTK>
+int launch_stream_t(const qrm::GemvParams& p, const StreamSel& sel, int sm_count, int32_t* err, cudaStream_t s) {
+    auto fn = qrm::expert_stream_kernel<FA, FB, M, NTK>;
     static bool attr_set = false;
     if (!attr_set) {
         if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
             return fail(QRM_E_CUDA, "expert kernel attribute");
         attr_set = true;
     }
-    cudaError_t e = launch_k(p.pdl != 0, fn, dim3(sm_count), dim3((sel.cw + 1) * 32), qrm::imma_smem_bytes(sel.cfg), s,
-                             q, sel.cfg, err);
+    cudaError_t e = launch_k(p.pdl != 0, fn, dim3(sm_count), dim3((sel.cfg.cw + 1) * 32),
+                             qrm::stream_smem_bytes(sel.cfg), s, p, sel.cfg, err);
     if (e == cudaSuccess) e = cudaGetLastError();
     return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
 }
 
-// launches the integer kernel for segment formats (FA, FB) when it takes the
-// launch (*used), else leaves it to the other kernels
+// the streaming kernel for segment formats (FA, FB); the matrices are tiled,
+// so no other kernel can take the launch
 template <int FA, int FB, int M>
-int launch_imma(int fa, int fb, int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s,
-                bool* used) {
-    *used = false;
-    ImmaSel sel;
-    if (!imma_select(fa, fb, M == 2, T, p, &sel)) return QRM_OK;
+int launch_stream(int fa, int fb, int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s) {
+    StreamSel sel;
+    if (!stream_select(fa, fb, M == 2, T, p, &sel))
+        return fail(QRM_E_STATE, "internal: no stage plan for the %d x %d expert matrices", p.rows, p.cols);
     // in-kernel tables only with a resident plan (the caller checked)
     if (p.xq_a && sel.cfg.res_rows == 0) return fail(QRM_E_STATE, "internal: activation tables were not built");
-    *used = true;
-#define QRM_IMMA_RT(R)                                                                          \
-    if (sel.rtiles == R)                                                                        \
-        return sel.ntk == 1 ? launch_imma_t<FA, FB, M, 1, R>(p, sel, sm_count, err, s)          \
-                            : launch_imma_t<FA, FB, M, 2, R>(p, sel, sm_count, err, s);
-    QRM_IMMA_RT(1)
-    QRM_IMMA_RT(2)
-    if constexpr (M == 1) {
-        QRM_IMMA_RT(4)
-    }
-#undef QRM_IMMA_RT
-    *used = false;
-    return QRM_OK;
+    return sel.ntk == 1 ? launch_stream_t<FA, FB, M, 1>(p, sel, sm_count, err, s)
+                        : launch_stream_t<FA, FB, M, 2>(p, sel, sm_count, err, s);
 }
 
 // routed items in Q4_K and a Q8_0 shared expert in one launch (mode 0)
 bool imma_pair_supported(int fa, int fb) { return fa == qrm::Q4_K && fb == qrm::Q8_0; }
-int launch_imma_pair(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, int sm_count, int32_t* err,
-                     cudaStream_t s, bool* used) {
-    *used = false;
-    if (!imma_pair_supported(fa, fb)) return QRM_OK;
-    return gateup ? launch_imma<qrm::Q4_K, qrm::Q8_0, 2>(fa, fb, T, p, sm_count, err, s, used)
-                  : launch_imma<qrm::Q4_K, qrm::Q8_0, 1>(fa, fb, T, p, sm_count, err, s, used);
+int launch_stream_pair(bool gateup, int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s) {
+    return gateup ? launch_stream<qrm::Q4_K, qrm::Q8_0, 2>(qrm::Q4_K, qrm::Q8_0, T, p, sm_count, err, s)
+                  : launch_stream<qrm::Q4_K, qrm::Q8_0, 1>(qrm::Q4_K, qrm::Q8_0, T, p, sm_count, err, s);
 }
 
 int launch_xquant(const float* src, int K, int rows, uint8_t* tab, cudaStream_t s) {
@@ -380,13 +295,12 @@ int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_c
     int rc = QRM_OK;
 #define QRM_GEMV_CASE(F)                                                                        \
     case F:                                                                                     \
-        if (F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) {                               \
+        if (imma_usable(F, p.rows, p.cols, gateup)) {                                           \
             constexpr int FI = (F == qrm::Q4_K || F == qrm::Q8_0 || F == qrm::Q4_0) ? F : qrm::Q4_K;  \
             int fa, fb;                                                                         \
             imma_seg_fmts(F, p, &fa, &fb);                                                      \
-            rc = gateup ? launch_imma<FI, FI, 2>(fa, fb, p.T, p, sm_count, err, s, &used)        \
-                        : launch_imma<FI, FI, 1>(fa, fb, p.T, p, sm_count, err, s, &used);       \
-            if (rc || used) return rc;                                                          \
+            return gateup ? launch_stream<FI, FI, 2>(fa, fb, p.T, p, sm_count, err, s)           \
+                          : launch_stream<FI, FI, 1>(fa, fb, p.T, p, sm_count, err, s);          \
         }                                                                                       \
         if (gateup) {                                                                           \
             rc = launch_tma<F, 2>(nt, p, sm_count, err, s, &used);                    \
@@ -463,15 +377,11 @@ struct qrm_layer {
     int32_t *topk_idx = nullptr, *perm = nullptr, *inv_perm = nullptr, *offsets = nullptr, *active = nullptr;
     int32_t* pos_tok = nullptr;
     int4* slot_info = nullptr;    // per active slot: expert, first position, tokens, first token
-    int32_t* qgrp_ctr = nullptr;  // gate/up outputs per (down table row, 32-group), zero between launches
     qrm::Schedule* sched = nullptr;
     uint8_t* staging = nullptr;
     size_t staging_bytes = 0;
     uint8_t* xtab_gu = nullptr;   // activation tables of the gate/up inputs [T]
     uint8_t* xtab_dn = nullptr;   // of the down inputs [T*k routed | T shared]
-    float* part_buf = nullptr;    // shared-expert items split along K: per-part sums
-    int32_t* part_ctr = nullptr;  // and their arrival counters
-    int32_t* tile_ctr = nullptr;  // finished down items per row tile (fused combine)
     int last_T = 0;
     int last_launches = 0;        // kernel launches of the last forward
     const float* last_xn = nullptr;
@@ -531,7 +441,7 @@ static void free_layer(qrm_layer* L) {
     void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_lm, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
                     L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn,
-                    L->part_buf, L->part_ctr, L->pos_tok, L->tile_ctr, L->slot_info, L->qgrp_ctr,
+                    L->pos_tok, L->slot_info,
                     L->rec_own, L->rec_all, L->ysend, L->peer_base, L->ep_state, L->xch};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -583,8 +493,6 @@ static int alloc_work(qrm_layer* L, int T) {
     QRM_CUDA(cudaMalloc(&L->inv_perm, sizeof(int32_t) * Tk));
     QRM_CUDA(cudaMalloc(&L->pos_tok, sizeof(int32_t) * Tk));
     QRM_CUDA(cudaMalloc(&L->slot_info, sizeof(int4) * (E + 1)));
-    QRM_CUDA(cudaMalloc(&L->qgrp_ctr, sizeof(int32_t) * (Tk + T) * (f / 32)));
-    QRM_CUDA(cudaMemset(L->qgrp_ctr, 0, sizeof(int32_t) * (Tk + T) * (f / 32)));
     QRM_CUDA(cudaMalloc(&L->offsets, sizeof(int32_t) * (E + 1)));
     QRM_CUDA(cudaMalloc(&L->active, sizeof(int32_t) * (E + 1)));
     QRM_CUDA(cudaMalloc(&L->sched, sizeof(qrm::Schedule)));
@@ -597,15 +505,6 @@ static int alloc_work(qrm_layer* L, int T) {
     }
     QRM_CUDA(cudaMalloc(&L->xtab_gu, (size_t)qrm::xtab_stride(d) * T));
     QRM_CUDA(cudaMalloc(&L->xtab_dn, (size_t)qrm::xtab_stride(f) * (Tk + T)));
-    QRM_CUDA(cudaMalloc(&L->tile_ctr, sizeof(int32_t) * (d / 16)));
-    QRM_CUDA(cudaMemset(L->tile_ctr, 0, sizeof(int32_t) * (d / 16)));
-    if (L->shared_enabled) {
-        // shared-expert items split along K: sums per part, arrival counters
-        const size_t cols = (size_t)std::max(d, f), tiles = (size_t)std::max(f / 8, d / 16);
-        QRM_CUDA(cudaMalloc(&L->part_buf, sizeof(float) * qrm::kImmaMaxSplit * T * 2 * cols));
-        QRM_CUDA(cudaMalloc(&L->part_ctr, sizeof(int32_t) * T * tiles));
-        QRM_CUDA(cudaMemset(L->part_ctr, 0, sizeof(int32_t) * T * tiles));
-    }
     L->cap_T = T;
     return QRM_OK;
 }
@@ -894,7 +793,8 @@ static int upload_common(qrm_layer* L, int expert, int which, int fmt, const voi
                     m.rows, m.cols, L->mat_bytes[i]);
     QRM_CUDA(cudaSetDevice(L->desc.device));
     uint8_t* dst = const_cast<uint8_t*>(m.base);
-    if (fmt == qrm::Q4_K) {
+    const bool tiled = imma_usable(fmt, m.rows, m.cols, which != 2);
+    if (fmt == qrm::Q4_K && !tiled) {
         QRM_CUDA(cudaMemcpyAsync(dst, bytes, nbytes, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, L->stream));
     } else {
         const uint8_t* src = (const uint8_t*)bytes;
@@ -912,7 +812,10 @@ static int upload_common(qrm_layer* L, int expert, int which, int fmt, const voi
         int bs, bb;
         qrm::block_spec(fmt, &bs, &bb);
         long long nb = (long long)(nbytes / bb);
-        qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(fmt, bb, src, dst, nb, 1);
+        if (tiled)
+            qrm::tile_relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(fmt, bb, m.cols / 256, src, dst, nb, 1);
+        else
+            qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(fmt, bb, src, dst, nb, 1);
         QRM_CUDA(cudaGetLastError());
     }
     QRM_CUDA(cudaStreamSynchronize(L->stream));
@@ -936,7 +839,8 @@ extern "C" int qrm_download_expert(qrm_layer* L, int expert, int which, void* by
     if (nbytes != L->mat_bytes[i]) return fail(QRM_E_SIZE, "buffer is %zu bytes, tensor is %zu", nbytes, L->mat_bytes[i]);
     const qrm::MatDev& m = L->mats[i];
     QRM_CUDA(cudaSetDevice(L->desc.device));
-    if (m.fmt == qrm::Q4_K) {
+    const bool tiled = imma_usable(m.fmt, m.rows, m.cols, which != 2);
+    if (m.fmt == qrm::Q4_K && !tiled) {
         QRM_CUDA(cudaMemcpy(bytes, m.base, nbytes, cudaMemcpyDeviceToHost));
         return QRM_OK;
     }
@@ -944,7 +848,11 @@ extern "C" int qrm_download_expert(qrm_layer* L, int expert, int which, void* by
     QRM_CUDA(cudaMalloc(&tmp, nbytes));
     int bs, bb;
     qrm::block_spec(m.fmt, &bs, &bb);
-    qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, m.base, tmp, (long long)(nbytes / bb), 0);
+    if (tiled)
+        qrm::tile_relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, m.cols / 256, m.base, tmp,
+                                                                         (long long)(nbytes / bb), 0);
+    else
+        qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, m.base, tmp, (long long)(nbytes / bb), 0);
     cudaError_t e1 = cudaStreamSynchronize(L->stream);
     cudaError_t e2 = cudaMemcpy(bytes, tmp, nbytes, cudaMemcpyDeviceToHost);
     cudaFree(tmp);
@@ -1087,7 +995,6 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU
     const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
     bool combined = false;
-    bool dn_tables_built = false;
     for (int stage = 0; stage < 2; stage++) {
         const bool gu = stage == 0;
         // activation tables for the integer tensor-core kernel
@@ -1121,41 +1028,28 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.has_shared = shared ? 1 : 0;
         const int fr = gu ? D.fmt_gate : D.fmt_down;
         const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
-        gp.part_buf = L->part_buf;
-        gp.part_ctr = L->part_ctr;
-        gp.part_rows = Tx;
         gp.pdl = (!prof && (L->pdl & (gu ? 1 : 2))) ? (gu ? 1 : 2) : 0;   // profiling events sit between the launches
         // routed + shared expert in one integer-kernel launch when the pair of
-        // formats has one (shared items split along K to fit the stage)
-        ImmaSel sp;
-        const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && imma_select(fr, fs, gu, Tx, gp, &sp);
-        // gate/up in one integer-kernel launch can build the down tables as its
-        // outputs complete (QRM_GU_TABLES=1; measured slower on B200 at C5,
-        // Tx = 1: 61 -> 85 us gate/up for 43 -> 40 us down)
-        if (gu && gu_tables_enabled() && imma_usable(D.fmt_down, d, f, false) &&
-            (!shared || imma_usable(D.fmt_sh_down, d, f, false) || same_fmt)) {
-            ImmaSel sg;
-            gp.mode = 0;
-            if (pair || (same_fmt && imma_select(fr, shared ? fr : -1, true, Tx, gp, &sg))) {
-                gp.qtab = L->xtab_dn;
-                gp.qtab_stride = qrm::xtab_stride(f);
-                gp.qgrp_ctr = L->qgrp_ctr;
-                dn_tables_built = true;
-            }
-        }
-        if (want_tab && !gu && dn_tables_built) {
-            // nothing to build: the gate/up launch wrote the tables
-        } else if (want_tab) {
+        // formats has one
+        StreamSel sp;
+        gp.mode = 0;
+        const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && stream_select(fr, fs, gu, Tx, gp, &sp);
+        if (want_tab) {
             // the kernels quantise resident tables themselves when every
             // integer-kernel launch of this stage keeps them resident
             bool in_kernel;
             if (pair) {
                 in_kernel = sp.cfg.res_rows > 0;
             } else {
-                ImmaSel sr, ss;
-                const bool ur = imma_select(fr, same_fmt && shared ? fr : -1, gu, Tx, gp, &sr);
-                const bool us = shared && !same_fmt && imma_select(-1, fs, gu, Tx, gp, &ss);
-                in_kernel = (ur || us) && (!ur || sr.cfg.res_rows > 0) && (!us || ss.cfg.res_rows > 0);
+                StreamSel sr, ss;
+                const bool ur = imma_usable(fr, gp.rows, gp.cols, gu);
+                const bool us = shared && !same_fmt && imma_usable(fs, gp.rows, gp.cols, gu);
+                gp.mode = same_fmt ? 0 : 1;
+                const bool pr = ur && stream_select(fr, same_fmt && shared ? fr : -1, gu, Tx, gp, &sr);
+                gp.mode = 2;
+                const bool ps = us && stream_select(-1, fs, gu, Tx, gp, &ss);
+                gp.mode = 0;
+                in_kernel = (ur || us) && (!ur || (pr && sr.cfg.res_rows > 0)) && (!us || (ps && ss.cfg.res_rows > 0));
             }
             if (in_kernel) {
                 gp.xq_a = gu ? xs : L->h;
@@ -1177,27 +1071,11 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                 if (rc) return rc;
             }
         }
-        // down in one integer-kernel launch: the kernel also combines
-        if (!gu) {
-            ImmaSel sd;
-            const bool one = pair || (same_fmt && imma_select(fr, shared ? fr : -1, false, Tx, gp, &sd));
-            if (one && !ep && L->n_local == E && fused_combine_enabled()) {
-                gp.fuse_combine = 1;
-                gp.cmb_x = (flags & QRM_ADD_RESIDUAL) ? x : nullptr;
-                gp.cmb_w = topk_w;
-                gp.cmb_inv = L->inv_perm;
-                gp.cmb_out = out;
-                gp.tile_ctr = L->tile_ctr;
-                combined = true;
-            }
-        }
         if (pair) {
             gp.mode = 0;
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
-            bool used = false;
-            int rc = launch_imma_pair(fr, fs, gu, Tx, gp, L->sm_count, &L->sched->err, s, &used);
+            int rc = launch_stream_pair(gu, Tx, gp, L->sm_count, &L->sched->err, s);
             if (rc) return rc;
-            if (!used) return fail(QRM_E_STATE, "internal: the paired expert kernel declined the launch");
             nl++;
         } else if (same_fmt) {
             gp.mode = 0;
@@ -1509,7 +1387,10 @@ extern "C" int qrm_matrix_create(int device, int fmt, int64_t rows, int64_t cols
     cudaMemcpy(staging, bytes, nbytes, cudaMemcpyHostToDevice);
     int bs, bb;
     qrm::block_spec(fmt, &bs, &bb);
-    if (fmt == qrm::Q4_K) cudaMemcpy(M->data, staging, nbytes, cudaMemcpyDeviceToDevice);
+    if (imma_usable(fmt, (int)rows, (int)cols, false))
+        qrm::tile_relayout_kernel<<<M->sm_count * 8, 256>>>(fmt, bb, (int)(cols / 256), staging, M->data,
+                                                            (long long)(nbytes / bb), 1);
+    else if (fmt == qrm::Q4_K) cudaMemcpy(M->data, staging, nbytes, cudaMemcpyDeviceToDevice);
     else qrm::relayout_kernel<<<M->sm_count * 8, 256>>>(fmt, bb, staging, M->data, (long long)(nbytes / bb), 1);
     cudaError_t e = cudaDeviceSynchronize();
     cudaFree(staging);
