@@ -27,28 +27,28 @@
 namespace qrm {
 
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void mma_u8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void mma_s8s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void mma_s8u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};\n"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
@@ -164,12 +164,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
     }
     return ok;
 }
-// lane 0 spins until *f == v; whole warp returns the outcome
+// lane 0 spins (with a short back-off, so the waiting warp leaves the issue
+// slots to the others) until *f == v; whole warp returns the outcome
 __device__ __forceinline__ bool warp_spin_eq(const volatile int* f, int v, volatile int* abort_flag, int32_t* err) {
     int ok = 1;
     if ((threadIdx.x & 31) == 0) {
         const uint64_t t0 = global_ns();
         while (*f != v) {
+            __nanosleep(32);
             if (*abort_flag || global_ns() - t0 > kWaitLimitNs) { ok = 0; break; }
         }
         if (!ok) {
@@ -210,9 +212,11 @@ __device__ __forceinline__ uint32_t lds16(uint32_t a) {
 // activation-table loads: shared (resident or staged tables) or global
 template <bool SM> struct TabLd;
 template <> struct TabLd<true> {
-    using Ptr = uint32_t;
-    __device__ static uint32_t ld32(Ptr b, int o) { return lds32(b + o); }
-    __device__ static uint2 ld64(Ptr b, int o) { return lds64(b + o); }
+    // plain loads: the compiler may schedule them (the mbarrier waits carry
+    // memory clobbers, so no load moves above the wait for its stage)
+    using Ptr = const uint8_t*;
+    __device__ static uint32_t ld32(Ptr b, int o) { return *reinterpret_cast<const uint32_t*>(b + o); }
+    __device__ static uint2 ld64(Ptr b, int o) { return *reinterpret_cast<const uint2*>(b + o); }
 };
 template <> struct TabLd<false> {
     using Ptr = const uint8_t*;

@@ -25,8 +25,8 @@
 // four mma.sync m16n8k32 per token on the raw codes against the 16-bit
 // fixed-point activation tables (gemv_imma.cuh), the per-group scales applied
 // in f32.  A stage is released as soon as its units are done; after the last
-// part each warp publishes its partial sums to a reduction slot, and one warp
-// adds the CW partials in a fixed order (SwiGLU for gate/up) one item later.
+// part each warp publishes its partial sums to a reduction slot, and the last
+// warp to publish adds the CW partials in a fixed order (SwiGLU for gate/up).
 // Tokens: passes of NTK tokens, stream_passes(NTK) passes per item chunk; an
 // expert slot with more tokens streams its weights once per chunk of
 // stream_chunk(NTK) tokens (one token per chunk when T = 1).  All waits are bounded.
@@ -250,6 +250,12 @@ inline size_t stream_smem_bytes(const StreamConfig& c) {
 }
 
 // ------------------------------------------------------------ one unit
+// Plain shared-memory loads of the stage bytes (the compiler may schedule
+// them; the mbarrier waits and arrivals carry memory clobbers, so none moves
+// above the wait for its stage or below its release).
+__device__ __forceinline__ uint2 ld2(const uint8_t* a) { return *reinterpret_cast<const uint2*>(a); }
+__device__ __forceinline__ uint32_t ld1(const uint8_t* a) { return *reinterpret_cast<const uint32_t*>(a); }
+
 // Adds to y[q][0] / y[q][1] (rows gid / gid+8 of the MMA tile; this lane's
 // groups t and t+4 when FULL, else group 4*half + t) the products of
 // super-block sbg (of the row) for nt <= NTK tokens: all eight groups (FULL)
@@ -257,7 +263,7 @@ inline size_t stream_smem_bytes(const StreamConfig& c) {
 // chunks of the tile's first / second 8 rows.  Group g's MMAs accumulate into
 // chain g / 4 (two independent chains when FULL).
 template <int FMT, int NTK, bool SM, bool FULL>
-__device__ __forceinline__ void stream_unit(uint32_t cA, uint32_t cB, const typename TabLd<SM>::Ptr (&tq)[NTK], int nt,
+__device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB, const typename TabLd<SM>::Ptr (&tq)[NTK], int nt,
                                             int K, int sbg, int half, int lane, const uint32_t (&bm)[4],
                                             float (&y)[NTK][2]) {
     using L = TabLd<SM>;
@@ -300,22 +306,22 @@ __device__ __forceinline__ void stream_unit(uint32_t cA, uint32_t cB, const type
         for (int hh = 0; hh < NH; hh++) {
             const int pr = 2 * (FULL ? hh : half) + pp;
             if (FMT == Q4_K) {
-                const uint32_t o = 128 + 256 * pr + 32 * gid + 8 * t;
-                const uint2 w0 = lds64(cA + o), w1 = lds64(cB + o);
+                const int o = 128 + 256 * pr + 32 * gid + 8 * t;
+                const uint2 w0 = ld2(cA + o), w1 = ld2(cB + o);
                 A0[hh][0] = w0.x & 0x0F0F0F0Fu; A0[hh][1] = w1.x & 0x0F0F0F0Fu;
                 A0[hh][2] = w0.y & 0x0F0F0F0Fu; A0[hh][3] = w1.y & 0x0F0F0F0Fu;
                 A1[hh][0] = w0.x & 0xF0F0F0F0u; A1[hh][1] = w1.x & 0xF0F0F0F0u;
                 A1[hh][2] = w0.y & 0xF0F0F0F0u; A1[hh][3] = w1.y & 0xF0F0F0F0u;
             } else if (FMT == Q8_0) {
-                const uint32_t o = 128 + 256 * (2 * pr) + 32 * gid + 8 * t;
-                const uint2 a0 = lds64(cA + o), a1 = lds64(cB + o);
-                const uint2 b0 = lds64(cA + o + 256), b1 = lds64(cB + o + 256);
+                const int o = 128 + 256 * (2 * pr) + 32 * gid + 8 * t;
+                const uint2 a0 = ld2(cA + o), a1 = ld2(cB + o);
+                const uint2 b0 = ld2(cA + o + 256), b1 = ld2(cB + o + 256);
                 A0[hh][0] = a0.x; A0[hh][1] = a1.x; A0[hh][2] = a0.y; A0[hh][3] = a1.y;
                 A1[hh][0] = b0.x; A1[hh][1] = b1.x; A1[hh][2] = b0.y; A1[hh][3] = b1.y;
             } else {  // Q4_0
-                const uint32_t o = 256 + 128 * (2 * pr) + 16 * gid + 4 * t;
-                const uint32_t a0 = lds32(cA + o), a1 = lds32(cB + o);
-                const uint32_t b0 = lds32(cA + o + 128), b1 = lds32(cB + o + 128);
+                const int o = 256 + 128 * (2 * pr) + 16 * gid + 4 * t;
+                const uint32_t a0 = ld1(cA + o), a1 = ld1(cB + o);
+                const uint32_t b0 = ld1(cA + o + 128), b1 = ld1(cB + o + 128);
                 A0[hh][0] = a0 & 0x0F0F0F0Fu; A0[hh][1] = a1 & 0x0F0F0F0Fu;
                 A0[hh][2] = (a0 >> 4) & 0x0F0F0F0Fu; A0[hh][3] = (a1 >> 4) & 0x0F0F0F0Fu;
                 A1[hh][0] = b0 & 0x0F0F0F0Fu; A1[hh][1] = b1 & 0x0F0F0F0Fu;
@@ -345,7 +351,7 @@ __device__ __forceinline__ void stream_unit(uint32_t cA, uint32_t cB, const type
         const uint32_t sel = 0x7044u | ((uint32_t)t << 8);   // byte t -> bits 16..23 of 2.0f
 #pragma unroll
         for (int rw = 0; rw < 2; rw++) {
-            const uint4 hd = lds128((rw ? cB : cA) + 16 * gid);
+            const uint4 hd = *reinterpret_cast<const uint4*>((rw ? cB : cA) + 16 * gid);
             const float d = h2f((uint16_t)(hd.x & 0xFFFF)), dmin = h2f((uint16_t)(hd.x >> 16));
             const float da = kq * d, db = -2.f * kq * d, ma = 64.f * dmin, mb = -128.f * dmin;
             // GetScaleMinK4 (BlockDequantizer.cs:155-166), four sub-blocks per word:
@@ -365,8 +371,8 @@ __device__ __forceinline__ void stream_unit(uint32_t cA, uint32_t cB, const type
     } else {
 #pragma unroll
         for (int hh = 0; hh < NH; hh++) {
-            const uint32_t o = 16 * gid + 2 * (t + 4 * (FULL ? hh : half));
-            const float dA = h2f((uint16_t)lds16(cA + o)), dB = h2f((uint16_t)lds16(cB + o));
+            const int o = 16 * gid + 2 * (t + 4 * (FULL ? hh : half));
+            const float dA = h2f(*reinterpret_cast<const uint16_t*>(cA + o)), dB = h2f(*reinterpret_cast<const uint16_t*>(cB + o));
             ar[hh][0] = dA;
             ar[hh][1] = dB;
             mr[hh][0] = FMT == Q4_0 ? 8.f * dA : 0.f;
@@ -406,7 +412,7 @@ struct StreamRed {
 
 // What a reduction needs once the stages and their headers are gone.
 struct StreamJob {
-    int r;         // reduction number (slot r % kStreamRedSlots); -1: none
+    int r;         // reduction number (slot r % kStreamRedSlots)
     int seg, rg, off, t0, nt, shared;
 };
 
@@ -446,23 +452,12 @@ __device__ __forceinline__ void stream_reduce(const GemvParams& p, const StreamC
     }
 }
 
-// Runs this warp's pending reduction once all warps' partials are in.
-template <int M, int NTK>
-__device__ __forceinline__ bool stream_flush(const GemvParams& p, const StreamConfig& cfg, StreamJob& pend,
-                                             const StreamRed& R, int lane, volatile int* abort_flag, int32_t* err) {
-    if (pend.r < 0) return true;
-    if (!warp_spin_eq(&R.arr[pend.r % kStreamRedSlots], cfg.cw, abort_flag, err)) return false;
-    stream_reduce<M, NTK>(p, cfg, pend, R, lane);
-    pend.r = -1;
-    return true;
-}
-
 // ------------------------------------------------------------ one stage
 // This warp's units of one stage (format FMT), accumulated into y: MMA tile
 // w / wpt, units w % wpt + n * wpt (n < sbs * halves / wpt).
 template <int FMT, int M, int NTK>
 __device__ __forceinline__ void stream_stage(const GemvParams& p, const StreamConfig& cfg, const StreamSeg& g,
-                                             const int* h, uint32_t st_u, uint32_t res_u, int warp, int lane,
+                                             const int* h, const uint8_t* st, const uint8_t* res, int warp, int lane,
                                              const uint32_t (&bm)[4], float (&y)[stream_passes(NTK)][NTK][2]) {
     constexpr int P = stream_passes(NTK);
     const int K = p.cols, nc = h[4], part = h[6];
@@ -474,17 +469,17 @@ __device__ __forceinline__ void stream_stage(const GemvParams& p, const StreamCo
     const int nu = g.sbs * g.halves;
     for (int u = wt; u < nu; u += wpt) {
         const int sl = g.halves == 2 ? u >> 1 : u, half = u & 1;
-        const uint32_t cA = st_u + (uint32_t)((ta * g.sbs + sl) * g.cb);
-        const uint32_t cB = st_u + (uint32_t)((tb * g.sbs + sl) * g.cb);
+        const uint8_t* cA = st + (ta * g.sbs + sl) * g.cb;
+        const uint8_t* cB = st + (tb * g.sbs + sl) * g.cb;
         const int sbg = part * g.sbs + sl;
 #pragma unroll
         for (int ps = 0; ps < P; ps++) {
             if (ps * NTK >= nc) break;
             const int nt = min(NTK, nc - ps * NTK);
             if (res_bytes > 0) {
-                uint32_t tq[NTK];
+                const uint8_t* tq[NTK];
 #pragma unroll
-                for (int q = 0; q < NTK; q++) tq[q] = res_u + h[8 + ps * NTK + min(q, nt - 1)] * cfg.xtab_bytes;
+                for (int q = 0; q < NTK; q++) tq[q] = res + h[8 + ps * NTK + min(q, nt - 1)] * cfg.xtab_bytes;
                 if (g.halves == 1) stream_unit<FMT, NTK, true, true>(cA, cB, tq, nt, K, sbg, 0, lane, bm, y[ps]);
                 else stream_unit<FMT, NTK, true, false>(cA, cB, tq, nt, K, sbg, half, lane, bm, y[ps]);
             } else {
@@ -711,12 +706,9 @@ expert_stream_kernel(GemvParams p, StreamConfig cfg, int32_t* err) {
     } else if (res_bytes > 0 && !warp_wait(tabbar, 0u, abort_flag, err)) {
         return;
     }
-    const uint32_t res_u = smem_u32(ssm + kStreamDataOff);
-    const uint32_t data_u = smem_u32(data);
+    const uint8_t* res = ssm + kStreamDataOff;
     float y[P][NTK][2];
     int rseq = 0;   // reductions this warp has taken part in (the same for every warp)
-    StreamJob pend;
-    pend.r = -1;
     for (int k = 0;; k++) {
         const int s = k % S;
         const uint32_t ph = (uint32_t)(k / S) & 1u;
@@ -731,9 +723,9 @@ expert_stream_kernel(GemvParams p, StreamConfig cfg, int32_t* err) {
 #pragma unroll
                 for (int q = 0; q < NTK; q++) y[ps][q][0] = y[ps][q][1] = 0.f;
         }
-        const uint32_t st_u = data_u + (uint32_t)(s * cfg.stage_bytes);
-        if (seg == 0) stream_stage<FA, M, NTK>(p, cfg, g, h, st_u, res_u, warp, lane, bm, y);
-        else stream_stage<FB, M, NTK>(p, cfg, g, h, st_u, res_u, warp, lane, bm, y);
+        const uint8_t* st = data + (size_t)s * cfg.stage_bytes;
+        if (seg == 0) stream_stage<FA, M, NTK>(p, cfg, g, h, st, res, warp, lane, bm, y);
+        else stream_stage<FB, M, NTK>(p, cfg, g, h, st, res, warp, lane, bm, y);
         // what the reduction needs, before the stage (and its header) is released
         const int nc = h[4], slot = h[1], off = h[3], rg = h[7] & 0xFFFF, t0 = h[7] >> 16;
         __syncwarp();
@@ -758,12 +750,14 @@ expert_stream_kernel(GemvParams p, StreamConfig cfg, int32_t* err) {
                 }
         __threadfence_block();
         __syncwarp();
-        if (lane == 0) atomicAdd(&R.arr[sq], 1);
-        // the previous reduction of this warp, then this one becomes pending
-        if (!stream_flush<M, NTK>(p, cfg, pend, R, lane, abort_flag, err)) return;
-        if (r % CW == warp) pend = StreamJob{r, seg, rg, off, t0, nc, slot >= n_active ? 1 : 0};
+        // the last warp to publish adds the partials (fixed order) and frees the slot
+        int last = 0;
+        if (lane == 0) last = atomicAdd(&R.arr[sq], 1) == CW - 1;
+        if (__shfl_sync(0xffffffffu, last, 0)) {
+            __threadfence_block();
+            stream_reduce<M, NTK>(p, cfg, StreamJob{r, seg, rg, off, t0, nc, slot >= n_active ? 1 : 0}, R, lane);
+        }
     }
-    stream_flush<M, NTK>(p, cfg, pend, R, lane, abort_flag, err);
 }
 
 }  // namespace qrm
