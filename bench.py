@@ -226,7 +226,7 @@ def build_layer(torch, Q, dev, T, seed=SEED, rank=0, world=1, nccl_id=None):
 
 def traffic_from_profiles():
     """dram bytes per gate/up launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "expert_gemv_c5_decode.md")
+    p = os.path.join(ROOT, "profiles", "expert_stream_c5_decode.md")
     try:
         with open(p) as fh:
             for line in fh:
