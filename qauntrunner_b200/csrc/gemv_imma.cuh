@@ -212,11 +212,9 @@ __device__ __forceinline__ uint32_t lds16(uint32_t a) {
 // activation-table loads: shared (resident or staged tables) or global
 template <bool SM> struct TabLd;
 template <> struct TabLd<true> {
-    // plain loads: the compiler may schedule them (the mbarrier waits carry
-    // memory clobbers, so no load moves above the wait for its stage)
     using Ptr = const uint8_t*;
-    __device__ static uint32_t ld32(Ptr b, int o) { return *reinterpret_cast<const uint32_t*>(b + o); }
-    __device__ static uint2 ld64(Ptr b, int o) { return *reinterpret_cast<const uint2*>(b + o); }
+    __device__ static uint32_t ld32(Ptr b, int o) { return lds32(smem_u32(b) + o); }
+    __device__ static uint2 ld64(Ptr b, int o) { return lds64(smem_u32(b) + o); }
 };
 template <> struct TabLd<false> {
     using Ptr = const uint8_t*;

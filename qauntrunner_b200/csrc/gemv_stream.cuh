@@ -250,11 +250,6 @@ inline size_t stream_smem_bytes(const StreamConfig& c) {
 }
 
 // ------------------------------------------------------------ one unit
-// Plain shared-memory loads of the stage bytes (the compiler may schedule
-// them; the mbarrier waits and arrivals carry memory clobbers, so none moves
-// above the wait for its stage or below its release).
-__device__ __forceinline__ uint2 ld2(const uint8_t* a) { return *reinterpret_cast<const uint2*>(a); }
-__device__ __forceinline__ uint32_t ld1(const uint8_t* a) { return *reinterpret_cast<const uint32_t*>(a); }
 
 // Adds to y[q][0] / y[q][1] (rows gid / gid+8 of the MMA tile; this lane's
 // groups t and t+4 when FULL, else group 4*half + t) the products of
@@ -268,8 +263,12 @@ __device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB
                                             float (&y)[NTK][2]) {
     using L = TabLd<SM>;
     constexpr int NH = FULL ? 2 : 1;   // group halves in this unit
+    constexpr int NW = FMT == Q8_0 ? 8 : 4;   // code words per half and group pair
     const int gid = lane >> 2, t = lane & 3, j = gid >> 1, hl = gid & 1;
-    // B bytes of group 4*h + j, this lane's part of the fixed point (hi or lo)
+    const uint32_t sA = smem_u32(cA), sB = smem_u32(cB);
+    // every shared load of the unit first (in this order), then the MMAs and
+    // the epilogue: B bytes of group 4*h + j (this lane's part of the fixed
+    // point), the codes, the scales, the table scale/sum entries
     const int bo = hl * xtab_lo(K) + 32 * j + (FMT == Q4_0 ? 4 : 8) * t + 256 * sbg;
     uint32_t bx[NH][NTK][2];
 #pragma unroll
@@ -291,6 +290,51 @@ __device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB
             }
         }
     }
+    uint32_t w[NH][2][NW];   // [half][group pair][words of rows gid, gid+8]
+#pragma unroll
+    for (int hh = 0; hh < NH; hh++) {
+#pragma unroll
+        for (int pp = 0; pp < 2; pp++) {
+            const int pr = 2 * (FULL ? hh : half) + pp;   // groups 2pr, 2pr+1
+            uint32_t* ww = w[hh][pp];
+            if (FMT == Q4_K) {
+                const uint32_t o = 128 + 256 * pr + 32 * gid + 8 * t;
+                const uint2 w0 = lds64(sA + o), w1 = lds64(sB + o);
+                ww[0] = w0.x; ww[1] = w0.y; ww[2] = w1.x; ww[3] = w1.y;
+            } else if (FMT == Q8_0) {
+                const uint32_t o = 128 + 256 * (2 * pr) + 32 * gid + 8 * t;
+                const uint2 a0 = lds64(sA + o), a1 = lds64(sB + o);
+                const uint2 b0 = lds64(sA + o + 256), b1 = lds64(sB + o + 256);
+                ww[0] = a0.x; ww[1] = a0.y; ww[2] = a1.x; ww[3] = a1.y;
+                ww[4] = b0.x; ww[5] = b0.y; ww[6] = b1.x; ww[7] = b1.y;
+            } else {  // Q4_0
+                const uint32_t o = 256 + 128 * (2 * pr) + 16 * gid + 4 * t;
+                ww[0] = lds32(sA + o); ww[1] = lds32(sB + o);
+                ww[2] = lds32(sA + o + 128); ww[3] = lds32(sB + o + 128);
+            }
+        }
+    }
+    uint4 hd[2];             // Q4_K block headers of rows gid, gid+8
+    uint32_t dd[NH][2];      // Q8_0 / Q4_0: d of rows gid, gid+8 per half
+    if (FMT == Q4_K) {
+        hd[0] = lds128(sA + 16 * gid);
+        hd[1] = lds128(sB + 16 * gid);
+    } else {
+#pragma unroll
+        for (int hh = 0; hh < NH; hh++) {
+            const uint32_t o = 16 * gid + 2 * (t + 4 * (FULL ? hh : half));
+            dd[hh][0] = lds16(sA + o);
+            dd[hh][1] = lds16(sB + o);
+        }
+    }
+    uint2 ss[NH][NTK];
+#pragma unroll
+    for (int hh = 0; hh < NH; hh++) {
+        const int so = xtab_ss(K) + 8 * (8 * sbg + 4 * (FULL ? hh : half) + t);
+#pragma unroll
+        for (int q = 0; q < NTK; q++) ss[hh][q] = (q == 0 || q < nt) ? L::ld64(tq[q], so) : make_uint2(0u, 0u);
+    }
+    // MMAs: group pairs (2pr, 2pr+1) of each half, the halves' chains interleaved
     int X[NH][NTK][4];
 #pragma unroll
     for (int hh = 0; hh < NH; hh++)
@@ -300,32 +344,23 @@ __device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB
             for (int i = 0; i < 4; i++) X[hh][q][i] = 0;
 #pragma unroll
     for (int pp = 0; pp < 2; pp++) {
-        // group pairs (2pr, 2pr+1) of each half, the halves' MMAs interleaved
         uint32_t A0[NH][4], A1[NH][4];
 #pragma unroll
         for (int hh = 0; hh < NH; hh++) {
-            const int pr = 2 * (FULL ? hh : half) + pp;
+            const uint32_t* ww = w[hh][pp];
             if (FMT == Q4_K) {
-                const int o = 128 + 256 * pr + 32 * gid + 8 * t;
-                const uint2 w0 = ld2(cA + o), w1 = ld2(cB + o);
-                A0[hh][0] = w0.x & 0x0F0F0F0Fu; A0[hh][1] = w1.x & 0x0F0F0F0Fu;
-                A0[hh][2] = w0.y & 0x0F0F0F0Fu; A0[hh][3] = w1.y & 0x0F0F0F0Fu;
-                A1[hh][0] = w0.x & 0xF0F0F0F0u; A1[hh][1] = w1.x & 0xF0F0F0F0u;
-                A1[hh][2] = w0.y & 0xF0F0F0F0u; A1[hh][3] = w1.y & 0xF0F0F0F0u;
+                A0[hh][0] = ww[0] & 0x0F0F0F0Fu; A0[hh][1] = ww[2] & 0x0F0F0F0Fu;
+                A0[hh][2] = ww[1] & 0x0F0F0F0Fu; A0[hh][3] = ww[3] & 0x0F0F0F0Fu;
+                A1[hh][0] = ww[0] & 0xF0F0F0F0u; A1[hh][1] = ww[2] & 0xF0F0F0F0u;
+                A1[hh][2] = ww[1] & 0xF0F0F0F0u; A1[hh][3] = ww[3] & 0xF0F0F0F0u;
             } else if (FMT == Q8_0) {
-                const int o = 128 + 256 * (2 * pr) + 32 * gid + 8 * t;
-                const uint2 a0 = ld2(cA + o), a1 = ld2(cB + o);
-                const uint2 b0 = ld2(cA + o + 256), b1 = ld2(cB + o + 256);
-                A0[hh][0] = a0.x; A0[hh][1] = a1.x; A0[hh][2] = a0.y; A0[hh][3] = a1.y;
-                A1[hh][0] = b0.x; A1[hh][1] = b1.x; A1[hh][2] = b0.y; A1[hh][3] = b1.y;
-            } else {  // Q4_0
-                const int o = 256 + 128 * (2 * pr) + 16 * gid + 4 * t;
-                const uint32_t a0 = ld1(cA + o), a1 = ld1(cB + o);
-                const uint32_t b0 = ld1(cA + o + 128), b1 = ld1(cB + o + 128);
-                A0[hh][0] = a0 & 0x0F0F0F0Fu; A0[hh][1] = a1 & 0x0F0F0F0Fu;
-                A0[hh][2] = (a0 >> 4) & 0x0F0F0F0Fu; A0[hh][3] = (a1 >> 4) & 0x0F0F0F0Fu;
-                A1[hh][0] = b0 & 0x0F0F0F0Fu; A1[hh][1] = b1 & 0x0F0F0F0Fu;
-                A1[hh][2] = (b0 >> 4) & 0x0F0F0F0Fu; A1[hh][3] = (b1 >> 4) & 0x0F0F0F0Fu;
+                A0[hh][0] = ww[0]; A0[hh][1] = ww[2]; A0[hh][2] = ww[1]; A0[hh][3] = ww[3];
+                A1[hh][0] = ww[4]; A1[hh][1] = ww[6]; A1[hh][2] = ww[5]; A1[hh][3] = ww[7];
+            } else {  // Q4_0: low nibbles = weights 0-15 of the block, high = 16-31
+                A0[hh][0] = ww[0] & 0x0F0F0F0Fu; A0[hh][1] = ww[1] & 0x0F0F0F0Fu;
+                A0[hh][2] = (ww[0] >> 4) & 0x0F0F0F0Fu; A0[hh][3] = (ww[1] >> 4) & 0x0F0F0F0Fu;
+                A1[hh][0] = ww[2] & 0x0F0F0F0Fu; A1[hh][1] = ww[3] & 0x0F0F0F0Fu;
+                A1[hh][2] = (ww[2] >> 4) & 0x0F0F0F0Fu; A1[hh][3] = (ww[3] >> 4) & 0x0F0F0F0Fu;
             }
         }
 #pragma unroll
@@ -351,8 +386,8 @@ __device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB
         const uint32_t sel = 0x7044u | ((uint32_t)t << 8);   // byte t -> bits 16..23 of 2.0f
 #pragma unroll
         for (int rw = 0; rw < 2; rw++) {
-            const uint4 hd = *reinterpret_cast<const uint4*>((rw ? cB : cA) + 16 * gid);
-            const float d = h2f((uint16_t)(hd.x & 0xFFFF)), dmin = h2f((uint16_t)(hd.x >> 16));
+            const uint4 h4 = hd[rw];
+            const float d = h2f((uint16_t)(h4.x & 0xFFFF)), dmin = h2f((uint16_t)(h4.x >> 16));
             const float da = kq * d, db = -2.f * kq * d, ma = 64.f * dmin, mb = -128.f * dmin;
             // GetScaleMinK4 (BlockDequantizer.cs:155-166), four sub-blocks per word:
             // sc[0..3] = q[0..3] & 63, m[0..3] = q[4..7] & 63,
@@ -360,8 +395,8 @@ __device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB
 #pragma unroll
             for (int hh = 0; hh < NH; hh++) {
                 const int h = FULL ? hh : half;
-                const uint32_t SC = h ? ((hd.w & 0x0F0F0F0Fu) | ((hd.y >> 2) & 0x30303030u)) : (hd.y & 0x3F3F3F3Fu);
-                const uint32_t MN = h ? (((hd.w >> 4) & 0x0F0F0F0Fu) | ((hd.z >> 2) & 0x30303030u)) : (hd.z & 0x3F3F3F3Fu);
+                const uint32_t SC = h ? ((h4.w & 0x0F0F0F0Fu) | ((h4.y >> 2) & 0x30303030u)) : (h4.y & 0x3F3F3F3Fu);
+                const uint32_t MN = h ? (((h4.w >> 4) & 0x0F0F0F0Fu) | ((h4.z >> 2) & 0x30303030u)) : (h4.z & 0x3F3F3F3Fu);
                 // byte b at bits 16..23 of 2.0f reads 2 + b/64: d*b = F*64d - 128d (the
                 // high-nibble groups take another 1/16)
                 ar[hh][rw] = fmaf(__uint_as_float(prmt(SC, 0x40000000u, sel)), da, db);
@@ -371,8 +406,7 @@ __device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB
     } else {
 #pragma unroll
         for (int hh = 0; hh < NH; hh++) {
-            const int o = 16 * gid + 2 * (t + 4 * (FULL ? hh : half));
-            const float dA = h2f(*reinterpret_cast<const uint16_t*>(cA + o)), dB = h2f(*reinterpret_cast<const uint16_t*>(cB + o));
+            const float dA = h2f((uint16_t)dd[hh][0]), dB = h2f((uint16_t)dd[hh][1]);
             ar[hh][0] = dA;
             ar[hh][1] = dB;
             mr[hh][0] = FMT == Q4_0 ? 8.f * dA : 0.f;
@@ -381,16 +415,14 @@ __device__ __forceinline__ void stream_unit(const uint8_t* cA, const uint8_t* cB
     }
 #pragma unroll
     for (int hh = 0; hh < NH; hh++) {
-        const int so = xtab_ss(K) + 8 * (8 * sbg + 4 * (FULL ? hh : half) + t);
 #pragma unroll
         for (int q = 0; q < NTK; q++) {
             if (q == 0 || q < nt) {
-                const uint2 u = L::ld64(tq[q], so);
-                const float sc = __uint_as_float(u.x), sum = __uint_as_float(u.y);
+                const float scl = __uint_as_float(ss[hh][q].x), sum = __uint_as_float(ss[hh][q].y);
                 const float c0 = (float)(X[hh][q][0] * 256 + X[hh][q][1]), c1 = (float)(X[hh][q][2] * 256 + X[hh][q][3]);
                 float a = y[q][0], b = y[q][1];
-                a = fmaf(ar[hh][0], c0 * sc, a);
-                b = fmaf(ar[hh][1], c1 * sc, b);
+                a = fmaf(ar[hh][0], c0 * scl, a);
+                b = fmaf(ar[hh][1], c1 * scl, b);
                 if (FMT != Q8_0) {
                     a = fmaf(-mr[hh][0], sum, a);
                     b = fmaf(-mr[hh][1], sum, b);
