@@ -136,7 +136,8 @@ struct StreamConfig {
     int stage_bytes;   // ring slot size (the larger segment)
     int xtab_bytes;    // per token table (16-byte multiple)
     int res_rows;      // > 0: all table rows resident in shared memory; 0: tables read from global
-    int red_bytes;     // one reduction slot: [CW][chunk tokens][16] floats
+    int red_bytes;     // one reduction slot: [CW][red_tok][16] floats
+    int red_tok;       // tokens per reduction slot: min(chunk tokens, tokens of the launch)
     int cw;            // consumer warps
 };
 
@@ -192,10 +193,11 @@ __host__ inline int stream_target_bytes() {
 // which every segment has a balanced geometry, 12 or more warps first (they
 // hide the MMA and shared-load latencies), then the most segments on whole
 // super-block units, then the most warps (QRM_STREAM_CW forces a count for
-// tuning runs).  tab_rows = table rows the launch reads;
+// tuning runs).  max_tok = the most tokens of one expert slot (the launch's
+// tokens).  tab_rows = table rows the launch reads;
 // they are kept resident when that leaves at least four stages, else read
 // from global memory.
-__host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols, int ntk, int tab_rows,
+__host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols, int ntk, int tab_rows, int max_tok,
                                  int smem_budget, StreamConfig* c) {
     if (fmt[0] < 0 && fmt[1] < 0) return false;
     const int target = stream_target_bytes();
@@ -227,7 +229,8 @@ __host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols,
     for (int i = 0; i < 2; i++)
         if (fmt[i] >= 0) c->stage_bytes = std::max(c->stage_bytes, c->seg[i].stage_bytes);
     c->xtab_bytes = xtab_stride(cols);
-    c->red_bytes = c->cw * stream_chunk(ntk) * 16 * 4;
+    c->red_tok = std::max(1, std::min(stream_chunk(ntk), max_tok));
+    c->red_bytes = c->cw * c->red_tok * 16 * 4;
     const long long avail = (long long)smem_budget - kStreamDataOff - (long long)kStreamRedSlots * c->red_bytes;
     const long long res = (long long)tab_rows * c->xtab_bytes;
     long long s_res = res < avail ? (avail - res) / c->stage_bytes : 0;
@@ -457,7 +460,6 @@ template <int M, int NTK>
 __device__ __forceinline__ void stream_reduce(const GemvParams& p, const StreamConfig& cfg, const StreamJob& j,
                                               const StreamRed& R, int lane) {
     constexpr int OUT = M == 2 ? 8 : 16;   // outputs per MMA tile and token
-    constexpr int C = stream_chunk(NTK);
     const int r16 = j.seg ? cfg.seg[1].r16 : cfg.seg[0].r16, wpt = cfg.cw / r16;
     const int sq = j.r % kStreamRedSlots;
     const float* red = R.buf + (size_t)sq * R.floats;
@@ -468,7 +470,7 @@ __device__ __forceinline__ void stream_reduce(const GemvParams& p, const StreamC
 #pragma unroll
         for (int m = 0; m < M; m++) {
             float sum = 0.f;
-            for (int w = i * wpt; w < (i + 1) * wpt; w++) sum += red[(w * C + q) * 16 + m * 8 + r];
+            for (int w = i * wpt; w < (i + 1) * wpt; w++) sum += red[(w * cfg.red_tok + q) * 16 + m * 8 + r];
             v[m] = sum;
         }
         const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
@@ -778,7 +780,7 @@ expert_stream_kernel(GemvParams p, StreamConfig cfg, int32_t* err) {
                     v += __shfl_xor_sync(0xffffffffu, v, 1);
                     v += __shfl_xor_sync(0xffffffffu, v, 2);
                     const int tq = ps * NTK + q;
-                    if ((lane & 3) == 0 && tq < nc) red[(warp * C + tq) * 16 + gid + 8 * hh] = v;
+                    if ((lane & 3) == 0 && tq < nc) red[(warp * cfg.red_tok + tq) * 16 + gid + 8 * hh] = v;
                 }
         __threadfence_block();
         __syncwarp();

@@ -230,7 +230,7 @@ bool stream_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p,
     if (fb >= 0 && !imma_usable(fb, p.rows, p.cols, gateup)) return false;
     sel->ntk = T <= 1 ? 1 : 2;
     const int fmts[2] = {fa, fb};
-    return qrm::stream_plan(fmts, gateup ? 2 : 1, p.rows, p.cols, sel->ntk, p.xtab_rows, 227 * 1024, &sel->cfg);
+    return qrm::stream_plan(fmts, gateup ? 2 : 1, p.rows, p.cols, sel->ntk, p.xtab_rows, T, 227 * 1024, &sel->cfg);
 }
 
 // segment formats of a launch of mode p.mode whose matrices are all format fmt
