@@ -56,7 +56,9 @@ def measured_peaks():
 # ------------------------------------------------------------------ clocks
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms in the background;
+    start() returns once the first sample is written (at most ~3 s), so a short
+    timed region still falls inside the sampling."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -72,8 +74,13 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.errf = open(self.path + ".err", "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.ident}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=self.fh, stderr=self.errf)
+            t0 = time.time()
+            while time.time() - t0 < 3.0 and self.proc.poll() is None:
+                if os.path.getsize(self.path) > 0:
+                    break
+                time.sleep(0.01)
         except Exception as ex:
             self.proc = None
             self.error = str(ex)
