@@ -55,6 +55,66 @@ def measured_peaks():
 
 # ------------------------------------------------------------------ clocks
 
+class NvmlClockSampler:
+    """SM clock and clock-event reasons read through NVML by a background
+    thread every ~1 ms between start() and stop(), so that even a timed region
+    of a few milliseconds holds many samples."""
+    NAMES = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+             ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+             ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+             ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, uuid):
+        import threading
+        import pynvml as N
+        self.N = N
+        N.nvmlInit()
+        self.h = N.nvmlDeviceGetHandleByUUID(uuid)
+        self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM))
+        self.samples = []
+        self.reasons = 0
+        self.stop_ev = threading.Event()
+        self.thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        N = self.N
+        while not self.stop_ev.is_set():
+            try:
+                self.samples.append(float(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)))
+                self.reasons |= int(N.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            except Exception:
+                pass
+            time.sleep(0.001)
+
+    def start(self):
+        self.thread.start()
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 1.0:
+            time.sleep(0.001)
+
+    def stop(self):
+        self.stop_ev.set()
+        self.thread.join(timeout=5)
+        N = self.N
+        reasons = sorted(n for n, c in self.NAMES if self.reasons & getattr(N, c))
+        try:
+            N.nvmlShutdown()
+        except Exception:
+            pass
+        if not self.samples:
+            return {"error": "no NVML samples"}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
+
+
+def clock_sampler(ident):
+    """NVML sampler when pynvml works on this box, else nvidia-smi."""
+    try:
+        return NvmlClockSampler(ident)
+    except Exception:
+        return ClockSampler(ident)
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 20 ms in the background;
     start() returns once the first sample is written (at most ~3 s), so a short
@@ -304,7 +364,7 @@ def run_ours(args, rank, world, dist):
         ident = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
         ident = str(dev)
-    clocks = ClockSampler(ident)
+    clocks = clock_sampler(ident)
     layer.set_profiling(False)
     if dist:
         dist.barrier()

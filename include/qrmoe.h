@@ -11,7 +11,7 @@
  * operator DotKernels.MatVecParallel(QuantFormat, byte* w, long rows,
  * long cols, float* x, float* y) (src/QuantRunner.Core/Kernels/
  * DotKernels.cs:610).  A P/Invoke shim binds the entry points below so the
- * engine can hand a whole MoE layer to the GPU (see INTEGRATION.md).
+ * engine can hand a whole MoE layer to the GPU.
  *
  * Conventions: every function returns QRM_OK (0) or a negative QRM_E_* code;
  * qrm_last_error() then describes the failure (thread-local, valid until the
@@ -178,7 +178,10 @@ int  qrm_matrix_gemv(qrm_matrix* m, const float* x_dev, int T, float* y_dev, voi
  *   - the array is shared by every call on the device: calls that overlap
  *     in time (other streams, other threads, other matrices) race on it;
  *   - the first call on each device looks up the array's address
- *     (cudaGetSymbolAddress) and must come before any stream capture.
+ *     (cudaGetSymbolAddress) and must come before any stream capture;
+ *   - that address is kept for the life of the process: it does not survive
+ *     a cudaDeviceReset of the device, after which this entry point must not
+ *     be called again in the same process.
  * Nothing needs to start at zero: every table byte read is written first. */
 int  qrm_matrix_gemv_static(qrm_matrix* m, const float* x_dev, int T, float* y_dev, void* stream);
 

@@ -422,14 +422,39 @@ static bool ep_barrier(qrm_layer* L) {
     return false;
 }
 
+// Waits up to `ms` milliseconds for the stream's work to finish.
+static bool drain_stream(cudaStream_t s, int ms) {
+    for (int i = 0; i < ms; i++) {
+        cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess) return true;
+        if (e != cudaErrorNotReady) return false;
+        struct timespec ts{0, 1000000};
+        nanosleep(&ts, nullptr);
+    }
+    return false;
+}
+
 static void free_layer(qrm_layer* L) {
     if (!L) return;
     cudaSetDevice(L->desc.device);
-    if (L->stream) cudaStreamSynchronize(L->stream);
     bool met = true;
+    if (L->stream) {
+        // an expert-parallel forward whose collective waits for a rank that
+        // left never ends by itself: bounded
+        if (L->world > 1) met = drain_stream(L->stream, 10000);
+        else cudaStreamSynchronize(L->stream);
+    }
+    // every rank meets here before its mailbox goes away (no peer writes into
+    // it afterwards); bounded, false when a rank did not arrive
+    if (met && L->comm) met = ep_barrier(L);
+    if (!met && L->comm) {
+        // abort first: it ends this communicator's kernels still in flight, so
+        // the device-synchronising calls below (stream sync, cudaFree) cannot
+        // wait behind a collective that never completes
+        ncclCommAbort(L->comm);
+        L->comm = nullptr;
+    }
     if (L->p2p) {
-        // no peer writes into this mailbox once every rank is here
-        met = ep_barrier(L);
         for (void* p : L->peer_open) cudaIpcCloseMemHandle(p);
         L->peer_open.clear();
     }
@@ -449,10 +474,7 @@ static void free_layer(qrm_layer* L) {
     for (cudaEvent_t e : L->ev)
         if (e) cudaEventDestroy(e);
     if (L->stream) cudaStreamDestroy(L->stream);
-    if (L->comm) {
-        if (met) ncclCommDestroy(L->comm);
-        else ncclCommAbort(L->comm);
-    }
+    if (L->comm) ncclCommDestroy(L->comm);   // every rank met: nothing of it is in flight
     delete L;
 }
 
