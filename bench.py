@@ -1,20 +1,28 @@
 #!/usr/bin/env python
 """bench.py -- MoE-layer tokens/s and expert-weight HBM GB/s on B200.
 
-Workload (the north-star layer): GLM-style sigmoid
-MoE, d_model 7168, 256 routed experts of d_ff 2048 in Q4_K plus one shared
-expert in Q8_0, top-8 with router bias N(0,0.01), weights renormalised and
-scaled by 2.5, router logits skewed by per-expert offsets N(0,1.5); weights
-N(0,0.02) from a seed, activations N(0,1) then RMSNorm.  A step is one
-forward of the layer over --tokens tokens per GPU (decode: 1).
+Default workload (the north-star layer): GLM-style
+sigmoid MoE, d_model 7168, 256 routed experts of d_ff 2048 in Q4_K plus one
+shared expert in Q8_0, top-8 with router bias N(0,0.01), weights
+renormalised and scaled by 2.5, router logits skewed by per-expert offsets
+N(0,1.5); weights N(0,0.02) from seeds, activations N(0,1) then RMSNorm.  A
+step is one forward of the layer over --tokens tokens per GPU (decode: 1).
+--config c1..c5 selects another BASELINE config (one layer of it), --sweep
+prints one line per (config, T) of the measurement plan.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--config c5]
+  python bench.py --sweep [--steps K]
   python bench.py --impl reference ...   # the reference CPU algorithm on the host cores
 
 Timing: W untimed warm-up steps, then K steps each timed with CUDA events on
 the forward's stream; L2 is flushed (256 MiB write) before every step outside
 the events, and each step feeds new tokens (so new experts).  Multi-GPU: one
-process per GPU under torchrun; value = all ranks' tokens / max-over-ranks time.
+process per GPU under torchrun; value = all ranks' tokens / max-over-ranks
+time.  e2e = the drop-in call (qrm_forward: pageable host arrays in and out,
+synchronous) timed by wall clock; e2e_pinned = the same forward with pinned
+host buffers, the copies inside CUDA events.  The first timed step's tokens
+are checked against the CPU oracle after the timed region (routing bit for
+bit, outputs as max relative error).
 """
 import argparse
 import json
@@ -29,14 +37,23 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-WORKLOAD = dict(name="c5_glm_sigmoid_256e_top8_q4k_shared_q8_0", d_model=7168, expert_ffn=2048, n_experts=256,
-                n_active=8, moe_sigmoid=1, routed_scale=2.5, n_shared=1, swiglu_limit=0.0, rms_eps=1e-5,
-                fmt=(6, 6, 6), shared_fmt=(4, 4, 4), weight_sigma=0.02, router_sigma=0.02, bias_sigma=0.01,
-                offset_sigma=1.5)
+from tests.moe_case import CONFIGS  # noqa: E402  (shapes only)
+
 METRIC = "MoE-layer tokens/s + expert-weight HBM GB/s vs 8 TB/s peak, 1/2/4/8 B200"
-SEED = 0x51520000 + 5 * 0x100  # config 5, layer 0
+NAMES = {
+    "c1": "c1_mixtral_small_8e_top2_q4_0",
+    "c2": "c2_mixtral_8x7b_layer_8e_top2_q4k",
+    "c3": "c3_glm_sigmoid_160e_top8_q4k_q6k_shared",
+    "c4": "c4_ternary_prefill_64e_top6_tri",
+    "c5": "c5_glm_sigmoid_256e_top8_q4k_shared_q8_0",
+}
+FORMATS = {"c1": "Q4_0", "c2": "Q4_K", "c3": "gate/up Q4_K, down Q6_K, shared same",
+           "c4": "TRI (QuantizeTriLegacy)", "c5": "routed Q4_K, shared Q8_0"}
+SWEEP = [("c5", 1), ("c5", 4), ("c5", 16), ("c5", 64), ("c5", 256), ("c5", 1024), ("c5", 4096),
+         ("c1", 1), ("c1", 32), ("c2", 1), ("c2", 8), ("c2", 64), ("c3", 1), ("c3", 16), ("c3", 256),
+         ("c4", 2048)]
 NOMINAL_HBM_GBS = 8000.0
-FALLBACK_HBM_GBS = 6650.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -50,7 +67,7 @@ def measured_peaks():
         with open(p) as fh:
             return json.load(fh), "measured"
     except Exception:
-        return {"hbm_gbs": FALLBACK_HBM_GBS}, "fallback"
+        return dict(FALLBACK), "fallback"
 
 
 # ------------------------------------------------------------------ clocks
@@ -107,18 +124,9 @@ class NvmlClockSampler:
                 "samples": len(self.samples), "source": "nvml"}
 
 
-def clock_sampler(ident):
-    """NVML sampler when pynvml works on this box, else nvidia-smi."""
-    try:
-        return NvmlClockSampler(ident)
-    except Exception:
-        return ClockSampler(ident)
-
-
-class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 20 ms in the background;
-    start() returns once the first sample is written (at most ~3 s), so a short
-    timed region still falls inside the sampling."""
+class SmiClockSampler:
+    """nvidia-smi clocks / throttle reasons every 20 ms (used when NVML is not
+    reachable from Python)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -132,10 +140,9 @@ class ClockSampler:
     def start(self):
         try:
             self.fh = open(self.path, "w")
-            self.errf = open(self.path + ".err", "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.ident}", f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "20"],
-                                         stdout=self.fh, stderr=self.errf)
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
             t0 = time.time()
             while time.time() - t0 < 3.0 and self.proc.poll() is None:
                 if os.path.getsize(self.path) > 0:
@@ -154,10 +161,6 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
-        self.errf.close()
-        with open(self.path + ".err") as fh:
-            err = fh.read().strip()
-        os.unlink(self.path + ".err")
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as fh:
@@ -175,74 +178,104 @@ class ClockSampler:
                         reasons.add(n)
         os.unlink(self.path)
         if not sm:
-            return {"error": err[-300:] or "no samples"}
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+            return {"error": "no samples"}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvidia-smi"}
+
+
+def clock_sampler(ident):
+    try:
+        return NvmlClockSampler(ident)
+    except Exception:
+        return SmiClockSampler(ident)
 
 
 # ------------------------------------------------------------------ CPU leg
 
-def cpu_sample(steps, warmup, budget_s=None, seed=SEED):
-    """Times the reference CPU algorithm (the oracle restatement of
-    StreamingEngine.GlmMoeFfn, MatVecParallel over nproc-1 threads) one token
-    per step on the host cores.  Expert matrices come from a pool of 8
-    distinct seeded experts (expert e uses pool entry e % 8): the CPU cost does
-    not depend on the values, and generating all 256 on the host would take
-    minutes.  Returns (tokens/s, threads, sample description)."""
+def cpu_case(cfg_name, seed=1):
+    """The config's full-size layer for the CPU restatement, on the host.
+    Expert matrices come from a pool of at most 8 distinct seeded experts
+    (expert e uses pool entry e % 8): the CPU cost does not depend on the
+    values, and generating every expert on the host would take minutes."""
     from tests import oracle_api as O  # the oracle: CPU baseline only
-    W = WORKLOAD
-    d, f, E = W["d_model"], W["expert_ffn"], W["n_experts"]
+    from tests.moe_case import MoeCase, storage_fmt
+    c = CONFIGS[cfg_name]
+    d, f, E = c["d_model"], c["expert_ffn"], c["n_experts"]
     rng = np.random.default_rng(seed)
-    pool = 8
+    pool = min(8, E)
 
     def q(fmt, rows, cols):
-        return O.quantize(fmt, (rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(W["weight_sigma"])))
+        return O.quantize(fmt, rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02))
 
-    gates = [q(6, f, d) for _ in range(pool)]
-    ups = [q(6, f, d) for _ in range(pool)]
-    downs = [q(6, d, f) for _ in range(pool)]
+    fq = c["fmt"]
+    mats = [[q(fq[w], *((d, f) if w == 2 else (f, d))) for _ in range(pool)] for w in range(3)]
+    shared, fmt_sh = None, (0, 0, 0)
+    if c["n_shared"] and c["moe_sigmoid"]:
+        sf = c.get("shared_fmt", fq)
+        shared = tuple(q(sf[w], *((d, f) if w == 2 else (f, d))) for w in range(3))
+        fmt_sh = tuple(storage_fmt(x) for x in sf)
+    case = MoeCase(cfg=c, norm_w=np.ones(d, np.float32),
+                   router=rng.standard_normal((E, d), dtype=np.float32) * np.float32(0.02),
+                   router_bias=(rng.standard_normal(E) * c["bias_sigma"]).astype(np.float32)
+                   if c.get("bias_sigma") else None,
+                   logit_offset=(rng.standard_normal(E) * c["offset_sigma"]).astype(np.float32)
+                   if c.get("offset_sigma") else None,
+                   gate=[mats[0][e % pool] for e in range(E)], up=[mats[1][e % pool] for e in range(E)],
+                   down=[mats[2][e % pool] for e in range(E)], fmt_gate=storage_fmt(fq[0]),
+                   fmt_up=storage_fmt(fq[1]), fmt_down=storage_fmt(fq[2]), shared=shared, fmt_sh=fmt_sh)
+    case.pool = pool
+    return case
 
-    class Case:
-        pass
 
-    c = Case()
-    c.cfg = dict(d_model=d, n_experts=E, n_active=W["n_active"], expert_ffn=f, moe_sigmoid=1,
-                 routed_scale=W["routed_scale"], n_shared=1, swiglu_limit=0.0, rms_eps=W["rms_eps"])
-    c.norm_w = np.ones(d, np.float32)
-    c.router = (rng.standard_normal((E, d), dtype=np.float32) * np.float32(W["router_sigma"]))
-    c.router_bias = (rng.standard_normal(E) * W["bias_sigma"]).astype(np.float32)
-    c.logit_offset = (rng.standard_normal(E) * W["offset_sigma"]).astype(np.float32)
-    c.gate = [gates[e % pool] for e in range(E)]
-    c.up = [ups[e % pool] for e in range(E)]
-    c.down = [downs[e % pool] for e in range(E)]
-    c.fmt_gate = c.fmt_up = c.fmt_down = 6
-    c.shared = (q(4, f, d), q(4, f, d), q(4, d, f))
-    c.fmt_sh = (4, 4, 4)
+def cpu_time(case, cfg_name, T, budget_s, seed=2):
+    """Times the reference CPU algorithm (the oracle restatement of
+    StreamingEngine.MoeFfn / GlmMoeFfn with MatVecParallel over nproc-1
+    threads, one Forward call per token as the engine runs) on host tokens
+    until budget_s has passed (at most the T tokens of one step).  Returns
+    (tokens/s, threads, sample description)."""
+    from tests import oracle_api as O  # the oracle: CPU baseline only
+    c = CONFIGS[cfg_name]
+    d = c["d_model"]
+    rng = np.random.default_rng(seed)
     threads = max(1, (os.cpu_count() or 2) - 1)
-    xs = rng.standard_normal((warmup + steps, 1, d), dtype=np.float32)
-    for i in range(warmup):
-        O.moe_forward(c, xs[i], O.APPLY_NORM, threads)
+    flags = O.APPLY_NORM | (0 if c["moe_sigmoid"] else O.ADD_RESIDUAL)
+    O.moe_forward(case, rng.standard_normal((1, d), dtype=np.float32), flags, threads)   # warm-up
     t0 = time.perf_counter()
     done = 0
-    for i in range(steps):
-        O.moe_forward(c, xs[warmup + i], O.APPLY_NORM, threads)
+    while done < T:
+        O.moe_forward(case, rng.standard_normal((1, d), dtype=np.float32), flags, threads)
         done += 1
-        if budget_s is not None and time.perf_counter() - t0 > budget_s:
+        if time.perf_counter() - t0 > budget_s:
             break
     dt = time.perf_counter() - t0
-    desc = (f"{done} decode tokens (T=1 each) of the full-size layer through the C++ restatement of "
-            f"StreamingEngine.GlmMoeFfn with MatVecParallel over {threads} threads; 8 distinct seeded experts "
-            f"reused across the 256 expert slots")
+    desc = (f"{done} of the {T} tokens of a step of the full-size {cfg_name} layer, one Forward call each, through "
+            f"the C++ restatement of StreamingEngine.{'GlmMoeFfn' if c['moe_sigmoid'] else 'MoeFfn'} with "
+            f"MatVecParallel over {threads} threads; {case.pool} distinct seeded experts reused across the "
+            f"{c['n_experts']} slots")
     return done / dt, threads, desc
+
+
+def cpu_sample(cfg_name, T, budget_s):
+    return cpu_time(cpu_case(cfg_name), cfg_name, T, budget_s)
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    val, threads, desc = cpu_sample(args.steps, args.warmup)
+    cfg_name, T = args.config, args.tokens
+    # each step a bounded sample of that step's tokens, the whole run within a few minutes
+    per_step = max(0.5, min(10.0, 120.0 / (args.steps + args.warmup)))
+    vals = []
+    case = cpu_case(cfg_name)
+    for i in range(args.warmup + args.steps):
+        v, threads, desc = cpu_time(case, cfg_name, T, per_step, seed=2 + i)
+        if i >= args.warmup:
+            vals.append(v)
+    val = float(np.mean(vals))
     line = dict(metric=METRIC, value=val, unit="tokens/s", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
-                ms_per_step=1000.0 / val, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f32",
+                ms_per_step=1000.0 * T / val, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="f32",
                 data="synthetic", impl="reference",
-                config=dict(workload=WORKLOAD["name"], tokens_per_step=1, parallelism="host threads"),
+                config=dict(workload=NAMES[cfg_name], tokens_per_rank=T, parallelism="host threads"),
                 cpu_baseline=dict(value=val, unit="tokens/s", cores=threads, kind="port", sample=desc),
                 e2e=dict(value=val, unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     print(json.dumps(line), flush=True)
@@ -251,67 +284,20 @@ def run_reference(args, rank, world):
 
 # ------------------------------------------------------------------ GPU leg
 
-def build_layer(torch, Q, dev, T, seed=SEED, rank=0, world=1, nccl_id=None):
-    """The workload's layer; with world > 1 an expert-parallel layer holding
-    this rank's block of routed experts (the weights are the same on every
-    rank: each expert is generated from its own seed)."""
-    W = WORKLOAD
-    d, f, E = W["d_model"], W["expert_ffn"], W["n_experts"]
-    layer = Q.MoeLayer(d, E, W["n_active"], f, moe_sigmoid=True, routed_scale=W["routed_scale"],
-                       n_shared=W["n_shared"], swiglu_limit=W["swiglu_limit"], rms_eps=W["rms_eps"],
-                       fmt=W["fmt"], shared_fmt=W["shared_fmt"], device=dev, max_tokens=T,
-                       rank=rank, world=world, nccl_id=nccl_id)
-    n = f * d
-    tmp = torch.empty(n, dtype=torch.float32, device=f"cuda:{dev}")
-    qbuf = torch.empty(Q.tensor_bytes(n, 4), dtype=torch.uint8, device=f"cuda:{dev}")
-
-    def synth(expert, which, fmt, s):
-        Q.synth_gaussian(tmp.data_ptr(), n, s, W["weight_sigma"])
-        nb = Q.tensor_bytes(n, fmt)
-        Q.synth_quantize(fmt, tmp.data_ptr(), n, qbuf.data_ptr())
-        layer.upload_expert_device(expert, which, fmt, qbuf.data_ptr(), nb)
-
-    first, count = layer.expert_range()
-    for e in range(first, first + count):
-        for w in range(3):
-            synth(e, w, W["fmt"][w], seed * 4096 + e * 3 + w)
-    for w in range(3):
-        synth(Q.SHARED_EXPERT, w, W["shared_fmt"][w], seed * 4096 + E * 3 + w)
-    small = torch.empty(E * d, dtype=torch.float32, device=f"cuda:{dev}")
-    Q.synth_gaussian(small.data_ptr(), E * d, seed + 1, W["router_sigma"])
-    router = small.cpu().numpy().reshape(E, d)
-    Q.synth_gaussian(small.data_ptr(), E, seed + 2, W["bias_sigma"])
-    bias = small[:E].cpu().numpy()
-    Q.synth_gaussian(small.data_ptr(), E, seed + 3, W["offset_sigma"])
-    offset = small[:E].cpu().numpy()
-    layer.upload_router(router, bias)
-    layer.upload_logit_offset(offset)
-    layer.upload_norm(np.ones(d, np.float32))  # synthetic norms are ones (Program.cs:357-360)
-    torch.cuda.synchronize()
-    return layer
+def expert_flops(cfg, counts, T, shared):
+    """2 * MACs of the expert products of one forward: per routed assignment
+    and shared token 3 d*f (gate, up, down)."""
+    d, f = cfg["d_model"], cfg["expert_ffn"]
+    rows = int(counts.sum()) + (T if shared else 0)
+    return 2.0 * rows * 3 * d * f, 2.0 * rows * 2 * d * f, 2.0 * rows * d * f
 
 
-def traffic_from_profiles():
-    """dram bytes per gate/up launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "expert_stream_c5_decode.md")
-    try:
-        with open(p) as fh:
-            for line in fh:
-                if line.startswith("dram_bytes_per_launch:"):
-                    return float(line.split(":")[1])
-    except Exception:
-        pass
-    return None
-
-
-def run_ours(args, rank, world, dist):
-    import torch
-    import qauntrunner_b200 as Q
+def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
+    from tests.synth_layer import SynthLayer
     dev = int(os.environ.get("LOCAL_RANK", 0))
-    torch.cuda.set_device(dev)
-    T = args.tokens
-    W = WORKLOAD
-    d = W["d_model"]
+    cfg = CONFIGS[cfg_name]
+    d, E = cfg["d_model"], cfg["n_experts"]
+    spec = SynthLayer(cfg_name)
     t_build = time.perf_counter()
     nccl_id = None
     if world > 1:
@@ -321,22 +307,23 @@ def run_ours(args, rank, world, dist):
             idt.copy_(torch.frombuffer(bytearray(Q.nccl_unique_id()), dtype=torch.uint8))
         dist.broadcast(idt, 0)
         nccl_id = bytes(idt.cpu().numpy().tobytes())
-    layer = build_layer(torch, Q, dev, T, seed=SEED, rank=rank, world=world, nccl_id=nccl_id)
-    log(f"[rank {rank}] layer built in {time.perf_counter() - t_build:.1f}s")
+    layer = spec.build(torch, Q, dev, T, rank=rank, world=world, nccl_id=nccl_id)
+    log(f"[rank {rank}] {cfg_name} layer built in {time.perf_counter() - t_build:.1f}s")
+    flags = Q.APPLY_NORM | (0 if cfg["moe_sigmoid"] else Q.ADD_RESIDUAL)
     nsteps = args.warmup + args.steps
+    nx = min(nsteps, max(2, (1 << 30) // max(1, T * d * 4)))     # distinct input batches (<= 1 GiB)
     g = torch.Generator(device=f"cuda:{dev}")
-    g.manual_seed(SEED + 17 + rank)
-    xs = torch.randn((nsteps, T, d), generator=g, device=f"cuda:{dev}", dtype=torch.float32)
+    g.manual_seed(spec.seed + 17 + rank)
+    xs = torch.randn((nx, T, d), generator=g, device=f"cuda:{dev}", dtype=torch.float32)
     out = torch.empty((T, d), dtype=torch.float32, device=f"cuda:{dev}")
     idx = torch.empty((T, layer.k), dtype=torch.int32, device=f"cuda:{dev}")
     wts = torch.empty((T, layer.k), dtype=torch.float32, device=f"cuda:{dev}")
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{dev}")
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
-    flags = Q.APPLY_NORM
 
     def step(i):
-        layer.forward_device(xs[i].data_ptr(), T, out.data_ptr(), flags, idx.data_ptr(), wts.data_ptr(), sp)
+        layer.forward_device(xs[i % nx].data_ptr(), T, out.data_ptr(), flags, idx.data_ptr(), wts.data_ptr(), sp)
 
     # expert parallel: the ranks' forwards wait for one another, so every rank
     # leaves the L2 flush together (a one-element all-reduce on the stream,
@@ -383,10 +370,12 @@ def run_ours(args, rank, world, dist):
     layer.sync()
     step_ms = [ev0[i].elapsed_time(ev1[i]) for i in range(args.steps)]
     total_ms = float(sum(step_ms))
+    launches_per_step = layer.last_launch_count()
 
     # ---- per-stage breakdown (library events inside the forward graph), same inputs
     stage_ms = np.zeros(Q.STAGE_COUNT)
     stage_bytes = np.zeros(Q.STAGE_COUNT)
+    stage_flops = np.zeros(3)
     nprof = min(args.steps, 64)
     if world == 1:
         layer.set_profiling(True)
@@ -397,19 +386,22 @@ def run_ours(args, rank, world, dist):
                 ms, by = layer.last_profile()
                 stage_ms += ms
                 stage_bytes += by
+                _, off = layer.last_dispatch(T)
+                stage_flops += np.array(expert_flops(cfg, np.diff(off), T, spec.shared))
         layer.set_profiling(False)
         torch.cuda.synchronize()
         layer.sync()
 
-    # ---- e2e: host (pinned) buffers through the C ABI, copies inside the timed region
-    xh = xs.cpu().pin_memory()
+    # ---- e2e (pinned): host buffers, copies inside the events
+    nh = min(nx, args.steps + args.warmup)
+    xh = xs[:nh].cpu().pin_memory()
     oh = torch.empty((T, d), dtype=torch.float32).pin_memory()
     xd = torch.empty((T, d), dtype=torch.float32, device=f"cuda:{dev}")
     e0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     e1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
-            xd.copy_(xh[i], non_blocking=True)
+            xd.copy_(xh[i % nh], non_blocking=True)
             layer.forward_device(xd.data_ptr(), T, out.data_ptr(), flags, None, None, sp)
             oh.copy_(out, non_blocking=True)
         torch.cuda.synchronize()
@@ -418,7 +410,7 @@ def run_ours(args, rank, world, dist):
         for i in range(args.steps):
             flush_l2(i)
             e0[i].record(stream)
-            xd.copy_(xh[args.warmup + i], non_blocking=True)
+            xd.copy_(xh[(args.warmup + i) % nh], non_blocking=True)
             layer.forward_device(xd.data_ptr(), T, out.data_ptr(), flags, None, None, sp)
             oh.copy_(out, non_blocking=True)
             e1[i].record(stream)
@@ -426,25 +418,72 @@ def run_ours(args, rank, world, dist):
     layer.sync()
     if dist:
         dist.barrier()
-    e2e_ms = float(sum(e0[i].elapsed_time(e1[i]) for i in range(args.steps)))
+    e2e_pinned_ms = float(sum(e0[i].elapsed_time(e1[i]) for i in range(args.steps)))
+
+    # ---- e2e (drop-in call): qrm_forward on ordinary (pageable) numpy arrays, wall clock
+    xp = [np.ascontiguousarray(xh[i].numpy()) for i in range(nh)]
+    outp = np.empty((T, d), np.float32)
+    idxp = np.empty((T, layer.k), np.int32)
+    wp = np.empty((T, layer.k), np.float32)
+    for i in range(args.warmup):
+        layer.forward_into(xp[i % nh], flags, outp, idxp, wp)
+    if dist:
+        dist.barrier()
+    e2e_ms = 0.0
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        layer.forward_into(xp[(args.warmup + i) % nh], flags, outp, idxp, wp)
+        e2e_ms += (time.perf_counter() - t0) * 1000.0
+
+    # ---- parity of the first timed step's tokens against the oracle (after timing)
+    parity = None
+    if not args.no_parity:
+        from tests.gpu_helpers import check_synth_batch
+        r = check_synth_batch(spec, layer, xh[args.warmup % nh].numpy(), flags, full_limit=8,
+                              check_dispatch=world == 1)
+        parity = dict(routing_bit_exact=r["routing_bit_exact"], max_rel_err=r["err"],
+                      tokens_checked=r["tokens_checked"], tolerance=1e-3)
 
     # ---- max over ranks
-    vals = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=f"cuda:{dev}")
+    vals = torch.tensor([total_ms, e2e_ms, e2e_pinned_ms, parity["max_rel_err"] if parity else 0.0],
+                        dtype=torch.float64, device=f"cuda:{dev}")
     if dist:
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    total_ms, e2e_ms = float(vals[0]), float(vals[1])
+    total_ms, e2e_ms, e2e_pinned_ms = float(vals[0]), float(vals[1]), float(vals[2])
+    if parity:
+        parity["max_rel_err"] = float(vals[3])
     tokens = args.steps * T * world
     value = tokens / (total_ms / 1000.0)
-    e2e_value = tokens / (e2e_ms / 1000.0)
 
     peaks, peak_kind = measured_peaks()
-    peak = float(peaks.get("hbm_gbs", FALLBACK_HBM_GBS))
-    gu_ms, gu_bytes = stage_ms[3], stage_bytes[3]   # over the nprof breakdown steps
-    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else 0.0
-    traffic = traffic_from_profiles()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK["hbm_gbs"]))
+    tensor = float(peaks.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"]))
+    roofline, layer_hbm = None, None
     if world == 1:
-        layer_bytes = (stage_bytes[3] + stage_bytes[4]) / nprof + (W["n_experts"] * d * 4 + T * d * 4 * 2)
-        roof_kernel = "expert gate/up fused dequant GEMV + SwiGLU"
+        gu_ms, dn_ms = stage_ms[3] / nprof, stage_ms[4] / nprof
+        gu_bytes, dn_bytes = stage_bytes[3] / nprof, stage_bytes[4] / nprof
+        _, gu_flops, dn_flops = stage_flops / nprof
+        # the dominant expert stage, bounded by HBM or by the tensor pipe
+        # (whichever its arithmetic intensity says: machine balance = tensor / hbm)
+        if dn_ms > gu_ms:
+            kern, ms_k, by_k, fl_k = "expert down (fused dequant product)", dn_ms, dn_bytes, dn_flops
+        else:
+            kern, ms_k, by_k, fl_k = "expert gate/up (fused dequant product + SwiGLU)", gu_ms, gu_bytes, gu_flops
+        tensor_bound = fl_k / max(by_k, 1.0) > tensor * 1e12 / (hbm * 1e9)
+        if tensor_bound:
+            ach = fl_k / (ms_k / 1000.0) / 1e12 if ms_k > 0 else 0.0
+            roofline = dict(bound="tensor", kernel=kern, achieved=ach, peak=tensor, unit="TFLOP/s",
+                            frac=ach / tensor, peak_kind=f"{peak_kind} bf16_tflops_sustained",
+                            flops_per_launch=fl_k, traffic=None)
+        else:
+            ach = by_k / (ms_k / 1000.0) / 1e9 if ms_k > 0 else 0.0
+            roofline = dict(bound="hbm", kernel=kern, achieved=ach, peak=hbm, unit="GB/s", frac=ach / hbm,
+                            peak_kind=f"{peak_kind} hbm_gbs", bytes_per_launch=by_k, traffic=None)
+        layer_bytes = gu_bytes + dn_bytes + E * d * 4 + T * d * 4 * 2
     else:
         # expert parallelism (no per-stage events): compressed bytes this rank streamed in
         # the last step (its experts that the gathered batch selected + shared expert +
@@ -452,82 +491,89 @@ def run_ours(args, rank, world, dist):
         _, off = layer.last_dispatch(T)
         first, count = layer.expert_range()
         used = int(np.count_nonzero(np.diff(off)[first:first + count]))
-        f = W["expert_ffn"]
-        ebytes = 3 * Q.tensor_bytes(d * f, W["fmt"][0])
-        sbytes = 3 * Q.tensor_bytes(d * f, W["shared_fmt"][0])
-        layer_bytes = used * ebytes + sbytes + W["n_experts"] * d * 4
-        achieved = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
-        traffic = None
-        roof_kernel = "whole layer step per rank (expert parallel: no per-stage events)"
+        f = cfg["expert_ffn"]
+        ebytes = sum(Q.tensor_bytes(d * f, x) for x in spec.fmt)
+        sbytes = sum(Q.tensor_bytes(d * f, x) for x in spec.fmt_sh) if spec.shared else 0
+        layer_bytes = used * ebytes + sbytes + E * d * 4
+        ach = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
+        roofline = dict(bound="hbm", kernel="whole layer step per rank (expert parallel: no per-stage events)",
+                        achieved=ach, peak=hbm, unit="GB/s", frac=ach / hbm, peak_kind=f"{peak_kind} hbm_gbs",
+                        traffic=None)
     layer_gbs = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
-
-    # the library counts the kernel launches of its forward (one graph replay)
-    launches_per_step = layer.last_launch_count()
+    layer_hbm = dict(achieved_gbs=layer_gbs, frac_of_8tbs=layer_gbs / NOMINAL_HBM_GBS, frac_of_measured=layer_gbs / hbm,
+                     bytes_per_step=layer_bytes)
     transport = layer.ep_transport()
     # an expert-parallel layer's close is collective: every rank closes here
     layer.close()
     if rank != 0:
-        return 0
+        return None
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         try:
-            v, cores, desc = cpu_sample(steps=64, warmup=1, budget_s=15.0)
+            v, cores, desc = cpu_sample(cfg_name, T, budget_s=12.0)
             cpu = dict(value=v, unit="tokens/s", cores=cores, kind="port", sample=desc)
         except Exception as ex:  # the baseline must never block the GPU number
             cpu = dict(value=None, unit="tokens/s", cores=None, kind="port", sample=f"failed: {ex}")
     line = dict(
         metric=METRIC, value=value, unit="tokens/s", n_gpus=world, steps=args.steps, warmup=args.warmup,
         ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
-        dtype="f32", data="synthetic",
-        config=dict(workload=WORKLOAD["name"], tokens_per_rank=T, d_model=d, n_experts=W["n_experts"],
-                    top_k=W["n_active"], expert_ffn=W["expert_ffn"], formats="routed Q4_K, shared Q8_0",
+        dtype="expert products: weight codes x 16-bit fixed-point activations (integer MMA, exact int32 sums, "
+              "f32 scales) or dequantised f16 x f16 (tensor MMA, f32 accumulate); routing and combine f32",
+        data="synthetic",
+        config=dict(workload=NAMES[cfg_name], tokens_per_rank=T, d_model=d, n_experts=E, top_k=cfg["n_active"],
+                    expert_ffn=cfg["expert_ffn"], formats=FORMATS[cfg_name],
                     l2="flushed before every step (256 MiB write, outside the timed events)",
                     parallelism="single GPU" if world == 1 else f"ep{world} (expert parallel, {transport} exchanges)"),
-        roofline=dict(bound="hbm", kernel=roof_kernel, achieved=achieved,
-                      peak=peak, unit="GB/s", frac=achieved / peak if peak else None, peak_kind=peak_kind,
-                      traffic=traffic),
-        layer_hbm=dict(achieved_gbs=layer_gbs, frac_of_8tbs=layer_gbs / NOMINAL_HBM_GBS,
-                       frac_of_measured=layer_gbs / peak, bytes_per_step=layer_bytes),
-        stage_ms_per_step={n: float(stage_ms[i] / nprof) for i, n in enumerate(Q.STAGES)},
+        roofline=roofline,
+        layer_hbm=layer_hbm,
+        stage_ms_per_step={n: float(stage_ms[i] / nprof) for i, n in enumerate(Q.STAGES)} if world == 1 else None,
         cpu_baseline=cpu,
-        e2e=dict(value=e2e_value, unit="tokens/s", h2d_bytes_per_step=T * d * 4, d2h_bytes_per_step=T * d * 4),
+        e2e=dict(value=tokens / (e2e_ms / 1000.0), unit="tokens/s", h2d_bytes_per_step=T * d * 4,
+                 d2h_bytes_per_step=T * d * 4 + T * layer.k * 8,
+                 call="qrm_forward, pageable host arrays, wall clock per synchronous call"),
+        e2e_pinned=dict(value=tokens / (e2e_pinned_ms / 1000.0), unit="tokens/s", h2d_bytes_per_step=T * d * 4,
+                        d2h_bytes_per_step=T * d * 4),
+        parity=parity,
         gpu_launches=launches_per_step * args.steps,
         clocks=clock_info,
     )
-    print(json.dumps(line), flush=True)
-    layer.close()
-    return 0
+    return line
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--config", choices=sorted(NAMES), default="c5")
+    ap.add_argument("--sweep", action="store_true", help="one line per (config, T) of the measurement plan")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--experts", type=int, default=None, help="profiling runs only: fewer experts")
+    ap.add_argument("--no-parity", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.experts:
-        WORKLOAD["n_experts"] = args.experts
-        WORKLOAD["name"] += f"_e{args.experts}"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
-    dist = None
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    import torch
+    import qauntrunner_b200 as Q
+    dist = None
     if world > 1:
         import datetime
-        import torch
         import torch.distributed as tdist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         dist = tdist
     try:
-        return run_ours(args, rank, world, dist)
+        runs = SWEEP if args.sweep else [(args.config, args.tokens)]
+        for cfg_name, T in runs:
+            line = run_one(args, cfg_name, T, rank, world, dist, torch, Q)
+            if line is not None:
+                print(json.dumps(line), flush=True)
+        return 0
     finally:
         if dist:
             dist.destroy_process_group()

@@ -115,6 +115,8 @@ int qrm_upload_logit_offset(qrm_layer* layer, const float* offset /* [E] or NULL
  * loads (qrm_download_expert returns the original bytes). */
 int qrm_upload_expert(qrm_layer* layer, int expert, int which, int fmt,
                       const void* bytes, size_t nbytes);
+/* Same from device memory of the layer's device; the call synchronises the
+ * device first, so bytes written by work on any stream are complete. */
 int qrm_upload_expert_device(qrm_layer* layer, int expert, int which, int fmt,
                              const void* bytes_dev, size_t nbytes);
 int qrm_download_expert(qrm_layer* layer, int expert, int which, void* bytes, size_t nbytes);

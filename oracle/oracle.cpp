@@ -791,6 +791,42 @@ void orc_dispatch(const int32_t* sel, int T, int k, int E, int32_t* perm, int32_
 
 // ------------------------------------------------------------ MoE layer
 
+// RMSNorm, router logits (+ harness offset) and top-k of one token: the part
+// of MoeFfn / GlmMoeFfn before the experts (StreamingEngine.cs:259-260,
+// 639-652, 727-767).
+static void route_token(const orc_moe_desc* desc, const orc_moe_weights* w, const float* xt, int flags, int k,
+                        float* xn, float* logits, int32_t* sel, float* wsel, int threads) {
+    const int d = desc->d_model, E = desc->n_experts;
+    if (flags & ORC_APPLY_NORM) orc_rmsnorm(xt, w->norm_w, xn, d, desc->rms_eps);
+    else std::memcpy(xn, xt, sizeof(float) * (size_t)d);
+    // router logits: MatVecParallel(F32) over the [E x d] router
+    orc_matvec_parallel(ORC_F32, (const uint8_t*)w->router, E, d, xn, logits, threads);
+    if (w->logit_offset)
+        for (int e = 0; e < E; e++) logits[e] = logits[e] + w->logit_offset[e];
+    if (desc->moe_sigmoid)
+        orc_route_sigmoid(logits, w->router_bias, E, k, desc->routed_scale, sel, wsel);
+    else
+        orc_route_softmax(logits, E, k, sel, wsel, nullptr);
+}
+
+int orc_moe_route(const orc_moe_desc* desc, const orc_moe_weights* w, const float* x, int T, int flags,
+                  int32_t* topk_idx, float* topk_w, float* logits_out, float* xn_out, int threads) {
+    const int d = desc->d_model, E = desc->n_experts;
+    const int k = std::min(desc->n_active, 8);
+    if (d <= 0 || E <= 0 || k <= 0 || k > E) return -1;
+    std::vector<float> xn((size_t)d), logits((size_t)E);
+    for (int t = 0; t < T; t++) {
+        int32_t sel[8];
+        float wsel[8];
+        route_token(desc, w, x + (size_t)t * d, flags, k, xn.data(), logits.data(), sel, wsel, threads);
+        if (xn_out) std::memcpy(xn_out + (size_t)t * d, xn.data(), sizeof(float) * (size_t)d);
+        if (logits_out) std::memcpy(logits_out + (size_t)t * E, logits.data(), sizeof(float) * (size_t)E);
+        if (topk_idx) std::memcpy(topk_idx + (size_t)t * k, sel, sizeof(int32_t) * (size_t)k);
+        if (topk_w) std::memcpy(topk_w + (size_t)t * k, wsel, sizeof(float) * (size_t)k);
+    }
+    return 0;
+}
+
 int orc_moe_forward(const orc_moe_desc* desc, const orc_moe_weights* w, const float* x, int T,
                     int flags, float* out, int32_t* topk_idx, float* topk_w, float* logits_out,
                     float* xn_out, int threads) {
@@ -801,20 +837,11 @@ int orc_moe_forward(const orc_moe_desc* desc, const orc_moe_weights* w, const fl
     for (int t = 0; t < T; t++) {
         const float* xt = x + (size_t)t * d;
         float* ot = out + (size_t)t * d;
-        if (flags & ORC_APPLY_NORM) orc_rmsnorm(xt, w->norm_w, xn.data(), d, desc->rms_eps);
-        else std::memcpy(xn.data(), xt, sizeof(float) * (size_t)d);
-        if (xn_out) std::memcpy(xn_out + (size_t)t * d, xn.data(), sizeof(float) * (size_t)d);
-        // router logits: MatVecParallel(F32) over the [E x d] router
-        orc_matvec_parallel(ORC_F32, (const uint8_t*)w->router, E, d, xn.data(), logits.data(), threads);
-        if (w->logit_offset)
-            for (int e = 0; e < E; e++) logits[(size_t)e] = logits[(size_t)e] + w->logit_offset[e];
-        if (logits_out) std::memcpy(logits_out + (size_t)t * E, logits.data(), sizeof(float) * (size_t)E);
         int32_t sel[8];
         float wsel[8];
-        if (desc->moe_sigmoid)
-            orc_route_sigmoid(logits.data(), w->router_bias, E, k, desc->routed_scale, sel, wsel);
-        else
-            orc_route_softmax(logits.data(), E, k, sel, wsel, nullptr);
+        route_token(desc, w, xt, flags, k, xn.data(), logits.data(), sel, wsel, threads);
+        if (xn_out) std::memcpy(xn_out + (size_t)t * d, xn.data(), sizeof(float) * (size_t)d);
+        if (logits_out) std::memcpy(logits_out + (size_t)t * E, logits.data(), sizeof(float) * (size_t)E);
         if (topk_idx) std::memcpy(topk_idx + (size_t)t * k, sel, sizeof(int32_t) * (size_t)k);
         if (topk_w) std::memcpy(topk_w + (size_t)t * k, wsel, sizeof(float) * (size_t)k);
         // MoeFfn accumulates into the residual x; the other two start from 0.

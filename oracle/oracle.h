@@ -127,6 +127,13 @@ int orc_moe_forward(const orc_moe_desc* desc, const orc_moe_weights* w,
                     int32_t* topk_idx, float* topk_w, float* logits_out,
                     float* xn_out, int threads);
 
+/* The routing part of orc_moe_forward alone (RMSNorm, router logits, top-k
+ * and combine weights; StreamingEngine.cs:259-260, 639-652, 727-767), for
+ * batches whose expert products are checked on a sample of tokens. */
+int orc_moe_route(const orc_moe_desc* desc, const orc_moe_weights* w,
+                  const float* x, int T, int flags, int32_t* topk_idx,
+                  float* topk_w, float* logits_out, float* xn_out, int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -247,6 +247,11 @@ class MoeLayer:
         _check(lib().qrm_forward(self._h, _ptr(x), T, flags, _ptr(out), _ptr(idx), _ptr(w)))
         return out, idx, w
 
+    def forward_into(self, x, flags, out, idx=None, w=None):
+        """qrm_forward on caller-owned host arrays (pageable memory, no
+        allocation here): the call the C# shim makes."""
+        _check(lib().qrm_forward(self._h, _ptr(x), x.shape[0], flags, _ptr(out), _ptr(idx), _ptr(w)))
+
     def forward_device(self, x_ptr, T, out_ptr, flags=APPLY_NORM, idx_ptr=None, w_ptr=None, stream=None):
         _check(lib().qrm_forward_device(self._h, x_ptr, T, flags, out_ptr, idx_ptr, w_ptr, stream))
 

@@ -814,6 +814,9 @@ static int upload_common(qrm_layer* L, int expert, int which, int fmt, const voi
         return fail(QRM_E_SIZE, "l.e%d.%s: %zu bytes, TensorBytes(%d x %d) = %zu", expert, which_name(which), nbytes,
                     m.rows, m.cols, L->mat_bytes[i]);
     QRM_CUDA(cudaSetDevice(L->desc.device));
+    // device bytes may still be in flight on another stream of the caller
+    // (the layer's own stream does not order with them): finish all work first
+    if (dev) QRM_CUDA(cudaDeviceSynchronize());
     uint8_t* dst = const_cast<uint8_t*>(m.base);
     const bool tiled = imma_usable(fmt, m.rows, m.cols, which != 2);
     if (fmt == qrm::Q4_K && !tiled) {

@@ -72,3 +72,51 @@ def assert_parity(case, x, flags, L=None, check_out=True):
     if check_out:
         assert err <= OUT_TOL, f"output max relative error {err:.3e}"
     return dict(err=err, out=out, ref=ref)
+
+
+def sample_tokens(idx, T, n=24, seed=0):
+    """Tokens whose outputs are checked against the oracle when a batch is too
+    large for the oracle to run whole: the first and last few, tokens of the
+    most loaded expert (its group takes the large-group path) and random ones."""
+    if T <= n:
+        return np.arange(T)
+    rng = np.random.default_rng(seed)
+    counts = np.bincount(idx.ravel())
+    top = int(np.argmax(counts))
+    busy = np.nonzero((idx == top).any(axis=1))[0]
+    pick = set(range(4)) | set(range(T - 4, T)) | set(busy[:: max(1, len(busy) // 8)][:8].tolist())
+    pick |= set(rng.choice(T, size=n, replace=False).tolist())
+    return np.array(sorted(pick))
+
+
+def check_synth_batch(spec, L, x, flags, full_limit=64, workers=None, check_dispatch=True):
+    """Runs the layer L (built from the tests.synth_layer.SynthLayer `spec`)
+    on host tokens x and checks it against the oracle: routing (xn, logits,
+    top-k, weights, dispatch) bit-exact for every token; outputs within
+    OUT_TOL for every token when T <= full_limit, else for a sample of tokens
+    (each token's output depends on that token alone).  Returns a summary."""
+    import torch
+    import qauntrunner_b200 as Q_
+    T = x.shape[0]
+    dev = L.desc.device
+    out, idx, w = L.forward(x, apply_norm=bool(flags & O.APPLY_NORM), add_residual=bool(flags & O.ADD_RESIDUAL))
+    logits, xn = L.last_router(T)
+    perm, off = L.last_dispatch(T)
+    case0 = spec.oracle_case(torch, Q_, dev, experts=())
+    r = O.moe_route_par(case0, x, flags, workers)
+    assert np.array_equal(xn.view(np.uint32), r["xn"].view(np.uint32)), "RMSNorm output differs"
+    assert np.array_equal(logits.view(np.uint32), r["logits"].view(np.uint32)), "router logits differ"
+    assert np.array_equal(idx, r["topk_idx"]), "top-k indices differ"
+    assert np.array_equal(w.view(np.uint32), r["topk_w"].view(np.uint32)), "top-k weights differ"
+    E = spec.cfg["n_experts"]
+    k = idx.shape[1]
+    rperm, _, roff = O.dispatch(r["topk_idx"], T, k, E)
+    if check_dispatch:   # (an expert-parallel layer dispatches every rank's tokens)
+        assert np.array_equal(perm, rperm), "dispatch permutation differs"
+        assert np.array_equal(off, roff), "dispatch offsets differ"
+    toks = np.arange(T) if T <= full_limit else sample_tokens(idx, T)
+    case = spec.oracle_case(torch, Q_, dev, experts=np.unique(idx[toks]))
+    ref = O.moe_forward_par(case, x[toks], flags, workers)
+    err = row_rel_err(out[toks], ref["out"])
+    return dict(err=err, tokens_checked=int(len(toks)), T=T, max_group=int(np.diff(roff).max()),
+                routing_bit_exact=True, out=out)

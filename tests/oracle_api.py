@@ -64,6 +64,7 @@ def _setup(L):
     L.orc_dispatch.argtypes = [P, C.c_int, C.c_int, C.c_int, P, P, P]
     L.orc_swiglu.argtypes = [P, P, C.c_int, C.c_float]
     L.orc_moe_forward.argtypes = [P, P, P, C.c_int, C.c_int, P, P, P, P, P, C.c_int]
+    L.orc_moe_route.argtypes = [P, P, P, C.c_int, C.c_int, P, P, P, P, C.c_int]
 
 
 def ptr(a):
@@ -143,11 +144,9 @@ class MoeWeights(C.Structure):
                 ("fmt_sh_gate", C.c_int32), ("fmt_sh_up", C.c_int32), ("fmt_sh_down", C.c_int32)]
 
 
-def moe_forward(layer, x, flags, threads=1):
-    """Runs the oracle MoE layer.  `layer` is a tests.moe_case.MoeCase."""
+def _moe_structs(layer):
     cfg = layer.cfg
-    T = x.shape[0]
-    d, E, k = cfg["d_model"], cfg["n_experts"], min(cfg["n_active"], 8)
+    d, E = cfg["d_model"], cfg["n_experts"]
     desc = MoeDesc(d, E, cfg["n_active"], cfg["expert_ffn"], int(cfg["moe_sigmoid"]),
                    cfg["routed_scale"], cfg["n_shared"], cfg["swiglu_limit"], cfg["rms_eps"])
     arr = P * E
@@ -160,6 +159,15 @@ def moe_forward(layer, x, flags, threads=1):
                    layer.fmt_gate, layer.fmt_up, layer.fmt_down,
                    ptr(sh[0]) if sh else None, ptr(sh[1]) if sh else None, ptr(sh[2]) if sh else None,
                    layer.fmt_sh[0], layer.fmt_sh[1], layer.fmt_sh[2])
+    return desc, w, (gate, up, down)
+
+
+def moe_forward(layer, x, flags, threads=1):
+    """Runs the oracle MoE layer.  `layer` is a tests.moe_case.MoeCase."""
+    cfg = layer.cfg
+    T = x.shape[0]
+    d, E, k = cfg["d_model"], cfg["n_experts"], min(cfg["n_active"], 8)
+    desc, w, keep = _moe_structs(layer)
     x = np.ascontiguousarray(x, dtype=np.float32)
     out = np.zeros((T, d), dtype=np.float32)
     idx = np.zeros((T, k), dtype=np.int32)
@@ -170,3 +178,42 @@ def moe_forward(layer, x, flags, threads=1):
                                ptr(wts), ptr(logits), ptr(xn), threads)
     assert rc == 0
     return dict(out=out, topk_idx=idx, topk_w=wts, logits=logits, xn=xn)
+
+
+def moe_route(layer, x, flags, threads=1):
+    """The oracle's routing alone (xn, logits, top-k) for every token of x."""
+    cfg = layer.cfg
+    T = x.shape[0]
+    d, E, k = cfg["d_model"], cfg["n_experts"], min(cfg["n_active"], 8)
+    desc, w, keep = _moe_structs(layer)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    idx = np.zeros((T, k), dtype=np.int32)
+    wts = np.zeros((T, k), dtype=np.float32)
+    logits = np.zeros((T, E), dtype=np.float32)
+    xn = np.zeros((T, d), dtype=np.float32)
+    assert lib().orc_moe_route(C.byref(desc), C.byref(w), ptr(x), T, flags, ptr(idx), ptr(wts),
+                               ptr(logits), ptr(xn), threads) == 0
+    return dict(topk_idx=idx, topk_w=wts, logits=logits, xn=xn)
+
+
+def _split(fn, layer, x, flags, workers):
+    """fn over token chunks on `workers` threads (every token is independent:
+    the results equal one call over all tokens)."""
+    from concurrent.futures import ThreadPoolExecutor
+    T = x.shape[0]
+    workers = max(1, min(workers, T))
+    if workers == 1:
+        return fn(layer, x, flags, 1)
+    bounds = np.linspace(0, T, workers + 1).astype(int)
+    with ThreadPoolExecutor(workers) as ex:
+        parts = list(ex.map(lambda i: fn(layer, x[bounds[i]:bounds[i + 1]], flags, 1), range(workers)))
+    return {key: np.concatenate([p[key] for p in parts]) for key in parts[0]}
+
+
+def moe_forward_par(layer, x, flags, workers=None):
+    """moe_forward with the tokens spread over host threads."""
+    return _split(moe_forward, layer, x, flags, workers or (os.cpu_count() or 1))
+
+
+def moe_route_par(layer, x, flags, workers=None):
+    return _split(moe_route, layer, x, flags, workers or (os.cpu_count() or 1))
