@@ -119,6 +119,12 @@ def lib():
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise ImportError(f"{LIB_PATH} is missing; build it with `python -m qauntrunner_b200.build`")
+        # libqrmoe.so resolves libnccl.so.2 at load time: in a process that also
+        # uses torch, torch's (newer) NCCL must be the one loaded first
+        try:
+            import torch  # noqa: F401
+        except ImportError:
+            pass
         L = C.CDLL(LIB_PATH)
         for name, (res, args) in _SIGS.items():
             fn = getattr(L, name)

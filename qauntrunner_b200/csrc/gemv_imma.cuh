@@ -117,7 +117,7 @@ __device__ __forceinline__ void xquant_group(float v, int lane, int gi, int K, u
 
 // Quantises activation rows into tables (global memory), one warp per four
 // groups (K % 128 == 0).
-__global__ void xquant_kernel(const float* __restrict__ src, int K, int rows, uint8_t* __restrict__ tab,
+static __global__ void xquant_kernel(const float* __restrict__ src, int K, int rows, uint8_t* __restrict__ tab,
                               int stride) {
     const int lane = threadIdx.x & 31;
     const int quads = K / 128;

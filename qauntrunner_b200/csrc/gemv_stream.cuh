@@ -79,7 +79,7 @@ __host__ __device__ inline long long tiled_offset(int fmt, int nsb, long long bl
 }
 
 // to_tiled = 1: .qw bytes -> tiled; 0: tiled -> .qw bytes.  One thread per byte.
-__global__ void tile_relayout_kernel(int fmt, int bb, int nsb, const uint8_t* __restrict__ src,
+static __global__ void tile_relayout_kernel(int fmt, int bb, int nsb, const uint8_t* __restrict__ src,
                                      uint8_t* __restrict__ dst, long long nb, int to_tiled) {
     const long long total = nb * bb;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;

@@ -28,7 +28,7 @@ __device__ __forceinline__ int split_fields(int fmt, Field* f) {
 
 // to_split = 1: .qw bytes -> split layout; 0: split -> .qw bytes.  One thread
 // per (block, byte) pair of the block.
-__global__ void relayout_kernel(int fmt, int bb, const uint8_t* __restrict__ src,
+static __global__ void relayout_kernel(int fmt, int bb, const uint8_t* __restrict__ src,
                                 uint8_t* __restrict__ dst, long long nb, int to_split) {
     Field f[4];
     const int nf = split_fields(fmt, f);

@@ -35,6 +35,7 @@
 #include "gemv_stream.cuh"
 #include "layout.cuh"
 #include "route.cuh"
+#include "umma_host.h"
 
 extern "C" int qrm_synth_quantize_impl(int fmt, const float* src, long long n, void* dst, cudaStream_t s);
 extern "C" int qrm_synth_gaussian_impl(float* dst, long long n, uint64_t seed, float sigma, cudaStream_t s);
@@ -382,6 +383,16 @@ struct qrm_layer {
     size_t staging_bytes = 0;
     uint8_t* xtab_gu = nullptr;   // activation tables of the gate/up inputs [T]
     uint8_t* xtab_dn = nullptr;   // of the down inputs [T*k routed | T shared]
+    // tcgen05 grouped path for large per-expert groups (umma.cu)
+    bool umma_ok = false;         // formats and shapes allow it; buffers allocated
+    int umma_mode = -1;           // -1 by group size, 0 never, 1 always (QRM_UMMA)
+    int umma_min_tpe = 24;        // average routed tokens per expert from which it is used (QRM_UMMA_MIN_TPE)
+    __half* act16 = nullptr;      // [Tx*k + Tx][d] f16 gate/up inputs in dispatch order
+    __half* h16 = nullptr;        // [Tx*k + Tx][f] f16 down inputs
+    qrm::UmmaItem* umma_items = nullptr;   // [2][cap]: gate/up items, down items
+    int32_t* umma_count = nullptr;         // [2]
+    long long umma_cap = 0;
+    CUtensorMap act_map{}, h_map{};
     int last_T = 0;
     int last_launches = 0;        // kernel launches of the last forward
     const float* last_xn = nullptr;
@@ -466,7 +477,7 @@ static void free_layer(qrm_layer* L) {
     void* ptrs[] = {L->slab, L->mats_dev, L->norm_w, L->router, L->router_lm, L->router_bias, L->offset, L->x, L->xn,
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
                     L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn,
-                    L->pos_tok, L->slot_info,
+                    L->pos_tok, L->slot_info, L->act16, L->h16, L->umma_items, L->umma_count,
                     L->rec_own, L->rec_all, L->ysend, L->peer_base, L->ep_state, L->xch};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -645,6 +656,40 @@ static int ep_open_peers(qrm_layer* L) {
     return QRM_OK;
 }
 
+// The tcgen05 grouped path (umma.cu): usable when every expert matrix is in
+// the tiled layout in a format pair it has, the gate/up rows come in blocks of
+// 64 and the down rows in blocks of 128, and a batch can reach the group size
+// it is used from.  Buffers for the largest batch are allocated here.
+static int umma_setup(qrm_layer* L) {
+    const qrm_layer_desc& D = L->desc;
+    const int d = D.d_model, f = D.expert_ffn, E = D.n_experts, k = L->k;
+    if (const char* e = getenv("QRM_UMMA")) L->umma_mode = atoi(e) > 0 ? 1 : 0;
+    if (const char* e = getenv("QRM_UMMA_MIN_TPE")) L->umma_min_tpe = std::max(1, atoi(e));
+    const long long Tx = (long long)D.max_tokens * L->world, Tk = Tx * k;
+    const int fsh = L->shared_enabled ? D.fmt_sh_gate : -1, fshd = L->shared_enabled ? D.fmt_sh_down : -1;
+    const bool fmts = qrm::umma_pair(D.fmt_gate, fsh) && qrm::umma_pair(D.fmt_down, fshd) &&
+                      (!L->shared_enabled || (D.fmt_sh_gate == D.fmt_sh_up));
+    const bool shapes = f % 64 == 0 && d % 128 == 0 && d % 256 == 0 && f % 256 == 0 &&
+                        imma_usable(D.fmt_gate, f, d, true) && imma_usable(D.fmt_down, d, f, false);
+    const bool reach = L->umma_mode == 1 || (L->umma_mode != 0 && Tk >= (long long)L->umma_min_tpe * E);
+    if (!fmts || !shapes || !reach) return QRM_OK;
+    const long long rows = Tk + (L->shared_enabled ? Tx : 0);
+    L->umma_cap = qrm::umma_item_cap(L->n_local, Tk, L->shared_enabled ? Tx : 0, f / 64, d / 128);
+    if (cudaMalloc(&L->act16, sizeof(__half) * rows * d) != cudaSuccess ||
+        cudaMalloc(&L->h16, sizeof(__half) * rows * f) != cudaSuccess ||
+        cudaMalloc(&L->umma_items, (size_t)qrm::kUmmaItemBytes * 2 * L->umma_cap) != cudaSuccess ||
+        cudaMalloc(&L->umma_count, sizeof(int32_t) * 2) != cudaSuccess)
+        return fail(QRM_E_NOMEM, "grouped-path buffers (%lld activation rows)", rows);
+    // rows past a batch's end are read as padding: start them at zero
+    QRM_CUDA(cudaMemset(L->act16, 0, sizeof(__half) * rows * d));
+    QRM_CUDA(cudaMemset(L->h16, 0, sizeof(__half) * rows * f));
+    QRM_CUDA(cudaMemset(L->umma_count, 0, sizeof(int32_t) * 2));
+    if (qrm::umma_encode_map(&L->act_map, L->act16, rows, d) != 0 || qrm::umma_encode_map(&L->h_map, L->h16, rows, f) != 0)
+        return fail(QRM_E_CUDA, "tensor map encoding failed");
+    L->umma_ok = true;
+    return QRM_OK;
+}
+
 static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out) {
     if (!out) return fail(QRM_E_INVALID, "out is NULL");
     *out = nullptr;
@@ -742,6 +787,8 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
         rc = ep_open_peers(L);
         if (rc) return bail(rc);
     }
+    rc = umma_setup(L);
+    if (rc) return bail(rc);
     // kernels with large dynamic shared memory
     if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(qrm::route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess ||
@@ -1016,11 +1063,32 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         nl += 3;
     }
     // 4. gate/up (+ SwiGLU) and 5. down
+    const bool umma = L->umma_ok && (L->umma_mode == 1 || (long long)Tx * k >= (long long)L->umma_min_tpe * E);
+    if (umma) {
+        // large groups: f16 activations in dispatch order, the work lists, then one
+        // tcgen05 grouped launch per stage
+        const int Tk = Tx * k;
+        const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;
+        const int fsh = shared ? D.fmt_sh_gate : -1, fshd = shared ? D.fmt_sh_down : -1;
+        QRM_CUDA(qrm::umma_gather(xs, L->pos_tok, Tk, shared ? Tx : 0, d, L->act16, L->sm_count, s));
+        QRM_CUDA(qrm::umma_plan(L->slot_info, &L->sched->n_active, shared ? 1 : 0, Tk, f / 64, d / 128, E,
+                                L->umma_items, L->umma_count, L->umma_items + L->umma_cap, L->umma_count + 1,
+                                (int)L->umma_cap, s));
+        cudaError_t e = qrm::umma_expert(D.fmt_gate, fsh, true, L->act_map, L->mats_dev, L->umma_items, L->umma_count, d,
+                                         f, Tk, limit, L->h16, nullptr, nullptr, &L->sched->err, L->sm_count, s);
+        if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped gate/up launch: %s", cudaGetErrorString(e));
+        mark(4);
+        e = qrm::umma_expert(D.fmt_down, fshd, false, L->h_map, L->mats_dev, L->umma_items + L->umma_cap,
+                             L->umma_count + 1, f, d, Tk, 0.f, nullptr, L->y, L->ys, &L->sched->err, L->sm_count, s);
+        if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped down launch: %s", cudaGetErrorString(e));
+        mark(5);
+        nl += 4;
+    }
     const int nt = pick_nt(Tx);
     const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU
     const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
     bool combined = false;
-    for (int stage = 0; stage < 2; stage++) {
+    for (int stage = 0; stage < 2 && !umma; stage++) {
         const bool gu = stage == 0;
         // activation tables for the integer tensor-core kernel
         const int frs = gu ? D.fmt_gate : D.fmt_down, fss = gu ? D.fmt_sh_gate : D.fmt_sh_down;
