@@ -43,21 +43,27 @@ namespace qrm {
 
 // ------------------------------------------------------------ tiled layout
 
-// bytes of one row's blocks in one super-block
+// bytes of one row's blocks in one super-block (256 columns)
 __host__ __device__ inline int tile_row_sb_bytes(int fmt) {
     switch (fmt) {
         case Q4_K: return 144;
         case Q8_0: return 272;
         case Q4_0: return 160;
+        case Q6_K: return 210;
+        case TRI: return 72;
         default: return 0;
     }
 }
 __host__ __device__ inline int tile_chunk_bytes(int fmt) { return 8 * tile_row_sb_bytes(fmt); }
 
 // Offset in the tiled matrix of byte `byte` of block `blk` (.qw order: row
-// major, `nsb` super-blocks per row).
+// major, `nsb` super-blocks per row).  Chunk layouts (8 rows r, one super-block):
+//   Q4_K hdr[r][16] | qs[pair][r][32]          Q8_0 d[r][blk][2] | qs[blk][r][32]
+//   Q4_0 d[r][blk][2] | pad[r][blk][2] | qs[blk][r][16]
+//   Q6_K ql[r][128] | qh[r][64] | sc[r][16] | d[r][2]
+//   TRI  codes[r][blk][16] | scale[r][blk][2]   (4 blocks of 64 weights)
 __host__ __device__ inline long long tiled_offset(int fmt, int nsb, long long blk, int byte) {
-    const int bps = fmt == Q4_K ? 1 : 8;           // blocks per super-block
+    const int bps = (fmt == Q4_K || fmt == Q6_K) ? 1 : fmt == TRI ? 4 : 8;   // blocks per super-block
     const long long bpr = (long long)nsb * bps;    // blocks per row
     const long long row = blk / bpr;
     const int b = (int)(blk - row * bpr), sb = b / bps, g = b - sb * bps;
@@ -71,6 +77,14 @@ __host__ __device__ inline long long tiled_offset(int fmt, int nsb, long long bl
         case Q8_0:
             if (byte < 2) return chunk + 16 * r + 2 * g + byte;
             return chunk + 128 + 256 * g + 32 * r + (byte - 2);
+        case Q6_K:   // ql (0-127), qh (128-191), scales (192-207), d (208-209)
+            if (byte < 128) return chunk + 128 * r + byte;
+            if (byte < 192) return chunk + 1024 + 64 * r + (byte - 128);
+            if (byte < 208) return chunk + 1536 + 16 * r + (byte - 192);
+            return chunk + 1664 + 2 * r + (byte - 208);
+        case TRI:    // scale (0-1), codes (2-17)
+            if (byte < 2) return chunk + 512 + 8 * r + 2 * g + byte;
+            return chunk + 64 * r + 16 * g + (byte - 2);
         default:  // Q4_0: d (0-1), qs (2-17), pad (18-19)
             if (byte < 2) return chunk + 16 * r + 2 * g + byte;
             if (byte >= 18) return chunk + 128 + 16 * r + 2 * g + (byte - 18);

@@ -223,6 +223,21 @@ bool imma_usable(int fmt, int rows, int cols, bool gateup) {
     return rows % (gateup ? 8 : 16) == 0;
 }
 
+// Shapes the tcgen05 grouped path takes: gate/up rows in blocks of 64, down
+// rows in blocks of 128, both K ranges whole super-blocks.
+bool umma_shapes(int d, int f) { return f % 64 == 0 && d % 128 == 0 && d % 256 == 0 && f % 256 == 0; }
+
+// true when an expert matrix of a layer with d_model d and expert_ffn f is
+// stored in the tiled layout: the integer streaming kernel's formats as
+// before, Q6_K and TRI when the grouped path takes the layer's shapes (it is
+// then their kernel at every batch size)
+bool layer_tiled(int fmt, int d, int f, bool gateup) {
+    const int rows = gateup ? f : d, cols = gateup ? d : f;
+    if (imma_format(fmt)) return imma_usable(fmt, rows, cols, gateup);
+    return (fmt == qrm::Q6_K || fmt == qrm::TRI) && umma_shapes(d, f);
+}
+bool umma_only_format(int fmt) { return fmt == qrm::Q6_K || fmt == qrm::TRI; }
+
 // Plans a launch whose routed items use format fa and shared items format fb
 // (-1: none); false when no plan fits (the caller reports it).
 bool stream_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, StreamSel* sel) {
@@ -386,6 +401,8 @@ struct qrm_layer {
     // tcgen05 grouped path for large per-expert groups (umma.cu)
     bool umma_ok = false;         // formats and shapes allow it; buffers allocated
     int umma_mode = -1;           // -1 by group size, 0 never, 1 always (QRM_UMMA)
+    bool umma_forced_gu = false;  // a gate/up format has no other kernel in the tiled layout (Q6_K, TRI)
+    bool umma_forced_dn = false;  // same for down
     int umma_min_tpe = 24;        // average routed tokens per expert from which it is used (QRM_UMMA_MIN_TPE)
     __half* act16 = nullptr;      // [Tx*k + Tx][d] f16 gate/up inputs in dispatch order
     __half* h16 = nullptr;        // [Tx*k + Tx][f] f16 down inputs
@@ -666,15 +683,21 @@ static int umma_setup(qrm_layer* L) {
     if (const char* e = getenv("QRM_UMMA")) L->umma_mode = atoi(e) > 0 ? 1 : 0;
     if (const char* e = getenv("QRM_UMMA_MIN_TPE")) L->umma_min_tpe = std::max(1, atoi(e));
     const long long Tx = (long long)D.max_tokens * L->world, Tk = Tx * k;
-    const int fsh = L->shared_enabled ? D.fmt_sh_gate : -1, fshd = L->shared_enabled ? D.fmt_sh_down : -1;
+    const bool sh = L->shared_enabled;
+    const int fsh = sh ? D.fmt_sh_gate : -1, fshd = sh ? D.fmt_sh_down : -1;
     const bool fmts = qrm::umma_pair(D.fmt_gate, fsh) && qrm::umma_pair(D.fmt_down, fshd) &&
-                      (!L->shared_enabled || (D.fmt_sh_gate == D.fmt_sh_up));
-    const bool shapes = f % 64 == 0 && d % 128 == 0 && d % 256 == 0 && f % 256 == 0 &&
-                        imma_usable(D.fmt_gate, f, d, true) && imma_usable(D.fmt_down, d, f, false);
-    const bool reach = L->umma_mode == 1 || (L->umma_mode != 0 && Tk >= (long long)L->umma_min_tpe * E);
+                      (!sh || (D.fmt_sh_gate == D.fmt_sh_up));
+    const bool shapes = umma_shapes(d, f) && layer_tiled(D.fmt_gate, d, f, true) && layer_tiled(D.fmt_down, d, f, false) &&
+                        (!sh || (layer_tiled(D.fmt_sh_gate, d, f, true) && layer_tiled(D.fmt_sh_down, d, f, false)));
+    L->umma_forced_gu = umma_only_format(D.fmt_gate) || (sh && umma_only_format(D.fmt_sh_gate));
+    L->umma_forced_dn = umma_only_format(D.fmt_down) || (sh && umma_only_format(D.fmt_sh_down));
+    const bool forced = L->umma_forced_gu || L->umma_forced_dn;
+    if (forced && (!fmts || !shapes))
+        return fail(QRM_E_FORMAT, "this combination of Q6_K / TRI expert formats and shapes has no kernel");
+    const bool reach = forced || L->umma_mode == 1 || (L->umma_mode != 0 && Tk >= (long long)L->umma_min_tpe * E);
     if (!fmts || !shapes || !reach) return QRM_OK;
-    const long long rows = Tk + (L->shared_enabled ? Tx : 0);
-    L->umma_cap = qrm::umma_item_cap(L->n_local, Tk, L->shared_enabled ? Tx : 0, f / 64, d / 128);
+    const long long rows = Tk + (sh ? Tx : 0);
+    L->umma_cap = qrm::umma_item_cap(L->n_local, Tk, sh ? Tx : 0, f / 64, d / 128);
     if (cudaMalloc(&L->act16, sizeof(__half) * rows * d) != cudaSuccess ||
         cudaMalloc(&L->h16, sizeof(__half) * rows * f) != cudaSuccess ||
         cudaMalloc(&L->umma_items, (size_t)qrm::kUmmaItemBytes * 2 * L->umma_cap) != cudaSuccess ||
@@ -865,7 +888,7 @@ static int upload_common(qrm_layer* L, int expert, int which, int fmt, const voi
     // (the layer's own stream does not order with them): finish all work first
     if (dev) QRM_CUDA(cudaDeviceSynchronize());
     uint8_t* dst = const_cast<uint8_t*>(m.base);
-    const bool tiled = imma_usable(fmt, m.rows, m.cols, which != 2);
+    const bool tiled = layer_tiled(fmt, L->desc.d_model, L->desc.expert_ffn, which != 2);
     if (fmt == qrm::Q4_K && !tiled) {
         QRM_CUDA(cudaMemcpyAsync(dst, bytes, nbytes, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, L->stream));
     } else {
@@ -911,7 +934,7 @@ extern "C" int qrm_download_expert(qrm_layer* L, int expert, int which, void* by
     if (nbytes != L->mat_bytes[i]) return fail(QRM_E_SIZE, "buffer is %zu bytes, tensor is %zu", nbytes, L->mat_bytes[i]);
     const qrm::MatDev& m = L->mats[i];
     QRM_CUDA(cudaSetDevice(L->desc.device));
-    const bool tiled = imma_usable(m.fmt, m.rows, m.cols, which != 2);
+    const bool tiled = layer_tiled(m.fmt, L->desc.d_model, L->desc.expert_ffn, which != 2);
     if (m.fmt == qrm::Q4_K && !tiled) {
         QRM_CUDA(cudaMemcpy(bytes, m.base, nbytes, cudaMemcpyDeviceToHost));
         return QRM_OK;
@@ -1063,33 +1086,53 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         nl += 3;
     }
     // 4. gate/up (+ SwiGLU) and 5. down
-    const bool umma = L->umma_ok && (L->umma_mode == 1 || (long long)Tx * k >= (long long)L->umma_min_tpe * E);
-    if (umma) {
-        // large groups: f16 activations in dispatch order, the work lists, then one
-        // tcgen05 grouped launch per stage
-        const int Tk = Tx * k;
-        const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;
-        const int fsh = shared ? D.fmt_sh_gate : -1, fshd = shared ? D.fmt_sh_down : -1;
-        QRM_CUDA(qrm::umma_gather(xs, L->pos_tok, Tk, shared ? Tx : 0, d, L->act16, L->sm_count, s));
+    // each stage takes the tcgen05 grouped path for large groups, and always
+    // for the formats that have no other kernel in the tiled layout
+    const bool large = L->umma_ok && (L->umma_mode == 1 || (long long)Tx * k >= (long long)L->umma_min_tpe * E);
+    const bool u_gu = L->umma_ok && (large || L->umma_forced_gu);
+    const bool u_dn = L->umma_ok && (large || L->umma_forced_dn);
+    const int Tk = Tx * k;
+    if (u_gu || u_dn) {
+        // work lists of both stages from the dispatch's slot table; f16
+        // activations in dispatch order for a grouped gate/up
+        if (u_gu) QRM_CUDA(qrm::umma_gather(xs, L->pos_tok, Tk, shared ? Tx : 0, d, L->act16, L->sm_count, s));
         QRM_CUDA(qrm::umma_plan(L->slot_info, &L->sched->n_active, shared ? 1 : 0, Tk, f / 64, d / 128, E,
                                 L->umma_items, L->umma_count, L->umma_items + L->umma_cap, L->umma_count + 1,
                                 (int)L->umma_cap, s));
-        cudaError_t e = qrm::umma_expert(D.fmt_gate, fsh, true, L->act_map, L->mats_dev, L->umma_items, L->umma_count, d,
-                                         f, Tk, limit, L->h16, nullptr, nullptr, &L->sched->err, L->sm_count, s);
-        if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped gate/up launch: %s", cudaGetErrorString(e));
-        mark(4);
-        e = qrm::umma_expert(D.fmt_down, fshd, false, L->h_map, L->mats_dev, L->umma_items + L->umma_cap,
-                             L->umma_count + 1, f, d, Tk, 0.f, nullptr, L->y, L->ys, &L->sched->err, L->sm_count, s);
-        if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped down launch: %s", cudaGetErrorString(e));
-        mark(5);
-        nl += 4;
+        nl += u_gu ? 2 : 1;
     }
     const int nt = pick_nt(Tx);
     const float limit = D.moe_sigmoid ? D.swiglu_limit : 0.f;  // MoeFfn / LegacyMoeInto use plain SiLU
     const bool same_fmt = !shared || (D.fmt_sh_gate == D.fmt_gate && D.fmt_sh_down == D.fmt_down);
     bool combined = false;
-    for (int stage = 0; stage < 2 && !umma; stage++) {
+    for (int stage = 0; stage < 2; stage++) {
         const bool gu = stage == 0;
+        const float ulimit = D.moe_sigmoid ? D.swiglu_limit : 0.f;
+        if (gu && u_gu) {
+            cudaError_t e = qrm::umma_expert(D.fmt_gate, shared ? D.fmt_sh_gate : -1, true, L->act_map, L->mats_dev,
+                                             L->umma_items, L->umma_count, d, f, Tk, ulimit, L->h16, nullptr, nullptr,
+                                             &L->sched->err, L->sm_count, s);
+            if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped gate/up launch: %s", cudaGetErrorString(e));
+            nl++;
+            mark(4);
+            continue;
+        }
+        if (!gu && u_dn != u_gu) {
+            // the stages took different paths: hand the SwiGLU outputs over
+            // (f32 h / hs of the decode kernels <-> f16 rows of the grouped one)
+            QRM_CUDA(qrm::umma_convert_h(L->h, shared ? L->hs : nullptr, Tk, shared ? Tx : 0, f, L->h16, u_dn ? 1 : 0,
+                                         L->sm_count, s));
+            nl++;
+        }
+        if (!gu && u_dn) {
+            cudaError_t e = qrm::umma_expert(D.fmt_down, shared ? D.fmt_sh_down : -1, false, L->h_map, L->mats_dev,
+                                             L->umma_items + L->umma_cap, L->umma_count + 1, f, d, Tk, 0.f, nullptr,
+                                             L->y, L->ys, &L->sched->err, L->sm_count, s);
+            if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped down launch: %s", cudaGetErrorString(e));
+            nl++;
+            mark(5);
+            continue;
+        }
         // activation tables for the integer tensor-core kernel
         const int frs = gu ? D.fmt_gate : D.fmt_down, fss = gu ? D.fmt_sh_gate : D.fmt_sh_down;
         const int rows_s = gu ? f : d, cols_s = gu ? d : f;

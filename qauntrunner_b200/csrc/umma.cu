@@ -12,7 +12,7 @@ namespace qrm {
 
 static_assert(sizeof(UmmaItem) == kUmmaItemBytes, "work item size");
 
-bool umma_format(int fmt) { return fmt == Q4_K || fmt == Q8_0 || fmt == Q4_0; }
+bool umma_format(int fmt) { return fmt == Q4_K || fmt == Q8_0 || fmt == Q4_0 || fmt == Q6_K || fmt == TRI; }
 
 // cuTensorMapEncodeTiled from the driver (no link-time dependency on libcuda)
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -47,6 +47,33 @@ cudaError_t umma_gather(const float* xn, const int32_t* pos_tok, int Tk, int sha
     if (n <= 0) return cudaSuccess;
     const int grid = (int)std::min<long long>((n + 255) / 256, (long long)sm_count * 8);
     umma_gather_kernel<<<grid, 256, 0, s>>>(xn, pos_tok, Tk, shared_rows, d, out);
+    return cudaGetLastError();
+}
+
+__global__ void umma_convert_h_kernel(float* __restrict__ h, float* __restrict__ hs, int Tk, int shared_rows, int f,
+                                      __half* __restrict__ h16, int to_f16) {
+    const long long n2 = (long long)(Tk + shared_rows) * (f / 2);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n2; i += (long long)gridDim.x * blockDim.x) {
+        const long long row = i / (f / 2);
+        const int c = (int)(i - row * (f / 2)) * 2;
+        float* src = row < Tk ? h + row * f + c : hs + (row - Tk) * f + c;
+        __half2* dst = reinterpret_cast<__half2*>(h16 + row * f + c);
+        if (to_f16) {
+            *dst = __floats2half2_rn(src[0], src[1]);
+        } else {
+            const float2 v = __half22float2(*dst);
+            src[0] = v.x;
+            src[1] = v.y;
+        }
+    }
+}
+
+cudaError_t umma_convert_h(float* h, float* hs, int Tk, int shared_rows, int f, __half* h16, int to_f16, int sm_count,
+                           cudaStream_t s) {
+    const long long n = (long long)(Tk + shared_rows) * (f / 2);
+    if (n <= 0) return cudaSuccess;
+    const int grid = (int)std::min<long long>((n + 255) / 256, (long long)sm_count * 8);
+    umma_convert_h_kernel<<<grid, 256, 0, s>>>(h, hs, Tk, shared_rows, f, h16, to_f16);
     return cudaGetLastError();
 }
 
@@ -99,6 +126,8 @@ cudaError_t umma_expert(int fa, int fb, bool gateup, const CUtensorMap& map, con
     if (fa == Q4_K && fb == Q8_0) return launch_pair<Q4_K, Q8_0>(gateup, map, p, grid, s);
     if (fa == Q8_0 && fb == Q8_0) return launch_pair<Q8_0, Q8_0>(gateup, map, p, grid, s);
     if (fa == Q4_0 && fb == Q4_0) return launch_pair<Q4_0, Q4_0>(gateup, map, p, grid, s);
+    if (fa == Q6_K && fb == Q6_K) return launch_pair<Q6_K, Q6_K>(gateup, map, p, grid, s);
+    if (fa == TRI && fb == TRI) return launch_pair<TRI, TRI>(gateup, map, p, grid, s);
     return cudaErrorInvalidValue;
 }
 

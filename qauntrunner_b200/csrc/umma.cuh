@@ -177,19 +177,76 @@ __device__ __forceinline__ void dq_words(uint32_t c0, uint32_t c1, __half2 off, 
     for (int i = 0; i < 4; i++) out[i] = h2_bits(__hfma2(__hsub2(bits_h2(p[i]), off), a, nb));
 }
 
-// The row's 16-byte header of the super-block (Q4_K: d, dmin, scales; Q8_0 /
-// Q4_0: the eight blocks' d), read once per raw stage.
+// The row's per-super-block header, read once per raw stage: Q4_K d, dmin
+// and scales; Q8_0 / Q4_0 the eight blocks' d; Q6_K the 16 scales (h) and d
+// (e); TRI the four blocks' scales (h.x, h.y).
+struct UmmaHdr {
+    uint4 h;
+    uint32_t e;
+};
 template <int FMT>
-__device__ __forceinline__ uint4 umma_row_header(const uint8_t* raw, int r) {
-    return *reinterpret_cast<const uint4*>(raw + (r >> 3) * umma_chunk_pitch(FMT) + 16 * (r & 7));
+__device__ __forceinline__ UmmaHdr umma_row_header(const uint8_t* raw, int r) {
+    const uint8_t* chunk = raw + (r >> 3) * umma_chunk_pitch(FMT);
+    const int rr = r & 7;
+    UmmaHdr hd;
+    hd.e = 0;
+    if (FMT == Q6_K) {
+        hd.h = *reinterpret_cast<const uint4*>(chunk + 1536 + 16 * rr);
+        hd.e = *reinterpret_cast<const uint16_t*>(chunk + 1664 + 2 * rr);
+    } else if (FMT == TRI) {
+        const uint2 v = *reinterpret_cast<const uint2*>(chunk + 512 + 8 * rr);
+        hd.h = make_uint4(v.x, v.y, 0u, 0u);
+    } else {
+        hd.h = *reinterpret_cast<const uint4*>(chunk + 16 * rr);
+    }
+    return hd;
+}
+
+// f16 pairs (t(c0), t(c1)) of the TRI codes in a nibble (c0 = low two bits):
+// code 01 -> +1, 10 -> -1, 00 and 11 -> 0 (BlockDequantizer.cs:258-276)
+__device__ __forceinline__ uint32_t tri_pair_bits(int n) {
+    const int c0 = n & 3, c1 = n >> 2;
+    const float t0 = c0 == 1 ? 1.f : c0 == 2 ? -1.f : 0.f, t1 = c1 == 1 ? 1.f : c1 == 2 ? -1.f : 0.f;
+    return h2_bits(__floats2half2_rn(t0, t1));
 }
 
 template <int FMT>
-__device__ __forceinline__ void umma_dequant(const uint8_t* raw, const uint4& h4, int r, int j, int part,
-                                             uint32_t (&w)[8]) {
+__device__ __forceinline__ void umma_dequant(const uint8_t* raw, const UmmaHdr& hd, const uint32_t* tri_lut, int r,
+                                             int j, int part, uint32_t (&w)[8]) {
     const uint8_t* chunk = raw + (r >> 3) * umma_chunk_pitch(FMT);
     const int rr = r & 7, half = part >> 1, sub = part & 1;
-    if (FMT == Q4_K) {
+    const uint4& h4 = hd.h;
+    if (FMT == TRI) {
+        // codes[r][blk][16]: weight i of block j at byte i/4, bits 2(i & 3); part p
+        // = weights 16p..16p+15 = one word; w = s * t exactly (s is f16)
+        const uint32_t x = *reinterpret_cast<const uint32_t*>(chunk + 64 * rr + 16 * j + 4 * part);
+        const uint32_t sw = j < 2 ? h4.x : h4.y;
+        const __half2 s2 = __half2half2(__ushort_as_half((uint16_t)(sw >> (16 * (j & 1)))));
+#pragma unroll
+        for (int k = 0; k < 8; k++) w[k] = h2_bits(__hmul2(bits_h2(tri_lut[(x >> (4 * k)) & 15u]), s2));
+    } else if (FMT == Q6_K) {
+        // DequantQ6_K (BlockDequantizer.cs:228-256): half h = j / 2 of the block
+        // (128 weights); in it, group g of 32 (q1..q4) takes ql[64h + 32(g & 1) + l]
+        // (low nibble for g < 2, high for g >= 2) and bits 2g of qh[32h + l],
+        // scale sc[8h + l/16 + 2g]; w = d * sc * (q - 32)
+        const int hh = j >> 1, local = 64 * (j & 1) + 16 * part, g = local >> 5, l0 = local & 31;
+        const uint4 ql = *reinterpret_cast<const uint4*>(chunk + 128 * rr + 64 * hh + 32 * (g & 1) + l0);
+        const uint4 qh = *reinterpret_cast<const uint4*>(chunk + 1024 + 64 * rr + 32 * hh + l0);
+        const int si = 8 * hh + (l0 >> 4) + 2 * g;
+        const uint32_t scw = si < 4 ? h4.x : si < 8 ? h4.y : si < 12 ? h4.z : h4.w;
+        const int sc = (int)(int8_t)((scw >> (8 * (si & 3))) & 0xFF);
+        const float d = h2f((uint16_t)hd.e);
+        const __half2 a = __float2half2_rn(d * (float)sc);
+        const __half2 nb = __float2half2_rn(0.f);
+        const __half2 off = __float2half2_rn(1056.f);   // 1024 + 32
+        const int ls = 4 * (g >> 1), hs = 2 * g;
+        const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w}, hw[4] = {qh.x, qh.y, qh.z, qh.w};
+        uint32_t qq[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) qq[i] = ((lw[i] >> ls) & 0x0F0F0F0Fu) | (((hw[i] >> hs) & 0x03030303u) << 4);
+        dq_words(qq[0], qq[1], off, a, nb, &w[0]);
+        dq_words(qq[2], qq[3], off, a, nb, &w[4]);
+    } else if (FMT == Q4_K) {
         // hdr[8][16] | qs[4 pairs][8 rows][32]: in pair j, byte i holds weight i
         // of sub-block 2j (low nibble) and of sub-block 2j+1 (high nibble)
         const uint4 q4 = *reinterpret_cast<const uint4*>(chunk + 128 + 256 * j + 32 * rr + 16 * sub);
@@ -312,6 +369,7 @@ expert_umma_kernel(const __grid_constant__ CUtensorMap act_map, UmmaParams p, in
     uint64_t* x_empty = x_full + 2;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + 512);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + 520);
+    uint32_t* tri_lut = reinterpret_cast<uint32_t*>(sm + 576);   // [16] TRI nibble -> f16 pair
     uint8_t* raw = sm + 1024;
     uint8_t* bring = sm + b_off;
     float* xch = reinterpret_cast<float*>(sm + x_off);
@@ -342,6 +400,9 @@ expert_umma_kernel(const __grid_constant__ CUtensorMap act_map, UmmaParams p, in
         }
         *abort_flag = 0;
         fence_barrier_init();
+    }
+    if (tid < 16) {
+        tri_lut[tid] = tri_pair_bits(tid);
     }
     if (warp == 1) tmem_alloc(smem_u32(tmem_slot), kUmmaTmemCols);
     tc_fence_before();
@@ -541,15 +602,15 @@ expert_umma_kernel(const __grid_constant__ CUtensorMap act_map, UmmaParams p, in
                 const int s = gr % RS;
                 if (!warp_wait(&raw_full[s], (gr / RS) & 1u, abort_flag, p.err)) { ok = false; break; }
                 const uint8_t* st = raw + (size_t)s * raw_bytes;
-                const uint4 hdr = shi ? umma_row_header<FB>(st, r) : umma_row_header<FA>(st, r);
+                const UmmaHdr hdr = shi ? umma_row_header<FB>(st, r) : umma_row_header<FA>(st, r);
                 for (int jp = 0; jp < 2; jp++) {
                     uint32_t w0[8], w1[8];
                     if (shi) {
-                        umma_dequant<FB>(st, hdr, r, 2 * jp, part, w0);
-                        umma_dequant<FB>(st, hdr, r, 2 * jp + 1, part, w1);
+                        umma_dequant<FB>(st, hdr, tri_lut, r, 2 * jp, part, w0);
+                        umma_dequant<FB>(st, hdr, tri_lut, r, 2 * jp + 1, part, w1);
                     } else {
-                        umma_dequant<FA>(st, hdr, r, 2 * jp, part, w0);
-                        umma_dequant<FA>(st, hdr, r, 2 * jp + 1, part, w1);
+                        umma_dequant<FA>(st, hdr, tri_lut, r, 2 * jp, part, w0);
+                        umma_dequant<FA>(st, hdr, tri_lut, r, 2 * jp + 1, part, w1);
                     }
                     if (jp == 1) {
                         __syncwarp();

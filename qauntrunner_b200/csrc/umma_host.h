@@ -26,6 +26,10 @@ int umma_encode_map(CUtensorMap* map, const void* base, long long rows, int K);
 // shared_rows token rows)
 cudaError_t umma_gather(const float* xn, const int32_t* pos_tok, int Tk, int shared_rows, int d, __half* out,
                         int sm_count, cudaStream_t s);
+// SwiGLU outputs between the two paths: to_f16 = 1 copies the f32 rows of h
+// (routed, [Tk][f]) and hs (shared, [T][f]) into h16 [Tk + T][f]; 0 the reverse
+cudaError_t umma_convert_h(float* h, float* hs, int Tk, int shared_rows, int f, __half* h16, int to_f16, int sm_count,
+                           cudaStream_t s);
 // both stages' work lists from the dispatch's slot table
 cudaError_t umma_plan(const int4* slot_info, const int32_t* n_active, int has_shared, int Tk, int rb_gateup,
                       int rb_down, int E, UmmaItem* gu_items, int32_t* gu_count, UmmaItem* dn_items,

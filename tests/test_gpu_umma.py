@@ -22,6 +22,8 @@ CASES = {
     "c5_small_q4k_shared_q8_0": ("c5", dict(d_model=1024, expert_ffn=512, n_experts=64)),
     "c5_small_q8_0": ("c5", dict(d_model=1024, expert_ffn=512, n_experts=32, fmt=(O.Q8_0,) * 3)),
     "c5_small_limit": ("c5", dict(d_model=1024, expert_ffn=512, n_experts=32, swiglu_limit=7.0)),
+    "c4_small_tri": ("c4", dict(d_model=1024, expert_ffn=1024, n_experts=16)),
+    "c3_small_q6k_down": ("c3", dict(d_model=1536, expert_ffn=512, n_experts=32)),
 }
 
 
