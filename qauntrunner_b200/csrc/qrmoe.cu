@@ -403,7 +403,11 @@ struct qrm_layer {
     int umma_mode = -1;           // -1 by group size, 0 never, 1 always (QRM_UMMA)
     bool umma_forced_gu = false;  // a gate/up format has no other kernel in the tiled layout (Q6_K, TRI)
     bool umma_forced_dn = false;  // same for down
-    int umma_min_tpe = 24;        // average routed tokens per expert from which it is used (QRM_UMMA_MIN_TPE)
+    // average routed tokens per expert from which it is used (QRM_UMMA_MIN_TPE),
+    // or shared-expert tokens: measured crossovers against the decode kernels
+    // on B200 (configs 1-5: from 4 tokens per expert, or 64 shared tokens)
+    int umma_min_tpe = 4;
+    int umma_min_shared = 64;
     __half* act16 = nullptr;      // [Tx*k + Tx][d] f16 gate/up inputs in dispatch order
     __half* h16 = nullptr;        // [Tx*k + Tx][f] f16 down inputs
     qrm::UmmaItem* umma_items = nullptr;   // [2][cap]: gate/up items, down items
@@ -694,7 +698,8 @@ static int umma_setup(qrm_layer* L) {
     const bool forced = L->umma_forced_gu || L->umma_forced_dn;
     if (forced && (!fmts || !shapes))
         return fail(QRM_E_FORMAT, "this combination of Q6_K / TRI expert formats and shapes has no kernel");
-    const bool reach = forced || L->umma_mode == 1 || (L->umma_mode != 0 && Tk >= (long long)L->umma_min_tpe * E);
+    const bool reach = forced || L->umma_mode == 1 ||
+                       (L->umma_mode != 0 && (Tk >= (long long)L->umma_min_tpe * E || (sh && Tx >= L->umma_min_shared)));
     if (!fmts || !shapes || !reach) return QRM_OK;
     const long long rows = Tk + (sh ? Tx : 0);
     L->umma_cap = qrm::umma_item_cap(L->n_local, Tk, sh ? Tx : 0, f / 64, d / 128);
@@ -1088,7 +1093,9 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     // 4. gate/up (+ SwiGLU) and 5. down
     // each stage takes the tcgen05 grouped path for large groups, and always
     // for the formats that have no other kernel in the tiled layout
-    const bool large = L->umma_ok && (L->umma_mode == 1 || (long long)Tx * k >= (long long)L->umma_min_tpe * E);
+    const bool large = L->umma_ok && (L->umma_mode == 1 ||
+                                      (L->umma_mode != 0 && ((long long)Tx * k >= (long long)L->umma_min_tpe * E ||
+                                                             (shared && Tx >= L->umma_min_shared))));
     const bool u_gu = L->umma_ok && (large || L->umma_forced_gu);
     const bool u_dn = L->umma_ok && (large || L->umma_forced_dn);
     const int Tk = Tx * k;
