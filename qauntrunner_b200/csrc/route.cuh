@@ -675,7 +675,8 @@ __host__ __device__ inline size_t route_fused_main_floats(int d, int T, int E) {
            (size_t)(T + 3) / 4 * 4 + (size_t)(E + 3) / 4 * 4 + 64;
 }
 inline size_t route_tail_smem(int E, int T) {
-    return sizeof(float) * (size_t)2 * T * E + sizeof(int) * 64;
+    // sv, key [T][E] | asg [32] | rsel [kRouteFusedMaxT][kMaxK] | wred [T][4]
+    return sizeof(float) * (size_t)2 * T * E + sizeof(int) * (32 + 4 * 8 + 16);
 }
 inline size_t route_fused_smem(int d, int T, int E) {
     return (sizeof(float) * route_fused_main_floats(d, T, E) + 15) / 16 * 16 + 4 * 8;   // + 3 mbarriers
@@ -721,7 +722,7 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
     float* sv = reinterpret_cast<float*>(scratch);                       // [T][E] weight sources
     uint32_t* key = reinterpret_cast<uint32_t*>(sv + (size_t)T * E);     // [T][E] ranking keys
     int* asg = reinterpret_cast<int*>(key + (size_t)T * E);              // [32] expert of assignment a
-    float* wred = reinterpret_cast<float*>(asg + 32);                    // [T][NW] max / sum scratch
+    float* wred = reinterpret_cast<float*>(asg + 32 + kRouteFusedMaxT * kMaxK);   // [T][NW] max / sum scratch
     if (!tp.sigmoid) {
         // max from float.MinValue (comparisons skip NaN like the reference loop)
         for (int t = 0; t < T; t++) {
@@ -772,57 +773,61 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
         }
     }
     __syncthreads();
-    if (warp < T) {
-        const int t = warp;
-        uint32_t kr[J];
+    // selection by rank: candidate c of token t has rank #{j : key_j > key_c
+    // or (key_j == key_c and j < c)} (value descending, index ascending, a
+    // total order), computed by every thread for its candidates in a short
+    // loop (the tail runs once per forward on one CTA: compact code matters
+    // more than instruction count); ranks below k name the selected experts
+    int* rsel = asg + 32;   // [T][kMaxK] (the weight scratch follows)
+    // a thread ranks up to 4 candidates of one token at once (c = tid + 128 m),
+    // each key load shared by them, four independent loads in flight
+    constexpr int CM = kMaxE / kRouteThreads;
+#pragma unroll 1
+    for (int t = 0; t < T; t++) {
+        const uint32_t* kt = key + (size_t)t * E;
+        uint32_t kc[CM];
+        int rank[CM];
 #pragma unroll
-        for (int jj = 0; jj < J; jj++) kr[jj] = lane + 32 * jj < E ? key[t * E + lane + 32 * jj] : 0u;
-        uint32_t taken = 0;
-        int sel[kMaxK];
-        float ssel[kMaxK];
+        for (int m = 0; m < CM; m++) {
+            const int c = tid + kRouteThreads * m;
+            kc[m] = c < E ? kt[c] : 0u;
+            rank[m] = 0;
+        }
+        const int ncm = (E - tid + kRouteThreads - 1) / kRouteThreads;   // candidates of this thread
+#pragma unroll 4
+        for (int j = 0; j < E; j++) {
+            const uint32_t q = kt[j];
 #pragma unroll
-        for (int r = 0; r < kMaxK; r++) {
-            if (r < k) {
-                uint32_t bk = 0;
-                int bj = -1;
-#pragma unroll
-                for (int jj = 0; jj < J; jj++) {
-                    const bool ok = lane + 32 * jj < E && !(taken & (1u << jj));
-                    if (ok && (bj < 0 || kr[jj] > bk)) { bk = kr[jj]; bj = jj; }
-                }
-                const uint32_t m = __reduce_max_sync(0xffffffffu, bj >= 0 ? bk : 0u);
-                // lanes hold indices lane + 32*jj: the lowest index among the maxima
-                const uint32_t cand = (bj >= 0 && bk == m) ? (uint32_t)(bj * 32 + lane) : 0xffffffffu;
-                const uint32_t win = __reduce_min_sync(0xffffffffu, cand);
-                sel[r] = (int)win;
-                ssel[r] = sv[t * E + (int)win];
-                if ((int)(win & 31) == lane) taken |= 1u << (win >> 5);
+            for (int m = 0; m < CM; m++) {
+                const int c = tid + kRouteThreads * m;
+                rank[m] += (q > kc[m] || (q == kc[m] && j < c)) ? 1 : 0;
             }
         }
-        if (lane == 0) {
-            int32_t* oi = tp.topk_idx + (size_t)t * k;
-            float* ow = tp.topk_w + (size_t)t * k;
+#pragma unroll
+        for (int m = 0; m < CM; m++)
+            if (m < ncm && rank[m] < k) rsel[t * kMaxK + rank[m]] = tid + kRouteThreads * m;
+    }
+    __syncthreads();
+    if (warp < T) {
+        // weights of token t = warp: the sum in rank order on lane 0 (bit-exact
+        // sequence), then one lane per selected expert
+        const int t = warp;
+        const int e = lane < k ? rsel[t * kMaxK + lane] : 0;
+        const float se = lane < k ? sv[t * E + e] : 0.f;
+        float sum = 0.f;
+#pragma unroll 1
+        for (int r = 0; r < k; r++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, se, r));
+        if (lane < k) {
+            float wv;
             if (!tp.sigmoid) {
-                float sum = 0.f;
-#pragma unroll
-                for (int r = 0; r < kMaxK; r++) if (r < k) sum = __fadd_rn(sum, ssel[r]);
-                if (sum <= 0.f) sum = 1.f;
-#pragma unroll
-                for (int r = 0; r < kMaxK; r++)
-                    if (r < k) { oi[r] = sel[r]; ow[r] = __fdiv_rn(ssel[r], sum); asg[t * k + r] = sel[r]; }
+                wv = __fdiv_rn(se, sum <= 0.f ? 1.f : sum);
             } else {
-                float wsum = 0.f;
-#pragma unroll
-                for (int r = 0; r < kMaxK; r++) if (r < k) wsum = __fadd_rn(wsum, ssel[r]);
-                const float inv2 = __fdiv_rn(1.f, __fadd_rn(wsum, 1e-20f));
-#pragma unroll
-                for (int r = 0; r < kMaxK; r++)
-                    if (r < k) {
-                        oi[r] = sel[r];
-                        ow[r] = __fmul_rn(__fmul_rn(ssel[r], inv2), tp.routed_scale);
-                        asg[t * k + r] = sel[r];
-                    }
+                const float inv2 = __fdiv_rn(1.f, __fadd_rn(sum, 1e-20f));
+                wv = __fmul_rn(__fmul_rn(se, inv2), tp.routed_scale);
             }
+            tp.topk_idx[(size_t)t * k + lane] = e;
+            tp.topk_w[(size_t)t * k + lane] = wv;
+            asg[t * k + lane] = e;
         }
     }
     for (int a = n + tid; a < 32; a += kRouteThreads) asg[a] = 0x7fffffff;   // padding sorts last
