@@ -15,7 +15,8 @@ prints one line per (config, T) of the measurement plan.
   python bench.py --impl reference ...   # the reference CPU algorithm on the host cores
 
 Timing: W untimed warm-up steps, then K steps each timed with CUDA events on
-the forward's stream; L2 is flushed (256 MiB write) before every step outside
+the forward's stream; L2 is flushed (256 MiB written, then another 256 MiB read,
+so no dirty lines are left to write back) before every step outside
 the events, and each step feeds new tokens (so new experts).  Multi-GPU: one
 process per GPU under torchrun; value = all ranks' tokens / max-over-ranks
 time.  e2e = the drop-in call (qrm_forward: pageable host arrays in and out,
@@ -297,7 +298,7 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
     dev = int(os.environ.get("LOCAL_RANK", 0))
     cfg = CONFIGS[cfg_name]
     d, E = cfg["d_model"], cfg["n_experts"]
-    spec = SynthLayer(cfg_name)
+    spec = SynthLayer(cfg_name, **({"n_experts": args.experts} if args.experts else {}))
     t_build = time.perf_counter()
     nccl_id = None
     if world > 1:
@@ -319,6 +320,17 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
     idx = torch.empty((T, layer.k), dtype=torch.int32, device=f"cuda:{dev}")
     wts = torch.empty((T, layer.k), dtype=torch.float32, device=f"cuda:{dev}")
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{dev}")
+    # write-read: a second buffer larger than L2 is read after the write, so
+    # the written lines are cleaned out of L2 before the step instead of being
+    # written back to HBM inside it (L2 holds no layer data either way)
+    flush_rd = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{dev}") \
+        if args.flush == "write-read" else None
+    flush_out = torch.empty(1, dtype=torch.float32, device=f"cuda:{dev}")
+
+    def flush_cache(i):
+        flush.fill_(float(i))
+        if flush_rd is not None:
+            torch.sum(flush_rd, dim=0, keepdim=True, out=flush_out)
     stream = torch.cuda.Stream()
     sp = stream.cuda_stream
 
@@ -331,12 +343,12 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
     sync_buf = torch.zeros(1, device=f"cuda:{dev}") if world > 1 else None
 
     def flush_l2(i):
-        flush.fill_(float(i))
+        flush_cache(i)
         if sync_buf is not None:
             dist.all_reduce(sync_buf)
 
     with torch.cuda.stream(stream):
-        for prof in ((False, True) if world == 1 else (False,)):   # capture the forward graphs before timing
+        for prof in (False, True):   # capture the forward graphs before timing
             layer.set_profiling(prof)
             for i in range(args.warmup):
                 flush_l2(i)
@@ -381,7 +393,7 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
         layer.set_profiling(True)
         with torch.cuda.stream(stream):
             for i in range(nprof):
-                flush.fill_(float(i))
+                flush_cache(i)
                 step(args.warmup + i)
                 ms, by = layer.last_profile()
                 stage_ms += ms
@@ -391,6 +403,23 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
         layer.set_profiling(False)
         torch.cuda.synchronize()
         layer.sync()
+    ep_stage = None
+    if world > 1:
+        # expert parallel: every rank runs the same profiled forwards
+        ep_ms = np.zeros(len(Q.EP_STAGES))
+        layer.set_profiling(True)
+        with torch.cuda.stream(stream):
+            for i in range(nprof):
+                flush_l2(i)
+                step(args.warmup + i)
+                ep_ms += layer.last_profile_ep()
+        layer.set_profiling(False)
+        torch.cuda.synchronize()
+        layer.sync()
+        mx = torch.tensor(ep_ms / nprof, dtype=torch.float64, device=f"cuda:{dev}")
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        ep_stage = dict(rank0={n: float(v) for n, v in zip(Q.EP_STAGES, ep_ms / nprof)},
+                        max_over_ranks={n: float(v) for n, v in zip(Q.EP_STAGES, mx.cpu().numpy())})
 
     # ---- e2e (pinned): host buffers, copies inside the events
     nh = min(nx, args.steps + args.warmup)
@@ -431,7 +460,7 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
         dist.barrier()
     e2e_ms = 0.0
     for i in range(args.steps):
-        flush.fill_(float(i))
+        flush_cache(i)
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
@@ -522,11 +551,13 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
         data="synthetic",
         config=dict(workload=NAMES[cfg_name], tokens_per_rank=T, d_model=d, n_experts=E, top_k=cfg["n_active"],
                     expert_ffn=cfg["expert_ffn"], formats=FORMATS[cfg_name],
-                    l2="flushed before every step (256 MiB write, outside the timed events)",
+                    l2=("flushed before every step outside the timed events: 256 MiB written" +
+                        (", then another 256 MiB buffer read (no dirty lines left to write back)"
+                         if args.flush == "write-read" else "")),
                     parallelism="single GPU" if world == 1 else f"ep{world} (expert parallel, {transport} exchanges)"),
         roofline=roofline,
         layer_hbm=layer_hbm,
-        stage_ms_per_step={n: float(stage_ms[i] / nprof) for i, n in enumerate(Q.STAGES)} if world == 1 else None,
+        stage_ms_per_step={n: float(stage_ms[i] / nprof) for i, n in enumerate(Q.STAGES)} if world == 1 else ep_stage,
         cpu_baseline=cpu,
         e2e=dict(value=tokens / (e2e_ms / 1000.0), unit="tokens/s", h2d_bytes_per_step=T * d * 4,
                  d2h_bytes_per_step=T * d * 4 + T * layer.k * 8,
@@ -551,6 +582,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--experts", type=int, default=0, help="routed experts (a smaller case of the config)")
+    ap.add_argument("--flush", choices=["write", "write-read"], default="write-read",
+                    help="L2 flush between steps: write a buffer larger than L2, then (write-read) read another")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -97,6 +97,8 @@ const char* qrm_last_error(void);
  * (PrefetchPipeline.cs:64-166): the layer's experts live in HBM. */
 int  qrm_create(const qrm_layer_desc* desc, qrm_layer** out);
 void qrm_destroy(qrm_layer* layer);
+/* The description the layer was created with. */
+int  qrm_layer_get_desc(qrm_layer* layer, qrm_layer_desc* desc);
 
 /* ---- uploads (host bytes are copied; the caller may unmap afterwards) ----
  * Replace Dequant1D(l{i}.ffn_norm) (StreamingEngine.cs:196-201,259),
@@ -120,6 +122,26 @@ int qrm_upload_expert(qrm_layer* layer, int expert, int which, int fmt,
 int qrm_upload_expert_device(qrm_layer* layer, int expert, int which, int fmt,
                              const void* bytes_dev, size_t nbytes);
 int qrm_download_expert(qrm_layer* layer, int expert, int which, void* bytes, size_t nbytes);
+
+/* ---- .qw weight files (ModelStore.Open, src/QuantRunner.Core/Memory/
+ * ModelStore.cs:85-126) ----
+ * qrm_qw_layer_desc fills *out for MoE layer `layer_index` of the file: the
+ * ModelConfig fields of the header's "config" (ModelConfig.cs:14-61; d_ff =
+ * EffectiveExpertFfn), the formats of l{i}.e0.w_gate / w_up / w_down and of
+ * l{i}.sw_* (n_shared becomes 0 when those tensors are absent, as the engine
+ * skips the shared expert then, StreamingEngine.cs:779), plus the caller's
+ * device and max_tokens.  No GPU work.  QRM_E_STATE when the layer has no
+ * l{i}.router (a dense FFN layer, StreamingEngine.cs:633-637).
+ * qrm_load_qw maps the file read-only for the call and uploads layer
+ * `layer_index`'s tensors by their canonical names (NameMapper.cs:7-12):
+ * l{i}.ffn_norm when present, l{i}.router and (GLM) l{i}.router_bias as
+ * F32 / F16 / BF16 (widened exactly), and as stored (no requantisation) the
+ * expert matrices l{i}.e{j}.w_gate / w_up / w_down of the experts the layer
+ * holds and l{i}.sw_gate / sw_up / sw_down when it has a shared expert.  A
+ * missing tensor is QRM_E_STATE, a wrong shape QRM_E_INVALID, a wrong format
+ * QRM_E_FORMAT, a malformed file QRM_E_INVALID. */
+int qrm_qw_layer_desc(const char* path, int layer_index, int device, int max_tokens, qrm_layer_desc* out);
+int qrm_load_qw(qrm_layer* layer, const char* path, int layer_index);
 
 /* ---- forward ----
  * One MoE layer over T tokens (the reference runs T sequential Forward calls).
@@ -194,19 +216,23 @@ int  qrm_matrix_gemv_static(qrm_matrix* m, const float* x_dev, int T, float* y_d
  * with QRM_E_INVALID) and replicas of norm, router and shared expert.  Every
  * rank calls qrm_forward / qrm_forward_device with the same T for its own
  * tokens, the same number of times; the forward routes them (bit-identical on
- * every rank), gathers the normalised tokens with their top-k on every rank,
- * runs the local experts for all ranks' tokens, returns the expert outputs to
- * the token owners and combines on the owner in slot order, so the output
- * equals the single-GPU forward bit for bit.  The exchanges are stores into
- * the peers' memory over NVLink (CUDA IPC mappings made at creation) when
- * every rank can map every other rank's memory, else NCCL all-gather and
- * grouped send/recv (QRM_EP_P2P=0 in the environment forces NCCL); a peer
+ * every rank), sends each token to the ranks that hold its experts, runs the
+ * local experts for the assignments this rank holds, returns each expert
+ * output row to the token's owner, runs the shared expert for the owner's own
+ * tokens and combines on the owner in slot order, so the output equals the
+ * single-GPU forward bit for bit.  The exchanges are stores into the peers'
+ * memory over NVLink (CUDA IPC mappings made at creation: a token row goes
+ * only to ranks holding one of its experts, an output row only to its owner)
+ * when every rank can map every other rank's memory, else NCCL all-gather and
+ * grouped send/recv of fixed-size blocks (QRM_EP_P2P=0 in the environment
+ * forces NCCL); a peer
  * that does not deliver within about a second makes qrm_sync return
  * QRM_E_TIMEOUT, after which the layer should be destroyed.  The id comes
  * from qrm_nccl_unique_id on one rank and is passed to every rank by the host
  * (128 bytes); qrm_create_ep returns once all ranks have joined, and
  * qrm_destroy of an expert-parallel layer is collective (it waits up to ~10 s
- * for the other ranks).  Per-stage profiling is single-GPU only. */
+ * for the other ranks).  qrm_last_profile_ep gives the stage times of an
+ * expert-parallel forward (qrm_set_profiling on). */
 #define QRM_NCCL_ID_BYTES 128
 int qrm_nccl_unique_id(void* id_out);
 int qrm_create_ep(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out);
@@ -217,6 +243,15 @@ int qrm_expert_range(qrm_layer* layer, int* first, int* count);
 #define QRM_EP_NCCL 1
 #define QRM_EP_PEER 2
 int qrm_ep_transport(qrm_layer* layer, int* transport);
+/* Per-stage device time (ms) of the last expert-parallel forward, run with
+ * qrm_set_profiling(layer, 1): route (RMSNorm, router, own top-k), records
+ * (token rows and top-k rows to the experts' ranks, then the dispatch, which
+ * waits for every rank's records), gate/up, down, outputs (expert output rows
+ * to the tokens' owners), combine (waits for every holder's rows).  A wait on
+ * a slower rank counts in the stage that waits. */
+enum { QRM_EP_STAGE_ROUTE = 0, QRM_EP_STAGE_RECORDS, QRM_EP_STAGE_GATEUP, QRM_EP_STAGE_DOWN, QRM_EP_STAGE_OUTPUTS,
+       QRM_EP_STAGE_COMBINE, QRM_EP_STAGE_COUNT };
+int qrm_last_profile_ep(qrm_layer* layer, float* ms);
 
 /* ---- synthetic weights on the device (the reference's `synthesize`,
  * src/QuantRunner.Cli/Program.cs:247-369) ----

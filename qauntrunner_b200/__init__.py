@@ -40,6 +40,8 @@ SHARED_EXPERT = -1
 APPLY_NORM, ADD_RESIDUAL = 1, 2
 STAGES = ("route", "topk", "dispatch", "gateup", "down", "combine")
 STAGE_COUNT = len(STAGES)
+EP_STAGES = ("route", "records", "gateup", "down", "outputs", "combine")
+E_INVALID, E_FORMAT, E_SIZE, E_STATE, E_CUDA, E_NCCL, E_TIMEOUT, E_NOMEM, E_CAPACITY = range(-1, -10, -1)
 ERRORS = {-1: "QRM_E_INVALID", -2: "QRM_E_FORMAT", -3: "QRM_E_SIZE", -4: "QRM_E_STATE", -5: "QRM_E_CUDA",
           -6: "QRM_E_NCCL", -7: "QRM_E_TIMEOUT", -8: "QRM_E_NOMEM", -9: "QRM_E_CAPACITY"}
 
@@ -84,6 +86,9 @@ _SIGS = {
     "qrm_last_error": (C.c_char_p, []),
     "qrm_create": (C.c_int, [C.POINTER(LayerDesc), C.POINTER(P)]),
     "qrm_destroy": (None, [P]),
+    "qrm_layer_get_desc": (C.c_int, [P, C.POINTER(LayerDesc)]),
+    "qrm_qw_layer_desc": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(LayerDesc)]),
+    "qrm_load_qw": (C.c_int, [P, C.c_char_p, C.c_int]),
     "qrm_upload_norm": (C.c_int, [P, P]),
     "qrm_upload_router": (C.c_int, [P, P, P]),
     "qrm_upload_logit_offset": (C.c_int, [P, P]),
@@ -106,6 +111,7 @@ _SIGS = {
     "qrm_create_ep": (C.c_int, [C.POINTER(LayerDesc), C.c_int, C.c_int, P, C.POINTER(P)]),
     "qrm_expert_range": (C.c_int, [P, P, P]),
     "qrm_ep_transport": (C.c_int, [P, P]),
+    "qrm_last_profile_ep": (C.c_int, [P, P]),
     "qrm_synth_gaussian": (C.c_int, [P, C.c_int64, C.c_uint64, C.c_float, P]),
     "qrm_synth_quantize": (C.c_int, [C.c_int, P, C.c_int64, P, P]),
 }
@@ -158,6 +164,14 @@ def _ptr(a):
     return a.ctypes.data_as(P).value
 
 
+def qw_layer_desc(path, layer_index, device=0, max_tokens=1):
+    """LayerDesc of MoE layer `layer_index` of a .qw file, from its header
+    (qrm_qw_layer_desc; no GPU work)."""
+    d = LayerDesc()
+    _check(lib().qrm_qw_layer_desc(os.fsencode(path), layer_index, device, max_tokens, C.byref(d)))
+    return d
+
+
 class MoeLayer:
     """One MoE FFN layer resident on a GPU.
 
@@ -187,6 +201,29 @@ class MoeLayer:
         else:
             _check(lib().qrm_create(C.byref(self.desc), C.byref(h)))
         self._h = h
+
+    @classmethod
+    def from_qw(cls, path, layer_index, device=0, max_tokens=1, rank=0, world=1, nccl_id=None):
+        """MoE layer `layer_index` of a .qw file (ModelStore.Open), its
+        description from the file's header and its tensors uploaded by their
+        canonical names."""
+        d = qw_layer_desc(path, layer_index, device, max_tokens)
+        L = cls(d.d_model, d.n_experts, d.n_active, d.expert_ffn, moe_sigmoid=bool(d.moe_sigmoid),
+                routed_scale=d.routed_scale, n_shared=d.n_shared, swiglu_limit=d.swiglu_limit, rms_eps=d.rms_eps,
+                fmt=(d.fmt_gate, d.fmt_up, d.fmt_down), shared_fmt=(d.fmt_sh_gate, d.fmt_sh_up, d.fmt_sh_down),
+                device=device, max_tokens=max_tokens, rank=rank, world=world, nccl_id=nccl_id)
+        try:
+            _check(lib().qrm_load_qw(L._h, os.fsencode(path), layer_index))
+        except Exception:
+            L.close()
+            raise
+        return L
+
+    def get_desc(self):
+        """The qrm_layer_desc the library holds for this layer."""
+        d = LayerDesc()
+        _check(lib().qrm_layer_get_desc(self._h, C.byref(d)))
+        return d
 
     def expert_range(self):
         """(first, count) of the routed experts this layer holds."""
@@ -280,6 +317,13 @@ class MoeLayer:
         by = np.zeros(STAGE_COUNT, np.float64)
         _check(lib().qrm_last_profile(self._h, _ptr(ms), _ptr(by)))
         return ms, by
+
+    def last_profile_ep(self):
+        """ms per stage of the last expert-parallel forward; stages: route,
+        records, gate/up, down, outputs, combine (EP_STAGES)."""
+        ms = np.zeros(len(EP_STAGES), np.float32)
+        _check(lib().qrm_last_profile_ep(self._h, _ptr(ms)))
+        return ms
 
     def last_launch_count(self):
         """Kernel launches of this library in the last forward."""

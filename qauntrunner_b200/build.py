@@ -22,7 +22,7 @@ LIB = os.path.join(PKG, "lib", "libqrmoe.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", os.path.join(ROOT, "include"),
           "--expt-relaxed-constexpr"]
-UNITS = [("qrmoe.cu", []), ("umma.cu", []), ("synth.cu", ["-fmad=false"])]
+UNITS = [("qrmoe.cu", []), ("umma.cu", []), ("qwfile.cu", []), ("synth.cu", ["-fmad=false"])]
 
 
 def nvcc():

@@ -1,38 +1,43 @@
-// ep.cuh -- expert-parallel data movement around the NCCL exchanges.
+// ep.cuh -- expert-parallel data movement.
 //
 // G ranks, one process per GPU, each holding the routed experts
 // [rank*E/G, (rank+1)*E/G) and a replica of norm, router and shared expert.
-// Per forward every rank routes its own T tokens, all-gathers (normalised
-// token, top-k indices, top-k weights) records, runs its experts for the
-// G*T gathered tokens, returns each expert output row to the owner of its
-// token, and the owner adds the rows in slot order.  The kernels here pack and
-// unpack those messages; the exchanges are ncclAllGather and grouped
-// ncclSend / ncclRecv in qrmoe.cu.
-//
-// Message layouts (f32 words):
-//   record of token t: xn[d] | top-k indices[k] (int32 bits) | top-k weights[k]
-//   output block for owner q: [T*k][d] rows, row t*k+j = expert output of q's
-//   token t, slot j (only the rows whose expert this rank holds are written;
-//   the owner reads exactly those).
+// Per forward every rank routes its own T tokens; gathered token u = p*T + t
+// is rank p's token t on every rank.
 //
 // Peer-memory mode (NVLink through NVSwitch, the default when every rank can
 // map every other rank's memory): each rank owns one "mailbox" allocation,
-// mapped into every peer's address space.  A sender stores its normalised
-// tokens and top-k indices straight into the gathered-token arrays of every
-// peer, and its expert output rows straight into each owner's receive blocks,
-// then raises a per-sender flag in the receiver's mailbox to the forward's
-// epoch; the receiving kernels (dispatch, combine) wait for the flags of all
-// senders.  The epoch is a per-rank counter in device memory (dispatch
-// advances it), so captured CUDA graphs replay correctly.  Every wait is
-// bounded: on expiry the kernel sets ERR_TIMEOUT and carries on over the
-// stale (in-bounds) contents; qrm_sync reports the error.
+// mapped into every peer's address space, holding
+//   rec_flag[G], out_flag[G]   epoch of the last records / outputs from rank p
+//   xn  [G*T][d]               gathered token rows (rows of rank p at p*T)
+//   idx [G*T][k]               gathered top-k rows
+//   y   [T*k][d]               expert output rows of this rank's tokens
+// A sender stores into every rank q the top-k rows of all its tokens and the
+// token rows of only those tokens with an expert on q (into its own mailbox
+// all of them: the shared expert runs there for the owner's tokens), then
+// raises its record flag in q's mailbox.  q's dispatch waits for all G record
+// flags and keeps the assignments of its own experts.  After the expert
+// stages, each output row (gathered token u = p*T + t, slot j) is stored at
+// row t*k + j of owner p's y block -- each assignment has exactly one holder,
+// so one block per owner takes every holder's rows -- and the last block of
+// the push raises this rank's output flag in every owner's mailbox.  The
+// owner's combine waits for all G output flags.  The epoch is a per-rank
+// counter in device memory (dispatch advances it), so captured CUDA graphs
+// replay correctly.  Every wait is bounded: on expiry the kernel sets
+// ERR_TIMEOUT and carries on over the stale (in-bounds) contents; qrm_sync
+// reports the error.
 //
 // Buffer reuse needs no extra handshake: a sender writes forward N+1's
 // records into a peer only after its combine of forward N has seen that
 // peer's outputs of forward N, which the peer pushed after its expert kernels
 // finished reading forward N's records; and it writes forward N+1's outputs
 // only after its dispatch has seen the owner's forward N+1 records, which the
-// owner sent after its combine of forward N was done with the receive blocks.
+// owner sent after its combine of forward N was done with its y block.
+//
+// NCCL mode: the (token row, top-k indices, top-k weights) records of every
+// rank are all-gathered, and output block q ([T*k][d], row t*k+j, only the
+// rows of experts this rank holds) goes to owner q by grouped send/recv; the
+// owner reads row t*k+j from the block of the rank holding expert idx[t][j].
 #pragma once
 #include "common.cuh"
 
@@ -103,43 +108,71 @@ __device__ inline void ep_signal(const EpPeers& p, int which, int q, uint32_t ep
     }
 }
 
-// Records of this rank's T tokens into every rank's gathered arrays, rows
-// [rank*T, rank*T + T).  Grid: G*nb blocks, nb per destination.
+// Records of this rank's T tokens into the gathered arrays of every rank q,
+// rows [rank*T, rank*T + T): the top-k rows of all T tokens (q's dispatch
+// reads them all and keeps the assignments of its own experts), the token
+// rows only of tokens with at least one expert on q (epr experts per rank) --
+// all of them into this rank's own mailbox, whose rows the shared expert
+// reads.  Rows that are not sent are never read.  Grid: G*nb blocks, nb per
+// destination.
 __global__ void ep_push_records_kernel(const float* __restrict__ xn, const int32_t* __restrict__ idx, int T, int d,
-                                       int k, EpPeers p) {
+                                       int k, int epr, EpPeers p) {
     const int nb = gridDim.x / p.G, q = blockIdx.x / nb, part = blockIdx.x - q * nb;
     const uint32_t epoch = *p.epoch + 1;
     char* mb = reinterpret_cast<char*>(p.base[q]);
     const int d4 = d / 4;
-    float4* dx = reinterpret_cast<float4*>(mb + p.mb.xn) + (size_t)p.rank * T * d4;
-    const float4* sx = reinterpret_cast<const float4*>(xn);
-    for (int i = part * blockDim.x + threadIdx.x; i < T * d4; i += nb * blockDim.x) dx[i] = sx[i];
     int32_t* di = reinterpret_cast<int32_t*>(mb + p.mb.idx) + (size_t)p.rank * T * k;
     for (int i = part * blockDim.x + threadIdx.x; i < T * k; i += nb * blockDim.x) di[i] = idx[i];
+    float4* dx = reinterpret_cast<float4*>(mb + p.mb.xn) + (size_t)p.rank * T * d4;
+    const float4* sx = reinterpret_cast<const float4*>(xn);
+    const bool own = q == p.rank;
+    int t_seen = -1;
+    bool need = false;
+    for (long long i = part * (long long)blockDim.x + threadIdx.x; i < (long long)T * d4; i += (long long)nb * blockDim.x) {
+        const int t = (int)(i / d4);
+        if (t != t_seen) {
+            t_seen = t;
+            need = own;
+            for (int j = 0; j < k && !need; j++) need = idx[t * k + j] / epr == q;
+        }
+        if (need) dx[i] = sx[i];
+    }
     ep_signal(p, 0, q, epoch, nb);
 }
 
 // Output rows of the local experts straight into the owners' receive blocks:
-// gathered assignment a = (owner q, local assignment i) -> owner q's block of
-// holder `rank`, row i.  Grid: G*nb blocks, nb per owner.
-__global__ void ep_push_outputs_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv_perm,
-                                       const int32_t* __restrict__ idx_all, int T, int k, int d, int first,
-                                       int n_local, EpPeers p) {
-    const int nb = gridDim.x / p.G, q = blockIdx.x / nb, part = blockIdx.x - q * nb;
+// position pos < n_pos of the dispatch holds assignment a = perm[pos] =
+// u*k + j of gathered token u = q*T + t (owner q, its token t), and its row
+// goes to row t*k + j of owner q's block.  Each assignment has exactly one
+// holder, so one [T*k][d] block per owner takes every holder's rows.  Once
+// every block has stored its rows, the last one raises this rank's output
+// flag in every owner's mailbox (also those that get no rows: the flags
+// count forwards).
+__global__ void ep_push_outputs_kernel(const float* __restrict__ y, const int32_t* __restrict__ perm,
+                                       const int32_t* __restrict__ n_pos, int T, int k, int d, EpPeers p) {
     const uint32_t epoch = *p.epoch;   // advanced by this forward's dispatch
-    char* mb = reinterpret_cast<char*>(p.base[q]);
-    const int d4 = d / 4, rows = T * k;
-    float4* dst = reinterpret_cast<float4*>(mb + p.mb.y) + (size_t)p.rank * rows * d4;
+    const int d4 = d / 4;
+    const long long n = (long long)(*n_pos) * d4;
     const float4* src = reinterpret_cast<const float4*>(y);
-    const int32_t* ia = idx_all + (size_t)q * rows;
-    const int32_t* pa = inv_perm + (size_t)q * rows;
-    for (int i = part * blockDim.x + threadIdx.x; i < rows * d4; i += nb * blockDim.x) {
-        const int r = i / d4, c = i - r * d4;
-        const int e = ia[r];
-        if (e < first || e >= first + n_local) continue;
-        dst[i] = src[(size_t)pa[r] * d4 + c];
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int pos = (int)(i / d4), c = (int)(i - (long long)pos * d4);
+        const int a = perm[pos], u = a / k, j = a - u * k, q = u / T, t = u - q * T;
+        char* mb = reinterpret_cast<char*>(p.base[q]);
+        reinterpret_cast<float4*>(mb + p.mb.y)[((size_t)t * k + j) * d4 + c] = src[i];
     }
-    ep_signal(p, 1, q, epoch, nb);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        uint32_t* c = p.cnt + p.G;   // output counter
+        if (atomicAdd(c, 1u) == gridDim.x - 1) {
+            *c = 0;
+            __threadfence_system();
+            for (int q = 0; q < p.G; q++) {
+                char* mb = reinterpret_cast<char*>(p.base[q]);
+                st_release_sys(reinterpret_cast<uint32_t*>(mb + p.mb.out_flag) + p.rank, epoch);
+            }
+        }
+    }
 }
 
 __global__ void ep_pack_records_kernel(const float* __restrict__ xn, const int32_t* __restrict__ idx,
@@ -188,14 +221,16 @@ __global__ void ep_pack_outputs_kernel(const float* __restrict__ y, const int32_
 
 // The owner's combine, in the reference's order: out = (x) + w_0 y_0 + ... +
 // w_{k-1} y_{k-1} (+ shared), each product and sum rounded separately
-// (combine_kernel's arithmetic); y_j comes from the block of the rank that
-// holds expert idx[t][j] (experts per rank: epr).
+// (combine_kernel's arithmetic).  recv holds row t*k + j of y_j: in one
+// [T*k][d] block (peer memory), or per holder ([G][T*k][d], NCCL; the block
+// of the rank that holds expert idx[t][j], epr experts per rank).
 // In peer-memory mode (`wait_flags` set) every block first waits for the
 // output flags of all G holders.
 __global__ void ep_combine_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                   const int32_t* __restrict__ idx, const float* __restrict__ recv,
-                                  const float* __restrict__ ys, int T, int k, int d, int epr, float* __restrict__ out,
-                                  const uint32_t* wait_flags, const uint32_t* epoch, int G, int32_t* err) {
+                                  const float* __restrict__ ys, int T, int k, int d, int epr, int per_holder,
+                                  float* __restrict__ out, const uint32_t* wait_flags, const uint32_t* epoch, int G,
+                                  int32_t* err) {
     if (wait_flags) {
         const uint32_t want = *epoch;
         if ((int)threadIdx.x < G && !ep_wait_flag(wait_flags + threadIdx.x, want)) atomicOr(err, (int32_t)ERR_TIMEOUT);
@@ -209,8 +244,8 @@ __global__ void ep_combine_kernel(const float* __restrict__ x, const float* __re
         float4 acc = x ? reinterpret_cast<const float4*>(x + (size_t)t * d)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
         for (int j = 0; j < k; j++) {
             const float wj = w[t * k + j];
-            const int q = idx[t * k + j] / epr;
-            const float4 v = reinterpret_cast<const float4*>(recv + (((size_t)q * T + t) * k + j) * d)[c];
+            const size_t q = per_holder ? (size_t)(idx[t * k + j] / epr) : 0;
+            const float4 v = reinterpret_cast<const float4*>(recv + ((q * T + t) * k + j) * d)[c];
             acc.x = __fadd_rn(acc.x, __fmul_rn(wj, v.x));
             acc.y = __fadd_rn(acc.y, __fmul_rn(wj, v.y));
             acc.z = __fadd_rn(acc.z, __fmul_rn(wj, v.z));

@@ -324,6 +324,7 @@ struct GemvParams {
     float* out_routed;         // gate/up: h [T*k x f]; down: y [T*k x d]
     float* out_shared;         // gate/up: hs [T x f]; down: ys [T x d]
     int T, k, E;
+    int T_sh;                  // shared-expert tokens (rows of x_shared / out_shared)
     int rows, cols, tiles;     // per expert matrix
     float limit;               // SwiGLU limit (<= 0: plain)
     int routed_by_token;       // gate/up: routed inputs are token rows (perm/k)
@@ -341,6 +342,11 @@ struct GemvParams {
     const float* xq_a;
     const float* xq_b;
     int xq_split;
+    // gate/up launches of the streaming kernel: once the ring is filled, the
+    // producers prefetch the down matrices of the active slots (and of the
+    // shared expert) into L2, each CTA its share, and mark the stage's own
+    // weight copies evict_first, so the down stage reads its weights from L2
+    int prefetch_down;
     // launched as a programmatic dependent: 1 = wait for the predecessor
     // before anything, 2 = the producer streams weights before the wait (the
     // routing it reads was final two launches earlier; only the activations
@@ -391,7 +397,7 @@ expert_gemv_kernel(GemvParams p) {
         const bool shared = slot >= n_active;
         const int r0 = tile * R;
         int n_tok, off = 0;
-        if (shared) n_tok = p.T;
+        if (shared) n_tok = p.T_sh;
         else { off = p.offsets[e]; n_tok = p.offsets[e + 1] - off; }
         const MatDev* md = p.mats + (size_t)e * 3;
         MatDev mat[M];

@@ -207,6 +207,15 @@ cudaError_t launch_k(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// L2 prefetch mask of new layers (qrm_layer::l2_prefetch).
+int l2_prefetch_default() {
+    if (const char* e = getenv("QRM_L2_PREFETCH")) return atoi(e) & 3;
+    return 3;
+}
+// largest prefetch of down matrices during gate/up: what fits in the 126 MB
+// L2 beside the lines the gate/up stream passes through
+constexpr double kPrefetchMaxBytes = 96.0 * 1024 * 1024;
+
 // The streaming integer kernel's launch shape for one matrix launch.
 struct StreamSel {
     int ntk = 1;
@@ -360,9 +369,11 @@ struct qrm_layer {
     float* rec_all = nullptr;     // [world*T][d + 2k] gathered records
     float* xn_all = nullptr;      // [world*T][d]
     int32_t* idx_all = nullptr;   // [world*T][k]
-    float* ysend = nullptr;       // [world][T*k][d] output rows per owner
-    float* yrecv = nullptr;       // [world][T*k][d] rows of this rank's tokens, per holder
-    // xn_all, idx_all and yrecv live in this rank's mailbox; in peer-memory
+    float* ysend = nullptr;       // [world][T*k][d] output rows per owner (NCCL)
+    float* yrecv = nullptr;       // rows of this rank's tokens: [T*k][d] in the mailbox (peer memory)
+                                  // or [world][T*k][d] per holder (yrecv_nccl)
+    float* yrecv_nccl = nullptr;
+    // xn_all, idx_all (and yrecv) live in this rank's mailbox; in peer-memory
     // mode every rank maps every other rank's mailbox and writes into it
     char* mbox = nullptr;
     qrm::EpMailbox mb{};
@@ -408,6 +419,10 @@ struct qrm_layer {
     // on B200 (configs 1-5: from 4 tokens per expert, or 64 shared tokens)
     int umma_min_tpe = 4;
     int umma_min_shared = 64;
+    // L2 prefetch of weights ahead of the stage that reads them (mask): 1 the
+    // shared expert's during the router, 2 the down matrices during gate/up
+    // (QRM_L2_PREFETCH overrides, for measurements)
+    int l2_prefetch = l2_prefetch_default();
     __half* act16 = nullptr;      // [Tx*k + Tx][d] f16 gate/up inputs in dispatch order
     __half* h16 = nullptr;        // [Tx*k + Tx][f] f16 down inputs
     qrm::UmmaItem* umma_items = nullptr;   // [2][cap]: gate/up items, down items
@@ -499,7 +514,7 @@ static void free_layer(qrm_layer* L) {
                     L->logits, L->topk_w, L->h, L->hs, L->y, L->ys, L->out, L->topk_idx, L->perm,
                     L->inv_perm, L->offsets, L->active, L->sched, L->staging, L->xtab_gu, L->xtab_dn,
                     L->pos_tok, L->slot_info, L->act16, L->h16, L->umma_items, L->umma_count,
-                    L->rec_own, L->rec_all, L->ysend, L->peer_base, L->ep_state, L->xch};
+                    L->rec_own, L->rec_all, L->ysend, L->yrecv_nccl, L->peer_base, L->ep_state, L->xch};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     clear_graphs(L);
@@ -564,6 +579,11 @@ static int alloc_work(qrm_layer* L, int T) {
 }
 
 extern "C" int qrm_version(void) { return QRM_ABI_VERSION; }
+// the error text of this thread's last failing call, for the other
+// translation units of the library (not exported)
+extern "C" __attribute__((visibility("hidden"))) int qrm_set_error(int code, const char* msg) {
+    return fail(code, "%s", msg);
+}
 extern "C" const char* qrm_last_error(void) { return g_err.c_str(); }
 
 static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out);
@@ -589,6 +609,12 @@ extern "C" int qrm_create_ep(const qrm_layer_desc* desc, int rank, int world, co
 extern "C" int qrm_ep_transport(qrm_layer* L, int* transport) {
     if (!L || !transport) return fail(QRM_E_INVALID, "NULL argument");
     *transport = L->world == 1 ? QRM_EP_SINGLE : (L->p2p ? QRM_EP_PEER : QRM_EP_NCCL);
+    return QRM_OK;
+}
+
+extern "C" int qrm_layer_get_desc(qrm_layer* L, qrm_layer_desc* desc) {
+    if (!L || !desc) return fail(QRM_E_INVALID, "NULL argument");
+    *desc = L->desc;
     return QRM_OK;
 }
 
@@ -791,18 +817,14 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
         L->mb.xn = (long long)up(8 * G);
         L->mb.idx = L->mb.xn + (long long)up(sizeof(float) * G * T * d);
         L->mb.y = L->mb.idx + (long long)up(sizeof(int32_t) * G * T * k);
-        const size_t mbox_bytes = (size_t)L->mb.y + sizeof(float) * G * T * k * d;
-        if (cudaMalloc(&L->rec_own, sizeof(float) * T * (d + 2 * k)) != cudaSuccess ||
-            cudaMalloc(&L->rec_all, sizeof(float) * G * T * (d + 2 * k)) != cudaSuccess ||
-            cudaMalloc(&L->ysend, sizeof(float) * G * T * k * d) != cudaSuccess ||
-            cudaMalloc(&L->mbox, mbox_bytes) != cudaSuccess ||
+        const size_t mbox_bytes = (size_t)L->mb.y + sizeof(float) * T * k * d;
+        if (cudaMalloc(&L->mbox, mbox_bytes) != cudaSuccess ||
             cudaMalloc(&L->peer_base, sizeof(unsigned long long) * G) != cudaSuccess ||
             cudaMalloc(&L->ep_state, sizeof(uint32_t) * (1 + 2 * G)) != cudaSuccess ||
             cudaMalloc(&L->xch, 128 * G) != cudaSuccess)
             return bail(fail(QRM_E_NOMEM, "expert-parallel buffers"));
         L->xn_all = reinterpret_cast<float*>(L->mbox + L->mb.xn);
         L->idx_all = reinterpret_cast<int32_t*>(L->mbox + L->mb.idx);
-        L->yrecv = reinterpret_cast<float*>(L->mbox + L->mb.y);
         // flags and counters start at zero before any peer can see the mailbox
         if (cudaMemset(L->mbox, 0, mbox_bytes) != cudaSuccess ||
             cudaMemset(L->ep_state, 0, sizeof(uint32_t) * (1 + 2 * G)) != cudaSuccess ||
@@ -814,6 +836,17 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
         if (nr != ncclSuccess) return bail(fail(QRM_E_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(nr)));
         rc = ep_open_peers(L);
         if (rc) return bail(rc);
+        if (L->p2p) {
+            L->yrecv = reinterpret_cast<float*>(L->mbox + L->mb.y);
+        } else {
+            // NCCL: gathered records, one send and one receive block per peer
+            if (cudaMalloc(&L->rec_own, sizeof(float) * T * (d + 2 * k)) != cudaSuccess ||
+                cudaMalloc(&L->rec_all, sizeof(float) * G * T * (d + 2 * k)) != cudaSuccess ||
+                cudaMalloc(&L->ysend, sizeof(float) * G * T * k * d) != cudaSuccess ||
+                cudaMalloc(&L->yrecv_nccl, sizeof(float) * G * T * k * d) != cudaSuccess)
+                return bail(fail(QRM_E_NOMEM, "expert-parallel NCCL buffers"));
+            L->yrecv = L->yrecv_nccl;
+        }
     }
     rc = umma_setup(L);
     if (rc) return bail(rc);
@@ -996,26 +1029,41 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const bool shared = L->shared_enabled && L->uploaded[(size_t)E * 3];
     const bool prof = L->profiling;
     int nl = 0;   // kernel launches of this forward
-    auto mark = [&](int i) { if (prof) cudaEventRecordWithFlags(L->ev[i], s, cudaEventRecordExternal); };
-    mark(0);
+    // expert parallelism: the expert stages run over every rank's tokens
+    const bool ep = L->world > 1;
+    // stage boundaries: event i_single of a single-GPU forward, i_ep of an
+    // expert-parallel one (-1: not a boundary there)
+    auto mark = [&](int i_single, int i_ep) {
+        const int i = ep ? i_ep : i_single;
+        if (prof && i >= 0) cudaEventRecordWithFlags(L->ev[i], s, cudaEventRecordExternal);
+    };
+    mark(0, 0);
     // 1. RMSNorm + router logits, 2. top-k, 3. dispatch
     const float* xn = L->xn;
     qrm::TopkParams tp{L->logits, L->has_bias ? L->router_bias : nullptr, topk_idx, topk_w, T, E, k,
                        D.moe_sigmoid ? 1 : 0, D.routed_scale};
     qrm::DispatchParams dp{topk_idx, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched, T, k, E,
                            L->first_expert, L->n_local, shared ? 1 : 0};
+    dp.T_sh = T;
     qrm::RouteParams rp{x, L->norm_w, L->router, L->has_offset ? L->offset : nullptr, L->xn, L->logits, T, d, E,
                         (flags & QRM_APPLY_NORM) ? 1 : 0, D.rms_eps};
     if (T <= qrm::route_fused_max_tokens(d, E) && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         // one launch: every CTA its experts' logits, the last CTA top-k + dispatch
         const int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
+        qrm::RouteFusedParams fp{rp, L->router_lm, tp, dp, {}, {}, 0};
+        if (shared && (L->l2_prefetch & 1)) {
+            for (int w = 0; w < 3; w++) {
+                fp.pf_ptr[w] = L->mats[(size_t)E * 3 + w].base;
+                fp.pf_bytes[w] = (long long)L->mat_bytes[(size_t)E * 3 + w];
+            }
+            fp.n_pf = 3;
+        }
         nl++;
-        qrm::route_fused_kernel<<<grid, qrm::kRouteThreads, qrm::route_fused_smem(d, T, E), s>>>(
-            qrm::RouteFusedParams{rp, L->router_lm, tp, dp});
+        qrm::route_fused_kernel<<<grid, qrm::kRouteThreads, qrm::route_fused_smem(d, T, E), s>>>(fp);
         QRM_CUDA(cudaGetLastError());
-        mark(1);
-        mark(2);
-        mark(3);
+        mark(1, -1);
+        mark(2, -1);
+        mark(3, 1);
     } else {
         if (T <= qrm::route_small_max_tokens(d)) {
             int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
@@ -1033,7 +1081,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             qrm::logits_tiled_kernel<<<grid, 256, 0, s>>>(xn, L->router, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
         }
         QRM_CUDA(cudaGetLastError());
-        mark(1);
+        mark(1, -1);
         // top-k and dispatch (fused into one single-CTA kernel for T <= 32)
         const bool fused = T <= qrm::kFusedTopkMaxT;
         if (!fused) {
@@ -1041,36 +1089,38 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
             QRM_CUDA(cudaGetLastError());
         }
-        mark(2);
+        mark(2, -1);
         nl++;
         qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, T, fused), s>>>(dp, tp, fused ? 1 : 0);
         QRM_CUDA(cudaGetLastError());
-        mark(3);
+        mark(3, 1);
     }
     L->last_xn = xn;
-    // expert parallelism: the expert stages run over every rank's tokens
-    const bool ep = L->world > 1;
     const int G = L->world;
     int Tx = T;
     const float* xs = xn;
     if (ep) {
-        if (prof) return fail(QRM_E_STATE, "per-stage profiling is single-GPU only");
         Tx = G * T;
         xs = L->xn_all;
     }
+    // the shared expert runs for this rank's own tokens only: rows
+    // [sh_row0, sh_row0 + T) of xs (each rank's rows sit at rank*T)
+    const int Tsh = T;
+    const int sh_row0 = ep ? L->rank * T : 0;
     if (ep && L->p2p) {
         // records straight into every rank's mailbox; the dispatch waits for all of them
         const qrm::EpPeers pe = ep_peers(L);
         const int nb = (int)std::min<long long>(((long long)T * d / 4 + 1023) / 1024, 16);
-        qrm::ep_push_records_kernel<<<G * nb, 256, 0, s>>>(xn, topk_idx, T, d, k, pe);
+        qrm::ep_push_records_kernel<<<G * nb, 256, 0, s>>>(xn, topk_idx, T, d, k, E / G, pe);
         QRM_CUDA(cudaGetLastError());
         qrm::TopkParams tpx{L->logits, nullptr, L->idx_all, nullptr, Tx, E, k, 0, 1.f};
         qrm::DispatchParams dpx{L->idx_all, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched,
                                 Tx, k, E, L->first_expert, L->n_local, shared ? 1 : 0,
-                                reinterpret_cast<const uint32_t*>(L->mbox + L->mb.rec_flag), L->ep_state, G};
+                                reinterpret_cast<const uint32_t*>(L->mbox + L->mb.rec_flag), L->ep_state, G, Tsh, 1};
         qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, Tx, false), s>>>(dpx, tpx, 0);
         QRM_CUDA(cudaGetLastError());
         nl += 2;
+        mark(-1, 2);
     } else if (ep) {
         // (normalised token, top-k) records of every rank
         const int W = d + 2 * k;
@@ -1086,9 +1136,12 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         qrm::TopkParams tpx{L->logits, nullptr, L->idx_all, nullptr, Tx, E, k, 0, 1.f};
         qrm::DispatchParams dpx{L->idx_all, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched,
                                 Tx, k, E, L->first_expert, L->n_local, shared ? 1 : 0};
+        dpx.T_sh = Tsh;
+        dpx.local_only = 1;
         qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, Tx, false), s>>>(dpx, tpx, 0);
         QRM_CUDA(cudaGetLastError());
         nl += 3;
+        mark(-1, 2);
     }
     // 4. gate/up (+ SwiGLU) and 5. down
     // each stage takes the tcgen05 grouped path for large groups, and always
@@ -1102,7 +1155,9 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     if (u_gu || u_dn) {
         // work lists of both stages from the dispatch's slot table; f16
         // activations in dispatch order for a grouped gate/up
-        if (u_gu) QRM_CUDA(qrm::umma_gather(xs, L->pos_tok, Tk, shared ? Tx : 0, d, L->act16, L->sm_count, s));
+        if (u_gu)
+            QRM_CUDA(qrm::umma_gather(xs, xs + (size_t)sh_row0 * d, L->pos_tok, Tk, shared ? Tsh : 0, d, L->act16,
+                                      L->sm_count, s));
         QRM_CUDA(qrm::umma_plan(L->slot_info, &L->sched->n_active, shared ? 1 : 0, Tk, f / 64, d / 128, E,
                                 L->umma_items, L->umma_count, L->umma_items + L->umma_cap, L->umma_count + 1,
                                 (int)L->umma_cap, s));
@@ -1121,13 +1176,13 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                                              &L->sched->err, L->sm_count, s);
             if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped gate/up launch: %s", cudaGetErrorString(e));
             nl++;
-            mark(4);
+            mark(4, 3);
             continue;
         }
         if (!gu && u_dn != u_gu) {
             // the stages took different paths: hand the SwiGLU outputs over
             // (f32 h / hs of the decode kernels <-> f16 rows of the grouped one)
-            QRM_CUDA(qrm::umma_convert_h(L->h, shared ? L->hs : nullptr, Tk, shared ? Tx : 0, f, L->h16, u_dn ? 1 : 0,
+            QRM_CUDA(qrm::umma_convert_h(L->h, shared ? L->hs : nullptr, Tk, shared ? Tsh : 0, f, L->h16, u_dn ? 1 : 0,
                                          L->sm_count, s));
             nl++;
         }
@@ -1137,7 +1192,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                                              L->y, L->ys, &L->sched->err, L->sm_count, s);
             if (e != cudaSuccess) return fail(QRM_E_CUDA, "grouped down launch: %s", cudaGetErrorString(e));
             nl++;
-            mark(5);
+            mark(5, 4);
             continue;
         }
         // activation tables for the integer tensor-core kernel
@@ -1147,8 +1202,8 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         qrm::GemvParams gp{};
         gp.xtab = want_tab ? (gu ? L->xtab_gu : L->xtab_dn) : nullptr;
         gp.xtab_stride = qrm::xtab_stride(cols_s);
-        gp.xtab_shared_base = gu ? 0 : Tx * k;
-        gp.xtab_rows = gu ? Tx : Tx * k + (shared ? Tx : 0);
+        gp.xtab_shared_base = gu ? sh_row0 : Tx * k;
+        gp.xtab_rows = gu ? Tx : Tx * k + (shared ? Tsh : 0);
         gp.mats = L->mats_dev;
         gp.active = L->active;
         gp.offsets = L->offsets;
@@ -1157,10 +1212,11 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         gp.slot_info = L->slot_info;
         gp.n_active = &L->sched->n_active;
         gp.x_routed = gu ? xs : L->h;
-        gp.x_shared = gu ? xs : L->hs;
+        gp.x_shared = gu ? xs + (size_t)sh_row0 * d : L->hs;
         gp.out_routed = gu ? L->h : L->y;
         gp.out_shared = gu ? L->hs : L->ys;
         gp.T = Tx;
+        gp.T_sh = Tsh;
         gp.k = k;
         gp.E = E;
         gp.rows = gu ? f : d;
@@ -1172,6 +1228,14 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         const int fr = gu ? D.fmt_gate : D.fmt_down;
         const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
         gp.pdl = (!prof && (L->pdl & (gu ? 1 : 2))) ? (gu ? 1 : 2) : 0;   // profiling events sit between the launches
+        // down weights into L2 during gate/up when they fit beside the stream
+        // (decode batches): at most min(T*k, local experts) routed matrices
+        if (gu && (L->l2_prefetch & 2)) {
+            const size_t e0 = (size_t)L->first_expert * 3 + 2;
+            const double pf = (double)std::min(Tx * k, L->n_local) * L->mat_bytes[e0] +
+                              (shared ? (double)L->mat_bytes[(size_t)E * 3 + 2] : 0.0);
+            gp.prefetch_down = pf <= kPrefetchMaxBytes ? 1 : 0;
+        }
         // routed + shared expert in one integer-kernel launch when the pair of
         // formats has one
         StreamSel sp;
@@ -1207,7 +1271,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                     rc = launch_xquant(L->h, f, Tx * k, L->xtab_dn, s);
                     nl++;
                     if (!rc && shared) {
-                        rc = launch_xquant(L->hs, f, Tx, L->xtab_dn + (size_t)qrm::xtab_stride(f) * Tx * k, s);
+                        rc = launch_xquant(L->hs, f, Tsh, L->xtab_dn + (size_t)qrm::xtab_stride(f) * Tx * k, s);
                         nl++;
                     }
                 }
@@ -1237,21 +1301,22 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             if (rc) return rc;
             nl += 2;
         }
-        mark(gu ? 4 : 5);
+        mark(gu ? 4 : 5, gu ? 3 : 4);
     }
     if (ep && L->p2p) {
         // expert output rows straight into the owners' mailboxes; the owner
         // combines in slot order once every holder's rows are in
         const qrm::EpPeers pe = ep_peers(L);
-        const int nb = (int)std::min<long long>(((long long)T * k * d / 4 + 2047) / 2048, 32);
-        qrm::ep_push_outputs_kernel<<<G * nb, 256, 0, s>>>(L->y, L->inv_perm, L->idx_all, T, k, d, L->first_expert,
-                                                           L->n_local, pe);
+        // grid for the largest possible number of local assignments
+        const long long n4 = (long long)Tx * k * (d / 4);
+        const int pgrid = (int)std::max<long long>(1, std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 4));
+        qrm::ep_push_outputs_kernel<<<pgrid, 256, 0, s>>>(L->y, L->perm, L->offsets + E, T, k, d, pe);
         QRM_CUDA(cudaGetLastError());
+        mark(-1, 5);
         const long long m4 = (long long)T * (d / 4);
         const int grid = (int)std::min<long long>((m4 + 255) / 256, (long long)L->sm_count * 16);
         qrm::ep_combine_kernel<<<grid, 256, 0, s>>>((flags & QRM_ADD_RESIDUAL) ? x : nullptr, topk_w, topk_idx, L->yrecv,
-                                                    shared ? L->ys + (size_t)L->rank * T * d : nullptr, T, k, d,
-                                                    E / G, out,
+                                                    shared ? L->ys : nullptr, T, k, d, E / G, 0, out,
                                                     reinterpret_cast<const uint32_t*>(L->mbox + L->mb.out_flag),
                                                     L->ep_state, G, &L->sched->err);
         QRM_CUDA(cudaGetLastError());
@@ -1271,11 +1336,12 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             QRM_NCCL(ncclRecv(L->yrecv + q * blk, blk, ncclFloat32, q, L->comm, s));
         }
         QRM_NCCL(ncclGroupEnd());
+        mark(-1, 5);
         const long long m4 = (long long)T * (d / 4);
         grid = (int)std::min<long long>((m4 + 255) / 256, (long long)L->sm_count * 16);
         qrm::ep_combine_kernel<<<grid, 256, 0, s>>>((flags & QRM_ADD_RESIDUAL) ? x : nullptr, topk_w, topk_idx, L->yrecv,
-                                                    shared ? L->ys + (size_t)L->rank * T * d : nullptr, T, k, d,
-                                                    E / G, out, nullptr, nullptr, 0, nullptr);
+                                                    shared ? L->ys : nullptr, T, k, d, E / G, 1, out, nullptr, nullptr,
+                                                    0, nullptr);
         QRM_CUDA(cudaGetLastError());
         nl += 2;
         combined = true;
@@ -1289,7 +1355,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         QRM_CUDA(launch_k(!prof && (L->pdl & 4), qrm::combine_kernel, dim3(cgrid), dim3(256), 0, s, cp));
         nl++;
     }
-    mark(6);
+    mark(6, 6);
     L->last_T = T;
     L->last_launches = nl;
     L->profiled_last = prof;
@@ -1455,8 +1521,19 @@ extern "C" int qrm_set_profiling(qrm_layer* L, int on) {
     return QRM_OK;
 }
 
+extern "C" int qrm_last_profile_ep(qrm_layer* L, float* ms) {
+    if (!L || !ms) return fail(QRM_E_INVALID, "NULL argument");
+    if (L->world < 2) return fail(QRM_E_STATE, "not an expert-parallel layer (use qrm_last_profile)");
+    if (!L->last_T || !L->profiled_last) return fail(QRM_E_STATE, "the last forward ran without profiling");
+    QRM_CUDA(cudaSetDevice(L->desc.device));
+    QRM_CUDA(cudaEventSynchronize(L->ev[QRM_EP_STAGE_COUNT]));
+    for (int i = 0; i < QRM_EP_STAGE_COUNT; i++) QRM_CUDA(cudaEventElapsedTime(&ms[i], L->ev[i], L->ev[i + 1]));
+    return QRM_OK;
+}
+
 extern "C" int qrm_last_profile(qrm_layer* L, float* ms, double* bytes) {
     if (!L) return fail(QRM_E_INVALID, "NULL layer");
+    if (L->world > 1) return fail(QRM_E_STATE, "expert-parallel layer: use qrm_last_profile_ep");
     if (!L->last_T || !L->profiled_last) return fail(QRM_E_STATE, "the last forward ran without profiling");
     QRM_CUDA(cudaSetDevice(L->desc.device));
     QRM_CUDA(cudaEventSynchronize(L->ev[QRM_STAGE_COUNT]));
@@ -1579,6 +1656,7 @@ extern "C" int qrm_matrix_gemv(qrm_matrix* M, const float* x_dev, int T, float* 
     gp.out_routed = y_dev;
     gp.out_shared = y_dev;
     gp.T = T;
+    gp.T_sh = T;
     gp.k = 1;
     gp.E = 0;
     gp.rows = M->mat.rows;
@@ -1658,6 +1736,7 @@ extern "C" int qrm_matrix_gemv_static(qrm_matrix* M, const float* x_dev, int T, 
     gp.out_routed = y_dev;
     gp.out_shared = y_dev;
     gp.T = T;
+    gp.T_sh = T;
     gp.k = 1;
     gp.E = 0;
     gp.rows = M->mat.rows;

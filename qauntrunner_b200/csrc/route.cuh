@@ -468,6 +468,8 @@ struct DispatchParams {
     const uint32_t* ep_flags; // [ep_G] or null
     uint32_t* ep_epoch;
     int ep_G;
+    int T_sh;                 // tokens of the shared expert's slot
+    int local_only;           // assignments outside the local window are dropped (not an error)
 };
 
 constexpr int kDispatchThreads = 1024;
@@ -508,10 +510,11 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
     }
     for (int e = tid; e <= E; e += kDispatchThreads) cnt[e] = 0;
     __syncthreads();
+    const int lo = p.local_only ? p.first_expert : 0, hi = p.local_only ? p.first_expert + p.n_local : E;
     for (int a = tid; a < n; a += kDispatchThreads) {
         int e = p.topk_idx[a];
-        if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
-        else atomicOr(&p.sched->err, (int)ERR_BOUNDS);
+        if (e >= lo && e < hi) atomicAdd(&cnt[e], 1);
+        else if (e < 0 || e >= E) atomicOr(&p.sched->err, (int)ERR_BOUNDS);
     }
     __syncthreads();
     // exclusive scans of the counts and of the "active local expert" flags:
@@ -563,7 +566,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
     for (int r0 = 0; r0 < n; r0 += kDispatchThreads) {
         const int a = r0 + tid;
         int e = a < n ? p.topk_idx[a] : -1;
-        if (e >= E || e < 0) e = -1;
+        if (e >= hi || e < lo) e = -1;
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank_w = __popc(peers & ((1u << lane) - 1));
         const int leader = __ffs(peers) - 1;
@@ -590,7 +593,7 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
         const int e = p.active[sl], off = p.offsets[e];
         p.slot_info[sl] = make_int4(e, off, p.offsets[e + 1] - off, p.perm[off] / p.k);
     }
-    if (tid == 0 && p.has_shared) p.slot_info[na] = make_int4(E, 0, p.T, 0);
+    if (tid == 0 && p.has_shared) p.slot_info[na] = make_int4(E, 0, p.T_sh, 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -694,6 +697,11 @@ struct RouteFusedParams {
     const float* router_lm;    // [E][8][P] lane-major router rows
     TopkParams tp;
     DispatchParams dp;
+    // matrices whose weights do not depend on the routing (the shared
+    // expert's), prefetched into L2 while the router runs; n_pf = 0: none
+    const uint8_t* pf_ptr[3];
+    long long pf_bytes[3];
+    int n_pf;
 };
 
 // order-preserving key of a ranking value: larger value -> larger key, NaN
@@ -871,7 +879,7 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
             const int nd = __popc(firsts);
             if (p.has_shared) {
                 p.active[nd] = E;
-                p.slot_info[nd] = make_int4(E, 0, p.T, 0);
+                p.slot_info[nd] = make_int4(E, 0, p.T_sh, 0);
             }
             p.sched->n_active = nd;
             for (int q = 0; q < 4; q++) p.sched->ctr[q] = 0;
@@ -921,6 +929,9 @@ route_fused_kernel(RouteFusedParams fp) {
         const uint32_t wb = (uint32_t)(sizeof(float) * P8);
         mbar_arrive_expect_tx(&bar[2], wb * ne);
         for (int e = 0; e < ne; e++) bulk_g2s(W + e * P8, fp.router_lm + (size_t)(e0 + e) * P8, wb, &bar[2]);
+        // HBM is otherwise idle during the chains: this CTA's share of the
+        // routing-independent weights into L2 for the expert stages
+        if (fp.n_pf > 0) prefetch_share(fp.pf_ptr, fp.pf_bytes, fp.n_pf);
     }
     // what the last CTA's ranking needs, staged while the chains run
     if (fp.tp.bias) {

@@ -41,12 +41,12 @@ int umma_encode_map(CUtensorMap* map, const void* base, long long rows, int K) {
     return (int)r;
 }
 
-cudaError_t umma_gather(const float* xn, const int32_t* pos_tok, int Tk, int shared_rows, int d, __half* out,
-                        int sm_count, cudaStream_t s) {
+cudaError_t umma_gather(const float* xn, const float* xn_shared, const int32_t* pos_tok, int Tk, int shared_rows, int d,
+                        __half* out, int sm_count, cudaStream_t s) {
     const long long n = (long long)(Tk + shared_rows) * (d / 8);
     if (n <= 0) return cudaSuccess;
     const int grid = (int)std::min<long long>((n + 255) / 256, (long long)sm_count * 8);
-    umma_gather_kernel<<<grid, 256, 0, s>>>(xn, pos_tok, Tk, shared_rows, d, out);
+    umma_gather_kernel<<<grid, 256, 0, s>>>(xn, xn_shared, pos_tok, Tk, shared_rows, d, out);
     return cudaGetLastError();
 }
 

@@ -664,16 +664,17 @@ expert_umma_kernel(const __grid_constant__ CUtensorMap act_map, UmmaParams p, in
 // ------------------------------------------------------------ helpers
 // f16 activation rows in dispatch order: row pos < T*k is token perm[pos] / k,
 // rows T*k + t (shared expert) are token t.
-__global__ void umma_gather_kernel(const float* __restrict__ xn, const int32_t* __restrict__ pos_tok, int Tk,
-                                   int shared_rows, int d, __half* __restrict__ out) {
+__global__ void umma_gather_kernel(const float* __restrict__ xn, const float* __restrict__ xn_shared,
+                                   const int32_t* __restrict__ pos_tok, int Tk, int shared_rows, int d,
+                                   __half* __restrict__ out) {
     const int rows = Tk + shared_rows;
     const int v8 = d / 8;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (long long)rows * v8;
          i += (long long)gridDim.x * blockDim.x) {
         const int row = (int)(i / v8), c = (int)(i - (long long)row * v8);
-        const int t = row < Tk ? pos_tok[row] : row - Tk;
-        const float4 a = __ldg(reinterpret_cast<const float4*>(xn + (size_t)t * d) + 2 * c);
-        const float4 b = __ldg(reinterpret_cast<const float4*>(xn + (size_t)t * d) + 2 * c + 1);
+        const float* src = row < Tk ? xn + (size_t)pos_tok[row] * d : xn_shared + (size_t)(row - Tk) * d;
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src) + 2 * c);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src) + 2 * c + 1);
         uint4 o;
         o.x = h2_bits(__floats2half2_rn(a.x, a.y));
         o.y = h2_bits(__floats2half2_rn(a.z, a.w));

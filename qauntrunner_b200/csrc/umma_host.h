@@ -22,10 +22,10 @@ bool umma_format(int fmt);
 // f16 [rows][K] row-major matrix at base as a TMA tensor map (boxes of 64
 // columns x 16 rows, 128-byte swizzle); 0 or a CUresult
 int umma_encode_map(CUtensorMap* map, const void* base, long long rows, int K);
-// f16 activation rows in dispatch order (routed rows from pos_tok, then
-// shared_rows token rows)
-cudaError_t umma_gather(const float* xn, const int32_t* pos_tok, int Tk, int shared_rows, int d, __half* out,
-                        int sm_count, cudaStream_t s);
+// f16 activation rows in dispatch order (routed rows: xn rows pos_tok[i],
+// then shared_rows rows of xn_shared)
+cudaError_t umma_gather(const float* xn, const float* xn_shared, const int32_t* pos_tok, int Tk, int shared_rows, int d,
+                        __half* out, int sm_count, cudaStream_t s);
 // SwiGLU outputs between the two paths: to_f16 = 1 copies the f32 rows of h
 // (routed, [Tk][f]) and hs (shared, [T][f]) into h16 [Tk + T][f]; 0 the reverse
 cudaError_t umma_convert_h(float* h, float* hs, int Tk, int shared_rows, int f, __half* h16, int to_f16, int sm_count,

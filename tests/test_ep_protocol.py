@@ -1,10 +1,12 @@
 """Expert-parallel exchange protocol on the CPU: world_size-2 gloo ranks run
-the message flow of the expert-parallel forward (qauntrunner_b200/csrc/ep.cuh,
-qrmoe.cu) with the oracle's arithmetic and must reproduce the single-process
-oracle forward bit for bit: each rank routes its own tokens, all-gathers
-(xn, top-k) records, computes its block of experts for every rank's tokens,
-returns output block q row t*k+j to token owner q, and the owner combines in
-slot order (residual, w_j y_j in slot order, shared expert)."""
+the message flow of the peer-memory expert-parallel forward
+(qauntrunner_b200/csrc/ep.cuh, qrmoe.cu) with the oracle's arithmetic and must
+reproduce the single-process oracle forward bit for bit: each rank routes its
+own tokens, sends every rank the top-k rows of all its tokens and the token
+rows only of tokens with an expert there, computes its experts for the
+assignments it holds, stores each output row at row t*k+j of the owner's one
+receive block, runs the shared expert for its own tokens, and the owner
+combines in slot order (residual, w_j y_j in slot order, shared expert)."""
 import os
 
 import numpy as np
@@ -54,37 +56,78 @@ def _rank(rank, port, q):
         x = x_all[rank * T:(rank + 1) * T]
         # 1. route this rank's tokens
         r = O.moe_forward(case, x, flags)
-        rec = np.concatenate([r["xn"], r["topk_idx"].view(np.float32), r["topk_w"]], axis=1)
-        # 2. all-gather the records
-        got = [torch.empty((T, d + 2 * k)) for _ in range(WORLD)]
-        dist.all_gather(got, torch.from_numpy(np.ascontiguousarray(rec)))
-        rec_all = torch.cat(got).numpy()
-        xn_all = rec_all[:, :d]
-        idx_all = np.ascontiguousarray(rec_all[:, d:d + k]).view(np.int32)
-        # 3. this rank's experts for every rank's tokens; block q, row t*k+j
-        send = np.zeros((WORLD, T * k, d), np.float32)
-        for a in range(WORLD * T * k):
-            t, j = divmod(a, k)
-            e = int(idx_all[t, j])
-            if first <= e < first + epr:
-                qq, tl = divmod(t, T)
-                send[qq, tl * k + j] = _expert(case, e, xn_all[t])
-        # shared expert for all gathered tokens (the same weights stream either way)
-        ys_all = np.stack([_expert(case, 0, xn_all[t], shared=True) for t in range(WORLD * T)]) if case.shared else None
-        # 4. blocks back to the owners (gathered; each rank keeps the blocks meant for it)
-        blocks = [torch.empty((WORLD, T * k, d)) for _ in range(WORLD)]
-        dist.all_gather(blocks, torch.from_numpy(send))
-        recv = np.stack([blocks[h].numpy()[rank] for h in range(WORLD)])   # [holder][T*k][d]
+        idx_own = np.ascontiguousarray(r["topk_idx"].astype(np.int32))
+        # 2. records to every rank q: the top-k rows of all T tokens; the token
+        #    rows only of tokens with an expert on q (all of them to itself).
+        #    Point-to-point messages stand in for the stores into q's mailbox.
+        owners = idx_own // epr                                   # [T][k] holder rank of each slot
+        xn_all = np.full((WORLD * T, d), np.nan, np.float32)      # rows never sent stay unread
+        idx_all = np.zeros((WORLD * T, k), np.int32)
+        reqs = []
+        for qq in range(WORLD):
+            rows = [t for t in range(T) if qq == rank or (owners[t] == qq).any()]
+            payload = np.zeros((T, d + k + 1), np.float32)
+            payload[:, d:d + k] = idx_own.view(np.float32)
+            for t in rows:
+                payload[t, :d] = r["xn"][t]
+                payload[t, d + k] = 1.0                           # "row sent" marker (for the check below)
+            if qq == rank:
+                mine = payload
+            else:
+                reqs.append(dist.isend(torch.from_numpy(payload), qq))
+        got = {rank: mine}
+        for qq in range(WORLD):
+            if qq != rank:
+                buf = torch.empty((T, d + k + 1))
+                dist.recv(buf, qq)
+                got[qq] = buf.numpy()
+        for rq in reqs:
+            rq.wait()
+        for p_ in range(WORLD):
+            pl = got[p_]
+            idx_all[p_ * T:(p_ + 1) * T] = np.ascontiguousarray(pl[:, d:d + k]).view(np.int32)
+            sent = pl[:, d + k] == 1.0
+            xn_all[p_ * T:(p_ + 1) * T][sent] = pl[sent, :d]
+        # 3. this rank's experts for the assignments it holds (gathered token
+        #    u = owner*T + t, slot j) -> owner's block row t*k + j
+        out_rows = {qq: {} for qq in range(WORLD)}
+        for u in range(WORLD * T):
+            qq, tl = divmod(u, T)
+            for j in range(k):
+                e = int(idx_all[u, j])
+                if first <= e < first + epr:
+                    assert not np.isnan(xn_all[u]).any(), "a needed token row was not sent"
+                    out_rows[qq][tl * k + j] = _expert(case, e, xn_all[u])
+        # the shared expert for this rank's own tokens only
+        ys = np.stack([_expert(case, 0, r["xn"][t], shared=True) for t in range(T)]) if case.shared else None
+        # 4. output rows to their owners: one [T*k][d] block per owner, each
+        #    row written by the one rank that holds the slot's expert
+        recv = np.full((T * k, d), np.nan, np.float32)
+        for rr, y in out_rows[rank].items():
+            recv[rr] = y
+        for step in range(1, WORLD):
+            dst, src = (rank + step) % WORLD, (rank - step) % WORLD
+            rows = sorted(out_rows[dst])
+            msg = np.zeros((T * k, d + 1), np.float32)
+            for rr in rows:
+                msg[rr, :d] = out_rows[dst][rr]
+                msg[rr, d] = 1.0
+            buf = torch.empty((T * k, d + 1))
+            sreq = dist.isend(torch.from_numpy(msg), dst)
+            dist.recv(buf, src)
+            sreq.wait()
+            b = buf.numpy()
+            for rr in np.nonzero(b[:, d] == 1.0)[0]:
+                recv[rr] = b[rr, :d]
         # 5. combine on the owner in slot order
         out = np.zeros((T, d), np.float32)
         for t in range(T):
             acc = x[t].astype(np.float32).copy()
             for j in range(k):
-                e = int(r["topk_idx"][t, j])
-                y = recv[e // epr, t * k + j]
+                y = recv[t * k + j]
                 acc = (acc + (np.float32(r["topk_w"][t, j]) * y).astype(np.float32)).astype(np.float32)
-            if ys_all is not None:
-                acc = (acc + (np.float32(1.0) * ys_all[rank * T + t]).astype(np.float32)).astype(np.float32)
+            if ys is not None:
+                acc = (acc + (np.float32(1.0) * ys[t]).astype(np.float32)).astype(np.float32)
             out[t] = acc
         ref = O.moe_forward(case, x_all, flags)
         q.put((rank, bool(np.array_equal(out, ref["out"][rank * T:(rank + 1) * T])),
