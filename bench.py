@@ -260,7 +260,7 @@ def cpu_sample(cfg_name, T, budget_s):
     return cpu_time(cpu_case(cfg_name), cfg_name, T, budget_s)
 
 
-def run_reference(args, rank, world):
+def run_reference(args, rank, world, out):
     if rank != 0:
         return 0
     cfg_name, T = args.config, args.tokens
@@ -279,7 +279,7 @@ def run_reference(args, rank, world):
                 config=dict(workload=NAMES[cfg_name], tokens_per_rank=T, parallelism="host threads"),
                 cpu_baseline=dict(value=val, unit="tokens/s", cores=threads, kind="port", sample=desc),
                 e2e=dict(value=val, unit="tokens/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
-    print(json.dumps(line), flush=True)
+    print(json.dumps(line), file=out, flush=True)
     return 0
 
 
@@ -571,7 +571,144 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
     return line
 
 
+def run_stack(args, cfg_name, T, torch, Q):
+    """One step = T tokens through args.layers MoE layers of the config on a
+    device-resident residual stream (qrm_stack): BASELINE config 2 is a
+    32-layer Mixtral-8x7B-shaped stack.  --hbm-budget-gb below the stack's
+    expert bytes keeps only the first layers resident and streams the others
+    from pinned host memory."""
+    from tests.synth_layer import SEED_BASE, SynthLayer
+    dev = 0
+    cfg = CONFIGS[cfg_name]
+    d, E, f = cfg["d_model"], cfg["n_experts"], cfg["expert_ffn"]
+    nL = args.layers
+    specs = [SynthLayer(cfg_name, seed=SEED_BASE + int(cfg_name[1:]) * 0x100 + 0x10000 * l) for l in range(nL)]
+    sp0 = specs[0]
+    t0 = time.perf_counter()
+    budget = int(args.hbm_budget_gb * (1 << 30))
+    S = Q.MoeStack(nL, d, E, cfg["n_active"], f, hbm_budget=budget, moe_sigmoid=bool(cfg["moe_sigmoid"]),
+                   routed_scale=cfg["routed_scale"], n_shared=cfg["n_shared"], swiglu_limit=cfg["swiglu_limit"],
+                   rms_eps=cfg["rms_eps"], fmt=sp0.fmt, shared_fmt=sp0.fmt_sh if sp0.shared else sp0.fmt,
+                   device=dev, max_tokens=T)
+    for sp, L in zip(specs, S.layers):
+        sp.upload_into(torch, Q, dev, L)
+    n_res, lbytes = S.info()
+    log(f"[rank 0] {cfg_name} stack of {nL} layers built in {time.perf_counter() - t0:.1f}s "
+        f"({n_res} resident, {nL - n_res} streamed, {lbytes / 1e9:.2f} GB per layer)")
+    flags = Q.APPLY_NORM | Q.ADD_RESIDUAL
+    nsteps = args.warmup + args.steps
+    nx = min(nsteps, max(2, (1 << 30) // max(1, T * d * 4)))
+    g = torch.Generator(device=f"cuda:{dev}")
+    g.manual_seed(sp0.seed + 17)
+    xs = torch.randn((nx, T, d), generator=g, device=f"cuda:{dev}", dtype=torch.float32)
+    out = torch.empty((T, d), dtype=torch.float32, device=f"cuda:{dev}")
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{dev}")
+    flush_rd = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=f"cuda:{dev}")
+    flush_out = torch.empty(1, dtype=torch.float32, device=f"cuda:{dev}")
+    stream = torch.cuda.Stream()
+    sp = stream.cuda_stream
+
+    def flush_l2(i):
+        flush.fill_(float(i))
+        torch.sum(flush_rd, dim=0, keepdim=True, out=flush_out)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            flush_l2(i)
+            S.forward_device(xs[i % nx].data_ptr(), T, out.data_ptr(), flags, sp)
+    torch.cuda.synchronize()
+    S.sync()
+    ev0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ev1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    try:
+        ident = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        ident = str(dev)
+    clocks = clock_sampler(ident)
+    clocks.start()
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            flush_l2(i)
+            ev0[i].record(stream)
+            S.forward_device(xs[(args.warmup + i) % nx].data_ptr(), T, out.data_ptr(), flags, sp)
+            ev1[i].record(stream)
+    torch.cuda.synchronize()
+    clock_info = clocks.stop()
+    S.sync()
+    total_ms = float(sum(ev0[i].elapsed_time(ev1[i]) for i in range(args.steps)))
+    launches = sum(L.last_launch_count() for L in S.layers)
+    # expert bytes the last step's batch selected, over all layers (+ routers)
+    ebytes = sum(Q.tensor_bytes(d * f, x) for x in sp0.fmt)
+    used = 0
+    for L in S.layers:
+        _, off = L.last_dispatch(T)
+        used += int(np.count_nonzero(np.diff(off)))
+    step_bytes = used * ebytes + nL * (E * d * 4 + 2 * T * d * 4)
+    # e2e: pinned host tokens in, the stack's output back, copies inside the events
+    xh = xs[:min(nx, nsteps)].cpu().pin_memory()
+    oh = torch.empty((T, d), dtype=torch.float32).pin_memory()
+    xd = torch.empty((T, d), dtype=torch.float32, device=f"cuda:{dev}")
+    e0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            flush_l2(i)
+            e0[i].record(stream)
+            xd.copy_(xh[i % xh.shape[0]], non_blocking=True)
+            S.forward_device(xd.data_ptr(), T, out.data_ptr(), flags, sp)
+            oh.copy_(out, non_blocking=True)
+            e1[i].record(stream)
+    torch.cuda.synchronize()
+    S.sync()
+    e2e_ms = float(sum(e0[i].elapsed_time(e1[i]) for i in range(args.steps)))
+    S.close()
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK["hbm_gbs"]))
+    step_s = total_ms / args.steps / 1000.0
+    ach = step_bytes / step_s / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        try:
+            # one token through one full-size layer, times the layer count
+            v, cores, desc = cpu_sample(cfg_name, 1, budget_s=12.0)
+            cpu = dict(value=v / nL, unit="tokens/s", cores=cores, kind="port",
+                       sample=desc + f"; tokens/s of one layer divided by the {nL} layers of the stack")
+        except Exception as ex:
+            cpu = dict(value=None, unit="tokens/s", cores=None, kind="port", sample=f"failed: {ex}")
+    streamed = nL - n_res
+    return dict(
+        metric=METRIC, value=args.steps * T / (total_ms / 1000.0), unit="tokens/s", n_gpus=1, steps=args.steps,
+        warmup=args.warmup, ms_per_step=total_ms / args.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
+        dtype="expert products: weight codes x 16-bit fixed-point activations (integer MMA, exact int32 sums, "
+              "f32 scales) or dequantised f16 x f16 (tensor MMA, f32 accumulate); routing and combine f32",
+        data="synthetic",
+        config=dict(workload=NAMES[cfg_name] + f"_stack{nL}", tokens_per_rank=T, layers=nL, resident_layers=n_res,
+                    streamed_layers=streamed, hbm_budget_gb=args.hbm_budget_gb or None, d_model=d, n_experts=E,
+                    top_k=cfg["n_active"], expert_ffn=f, formats=FORMATS[cfg_name],
+                    l2="flushed before every step outside the timed events: 256 MiB written, then another 256 MiB "
+                       "buffer read", parallelism="single GPU"),
+        roofline=dict(bound="hbm", kernel=f"whole {nL}-layer stack step (expert bytes the batch selected + routers)",
+                      achieved=ach, peak=hbm, unit="GB/s", frac=ach / hbm, peak_kind=f"{peak_kind} hbm_gbs",
+                      bytes_per_launch=step_bytes, traffic=None),
+        layer_hbm=dict(achieved_gbs=ach, frac_of_8tbs=ach / NOMINAL_HBM_GBS, frac_of_measured=ach / hbm,
+                       bytes_per_step=step_bytes),
+        h2d_stream=dict(bytes_per_step=streamed * lbytes, gbs=streamed * lbytes / step_s / 1e9) if streamed else None,
+        cpu_baseline=cpu,
+        e2e=dict(value=args.steps * T / (e2e_ms / 1000.0), unit="tokens/s", h2d_bytes_per_step=T * d * 4,
+                 d2h_bytes_per_step=T * d * 4, call="qrm_stack_forward_device, pinned host buffers, copies inside "
+                                                    "the events"),
+        parity=dict(note="per-layer parity and stack == chain of single layers: tests/test_gpu_stack.py"),
+        gpu_launches=launches * args.steps,
+        clocks=clock_info,
+    )
+
+
 def main():
+    # the JSON lines go to the original stdout; everything else written to
+    # fd 1 (NCCL's version banner, library prints) goes to stderr
+    out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -583,6 +720,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--experts", type=int, default=0, help="routed experts (a smaller case of the config)")
+    ap.add_argument("--layers", type=int, default=32, help="config c2: layers of the stack (1: one layer)")
+    ap.add_argument("--hbm-budget-gb", type=float, default=0.0,
+                    help="config c2 stack: expert bytes kept in HBM (0: all); the other layers stream from host")
     ap.add_argument("--flush", choices=["write", "write-read"], default="write-read",
                     help="L2 flush between steps: write a buffer larger than L2, then (write-read) read another")
     args = ap.parse_args()
@@ -591,7 +731,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
-        return run_reference(args, rank, world)
+        return run_reference(args, rank, world, out)
     import torch
     import qauntrunner_b200 as Q
     dist = None
@@ -604,9 +744,12 @@ def main():
     try:
         runs = SWEEP if args.sweep else [(args.config, args.tokens)]
         for cfg_name, T in runs:
-            line = run_one(args, cfg_name, T, rank, world, dist, torch, Q)
+            if cfg_name == "c2" and args.layers > 1 and world == 1:
+                line = run_stack(args, cfg_name, T, torch, Q)
+            else:
+                line = run_one(args, cfg_name, T, rank, world, dist, torch, Q)
             if line is not None:
-                print(json.dumps(line), flush=True)
+                print(json.dumps(line), file=out, flush=True)
         return 0
     finally:
         if dist:

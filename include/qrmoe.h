@@ -180,6 +180,32 @@ int qrm_last_profile(qrm_layer* layer, float* ms, double* bytes);
  * graph replay).  No counterpart in the reference. */
 int qrm_last_launch_count(qrm_layer* layer, int* count);
 
+/* ---- layer stack: n MoE layers of one shape on a device-resident residual
+ * stream (the MoE part of ForwardLegacy, StreamingEngine.cs:213-286: each
+ * layer x += MoeFfn(RmsNorm(x)), or what `flags` asks per layer) ----
+ * hbm_budget: bytes of expert weights the stack may keep in HBM (0 = no
+ * limit).  While every layer fits, all are resident.  Otherwise the first
+ * n_resident layers stay resident and the others are kept in pinned host
+ * memory and streamed into two device slots by layer parity, each copy
+ * overlapping the compute of the layer before (PrefetchPipeline's ping-pong
+ * staging, src/QuantRunner.Core/Runtime/PrefetchPipeline.cs:64-166; its
+ * over-budget fallback :131-135 becomes streaming from host memory).
+ * Uploads go through each layer (qrm_stack_layer + qrm_upload_*, or
+ * qrm_stack_load_qw for .qw file layers first_layer ... first_layer+n-1); a
+ * streamed layer's expert upload also fills its host image.  The stack owns
+ * its layers (do not qrm_destroy them).  qrm_stack_forward_device runs all
+ * layers on `stream` (NULL = layer 0's stream): x_dev [T x d] in, out_dev
+ * [T x d] out (may alias x_dev); asynchronous; qrm_stack_sync reports
+ * device-side errors. */
+typedef struct qrm_stack qrm_stack;
+int  qrm_stack_create(const qrm_layer_desc* desc, int n_layers, size_t hbm_budget, qrm_stack** out);
+void qrm_stack_destroy(qrm_stack* stack);
+int  qrm_stack_layer(qrm_stack* stack, int i, qrm_layer** layer);
+int  qrm_stack_info(qrm_stack* stack, int* n_resident, size_t* layer_bytes);
+int  qrm_stack_load_qw(qrm_stack* stack, const char* path, int first_layer);
+int  qrm_stack_forward_device(qrm_stack* stack, const float* x_dev, int T, int flags, float* out_dev, void* stream);
+int  qrm_stack_sync(qrm_stack* stack);
+
 /* ---- operator API: DotKernels.MatVecParallel / DotKernels.GEMM on the GPU ----
  * (DotKernels.cs:610-660).  A qrm_matrix holds one [rows x cols] matrix in
  * HBM; qrm_matrix_gemv computes y[t] = W x[t] for T tokens
@@ -189,6 +215,22 @@ int  qrm_matrix_create(int device, int fmt, int64_t rows, int64_t cols,
                        const void* bytes, size_t nbytes, qrm_matrix** out);
 void qrm_matrix_destroy(qrm_matrix* m);
 int  qrm_matrix_gemv(qrm_matrix* m, const float* x_dev, int T, float* y_dev, void* stream);
+
+/* ---- dense FFN: StreamingEngine.DenseFfn / DenseFfnOut
+ * (src/QuantRunner.Core/Runtime/StreamingEngine.cs:599-622), the FFN of the
+ * dense layers of a MoE model (first_k_dense_replace, :633-637), from three
+ * matrix operators ----
+ * gate, up: [f x d]; down: [d x f], all on one device (the qrm_ffn refers to
+ * them; destroy it before them).  qrm_ffn_forward computes, for T <=
+ * max_tokens tokens, out = x + W_down SwiGLU(W_gate xn, W_up xn) (DenseFfn,
+ * x_dev given) or out = W_down SwiGLU(...) (DenseFfnOut, x_dev NULL), with
+ * Glm5Ops.LimitedSwiglu's clamp when swiglu_limit > 0; asynchronous on
+ * `stream`.  out_dev may alias x_dev (the engine adds into x in place). */
+typedef struct qrm_ffn qrm_ffn;
+int  qrm_ffn_create(qrm_matrix* gate, qrm_matrix* up, qrm_matrix* down, int max_tokens, qrm_ffn** out);
+void qrm_ffn_destroy(qrm_ffn* ffn);
+int  qrm_ffn_forward(qrm_ffn* ffn, const float* xn_dev, const float* x_dev, int T, float swiglu_limit,
+                     float* out_dev, void* stream);
 
 /* qrm_matrix_gemv without any device allocation.  No counterpart in the
  * reference.  qrm_matrix_gemv grows the matrix's activation-table buffer when
@@ -226,7 +268,8 @@ int  qrm_matrix_gemv_static(qrm_matrix* m, const float* x_dev, int T, float* y_d
  * when every rank can map every other rank's memory, else NCCL all-gather and
  * grouped send/recv of fixed-size blocks (QRM_EP_P2P=0 in the environment
  * forces NCCL); a peer
- * that does not deliver within about a second makes qrm_sync return
+ * that does not deliver within the wait limit (2 s, or QRM_WAIT_LIMIT_US
+ * microseconds in the environment when a layer is created) makes qrm_sync return
  * QRM_E_TIMEOUT, after which the layer should be destroyed.  The id comes
  * from qrm_nccl_unique_id on one rank and is passed to every rank by the host
  * (128 bytes); qrm_create_ep returns once all ranks have joined, and
@@ -252,6 +295,19 @@ int qrm_ep_transport(qrm_layer* layer, int* transport);
 enum { QRM_EP_STAGE_ROUTE = 0, QRM_EP_STAGE_RECORDS, QRM_EP_STAGE_GATEUP, QRM_EP_STAGE_DOWN, QRM_EP_STAGE_OUTPUTS,
        QRM_EP_STAGE_COMBINE, QRM_EP_STAGE_COUNT };
 int qrm_last_profile_ep(qrm_layer* layer, float* ms);
+
+/* ---- self-tests (no counterpart in the reference; its `selftest` command
+ * checks the CPU kernels, src/QuantRunner.Cli/Commands.cs:2257-2325) ----
+ * qrm_selftest_expf writes the bits of the routing kernels' binary32 exp of
+ * the floats with bit patterns first .. first+count-1 (wrapping) to out_dev
+ * [count] (asynchronous on `stream`), for comparison with the C runtime's
+ * expf that the reference's MathF.Exp calls.
+ * qrm_selftest_waits runs the library's bounded waits on an mbarrier nothing
+ * arrives at and on a peer flag nothing raises, with a limit of limit_us
+ * (1 us .. 10 s) on `device`; it returns QRM_E_TIMEOUT when they gave up (the
+ * expected outcome; gave_up[2] says which did), and the device stays usable. */
+int qrm_selftest_expf(uint32_t first, uint32_t count, uint32_t* out_dev, void* stream);
+int qrm_selftest_waits(int device, int64_t limit_us, int* gave_up);
 
 /* ---- synthetic weights on the device (the reference's `synthesize`,
  * src/QuantRunner.Cli/Program.cs:247-369) ----

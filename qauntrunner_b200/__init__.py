@@ -107,11 +107,23 @@ _SIGS = {
     "qrm_matrix_destroy": (None, [P]),
     "qrm_matrix_gemv": (C.c_int, [P, P, C.c_int, P, P]),
     "qrm_matrix_gemv_static": (C.c_int, [P, P, C.c_int, P, P]),
+    "qrm_stack_create": (C.c_int, [C.POINTER(LayerDesc), C.c_int, C.c_size_t, C.POINTER(P)]),
+    "qrm_stack_destroy": (None, [P]),
+    "qrm_stack_layer": (C.c_int, [P, C.c_int, C.POINTER(P)]),
+    "qrm_stack_info": (C.c_int, [P, P, P]),
+    "qrm_stack_load_qw": (C.c_int, [P, C.c_char_p, C.c_int]),
+    "qrm_stack_forward_device": (C.c_int, [P, P, C.c_int, C.c_int, P, P]),
+    "qrm_stack_sync": (C.c_int, [P]),
+    "qrm_ffn_create": (C.c_int, [P, P, P, C.c_int, C.POINTER(P)]),
+    "qrm_ffn_destroy": (None, [P]),
+    "qrm_ffn_forward": (C.c_int, [P, P, P, C.c_int, C.c_float, P, P]),
     "qrm_nccl_unique_id": (C.c_int, [P]),
     "qrm_create_ep": (C.c_int, [C.POINTER(LayerDesc), C.c_int, C.c_int, P, C.POINTER(P)]),
     "qrm_expert_range": (C.c_int, [P, P, P]),
     "qrm_ep_transport": (C.c_int, [P, P]),
     "qrm_last_profile_ep": (C.c_int, [P, P]),
+    "qrm_selftest_expf": (C.c_int, [C.c_uint32, C.c_uint32, P, P]),
+    "qrm_selftest_waits": (C.c_int, [C.c_int, C.c_int64, P]),
     "qrm_synth_gaussian": (C.c_int, [P, C.c_int64, C.c_uint64, C.c_float, P]),
     "qrm_synth_quantize": (C.c_int, [C.c_int, P, C.c_int64, P, P]),
 }
@@ -239,7 +251,8 @@ class MoeLayer:
 
     def close(self):
         if getattr(self, "_h", None):
-            lib().qrm_destroy(self._h)
+            if not getattr(self, "_borrowed", False):   # a stack's layer belongs to the stack
+                lib().qrm_destroy(self._h)
             self._h = None
 
     def __del__(self):
@@ -359,6 +372,86 @@ class Matrix:
     def close(self):
         if getattr(self, "_h", None):
             lib().qrm_matrix_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class MoeStack:
+    """n MoE layers of one shape on a device-resident residual stream
+    (qrm_stack_*): the first n_resident layers' weights stay in HBM, the rest
+    stream from pinned host memory through two device slots when hbm_budget
+    (bytes, 0 = no limit) does not hold them all."""
+
+    def __init__(self, n_layers, d_model, n_experts, n_active, expert_ffn, hbm_budget=0, moe_sigmoid=False,
+                 routed_scale=1.0, n_shared=0, swiglu_limit=0.0, rms_eps=1e-5, fmt=(6, 6, 6), shared_fmt=None,
+                 device=0, max_tokens=1):
+        shared_fmt = shared_fmt or fmt
+        self.desc = LayerDesc(d_model, n_experts, n_active, expert_ffn, int(bool(moe_sigmoid)), routed_scale,
+                              n_shared, swiglu_limit, rms_eps, int(fmt[0]), int(fmt[1]), int(fmt[2]),
+                              int(shared_fmt[0]), int(shared_fmt[1]), int(shared_fmt[2]), device, max_tokens)
+        h = P()
+        _check(lib().qrm_stack_create(C.byref(self.desc), n_layers, int(hbm_budget), C.byref(h)))
+        self._h = h
+        self.n_layers = n_layers
+        self.layers = []
+        for i in range(n_layers):
+            lh = P()
+            _check(lib().qrm_stack_layer(h, i, C.byref(lh)))
+            L = MoeLayer.__new__(MoeLayer)
+            L._h, L._borrowed, L.desc, L.k, L.rank, L.world = lh, True, self.desc, min(n_active, 8), 0, 1
+            self.layers.append(L)
+
+    def info(self):
+        """(resident layers, expert bytes of one layer)."""
+        a, b = C.c_int(0), C.c_size_t(0)
+        _check(lib().qrm_stack_info(self._h, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+    def load_qw(self, path, first_layer=0):
+        _check(lib().qrm_stack_load_qw(self._h, os.fsencode(path), first_layer))
+
+    def forward_device(self, x_ptr, T, out_ptr, flags=APPLY_NORM | ADD_RESIDUAL, stream=None):
+        _check(lib().qrm_stack_forward_device(self._h, x_ptr, T, flags, out_ptr, stream))
+
+    def sync(self):
+        _check(lib().qrm_stack_sync(self._h))
+
+    def close(self):
+        for L in getattr(self, "layers", []):
+            L._h = None
+        if getattr(self, "_h", None):
+            lib().qrm_stack_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class DenseFfn:
+    """StreamingEngine.DenseFfn / DenseFfnOut (StreamingEngine.cs:599-622) on
+    the GPU from three Matrix objects (gate, up [f x d]; down [d x f])."""
+
+    def __init__(self, gate, up, down, max_tokens=1):
+        h = P()
+        _check(lib().qrm_ffn_create(gate._h, up._h, down._h, max_tokens, C.byref(h)))
+        self._h = h
+        self._mats = (gate, up, down)   # the FFN refers to them: keep them alive
+
+    def forward(self, xn_ptr, x_ptr, T, out_ptr, swiglu_limit=0.0, stream=None):
+        """out = x + W_down SwiGLU(W_gate xn, W_up xn) (x_ptr None: without x)."""
+        _check(lib().qrm_ffn_forward(self._h, xn_ptr, x_ptr, T, swiglu_limit, out_ptr, stream))
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().qrm_ffn_destroy(self._h)
             self._h = None
 
     def __del__(self):

@@ -49,6 +49,22 @@ struct MatDev {
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+// Limit of the waits that give up on a stage or a peer that does not deliver
+// (producers, consumers, peer flags): 2 s, or QRM_WAIT_LIMIT_US read at layer
+// creation.  One copy per translation unit and device; set_wait_limit_here
+// sets the calling unit's.  Drains of copies already in flight, which always
+// complete, keep a fixed limit.
+static __device__ uint64_t g_wait_limit_ns = 2000000000ull;
+__device__ __forceinline__ uint64_t wait_limit_ns() { return *reinterpret_cast<volatile uint64_t*>(&g_wait_limit_ns); }
+static inline cudaError_t set_wait_limit_here(uint64_t ns) {
+    return cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof ns);
+}
+
 // Programmatic dependent launch.  A kernel launched with programmatic stream
 // serialization may start while its predecessor still runs: pdl_wait() blocks
 // until the predecessor grid has completed and its writes are visible (a no-op

@@ -61,7 +61,6 @@ struct EpPeers {
     int G, rank;
 };
 
-constexpr long long kEpSpinLimit = 1ll << 22;   // polls; with the back-off below about 1-2 s
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
@@ -74,13 +73,15 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 }
 
 // Waits until *flag has reached `want` (epochs only grow; wrap-safe compare).
-// Returns false when the wait gave up.
+// Returns false when the wait gave up (after wait_limit_ns()).
 __device__ inline bool ep_wait_flag(const uint32_t* flag, uint32_t want) {
-    for (long long i = 0; i < kEpSpinLimit; i++) {
+    if ((int32_t)(ld_acquire_sys(flag) - want) >= 0) return true;
+    const uint64_t t0 = global_ns(), lim = wait_limit_ns();
+    for (int i = 0;; i++) {
         if ((int32_t)(ld_acquire_sys(flag) - want) >= 0) return true;
         if (i >= 256) __nanosleep(256);
+        if ((i & 63) == 63 && global_ns() - t0 > lim) return false;
     }
-    return false;
 }
 
 // The calling block's stores to rank q are complete: the last of the `nb`

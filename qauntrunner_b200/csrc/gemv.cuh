@@ -342,11 +342,6 @@ struct GemvParams {
     const float* xq_a;
     const float* xq_b;
     int xq_split;
-    // gate/up launches of the streaming kernel: once the ring is filled, the
-    // producers prefetch the down matrices of the active slots (and of the
-    // shared expert) into L2, each CTA its share, and mark the stage's own
-    // weight copies evict_first, so the down stage reads its weights from L2
-    int prefetch_down;
     // launched as a programmatic dependent: 1 = wait for the predecessor
     // before anything, 2 = the producer streams weights before the wait (the
     // routing it reads was final two launches earlier; only the activations

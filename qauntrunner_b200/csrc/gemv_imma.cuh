@@ -131,8 +131,8 @@ static __global__ void xquant_kernel(const float* __restrict__ src, int K, int r
 }
 
 // ------------------------------------------------------------ bounded waits
-// Every wait gives up after kWaitLimitNs or as soon as another warp of the CTA
-// has given up (abort flag), so no warp can wait forever on one that left.
+// Every wait gives up after wait_limit_ns() or as soon as another warp of the
+// CTA has given up (abort flag), so no warp can wait forever on one that left.
 // try_wait carries a suspend-time hint so a waiting warp sleeps instead of
 // taking issue slots from the warps that compute.
 constexpr uint32_t kSuspendHintNs = 20000;
@@ -147,12 +147,12 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
 }
 __device__ __forceinline__ bool mbar_wait_abort(uint64_t* bar, uint32_t parity, const volatile int* abort_flag) {
     if (mbar_try_wait_hint(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
+    const uint64_t t0 = global_ns(), lim = wait_limit_ns();
     for (;;) {
         for (int i = 0; i < 4; i++)
             if (mbar_try_wait_hint(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (global_ns() - t0 > kWaitLimitNs) return false;
+        if (global_ns() - t0 > lim) return false;
     }
 }
 // whole warp; false (for every lane) when any lane gave up
@@ -169,10 +169,10 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ bool warp_spin_eq(const volatile int* f, int v, volatile int* abort_flag, int32_t* err) {
     int ok = 1;
     if ((threadIdx.x & 31) == 0) {
-        const uint64_t t0 = global_ns();
+        const uint64_t t0 = global_ns(), lim = wait_limit_ns();
         while (*f != v) {
             __nanosleep(32);
-            if (*abort_flag || global_ns() - t0 > kWaitLimitNs) { ok = 0; break; }
+            if (*abort_flag || global_ns() - t0 > lim) { ok = 0; break; }
         }
         if (!ok) {
             *abort_flag = 1;

@@ -548,7 +548,7 @@ __device__ __forceinline__ void stream_stage(const GemvParams& p, const StreamCo
 // holds whole rows (the tiles are then consecutive in HBM).
 template <int M>
 __device__ __forceinline__ void stream_issue(const StreamSeg& g, const MatDev* md, int rg, int part, uint8_t* st,
-                                             uint64_t* bar, int lane, uint64_t pol) {
+                                             uint64_t* bar, int lane) {
     const int nsb = g.parts * g.sbs;
     const size_t run = (size_t)g.sbs * g.cb;
     if (g.parts == 1) {
@@ -558,8 +558,7 @@ __device__ __forceinline__ void stream_issue(const StreamSeg& g, const MatDev* m
             const MatDev mat = md[M == 2 ? c : 2];
             const int nt = M == 2 ? g.r16 : 2 * g.r16;           // 8-row tiles in the run
             const long long t0 = (long long)rg * nt;
-            if (pol) bulk_g2s_hint(st + (size_t)c * nt * run, mat.base + t0 * nsb * g.cb, (uint32_t)(nt * run), bar, pol);
-            else bulk_g2s(st + (size_t)c * nt * run, mat.base + t0 * nsb * g.cb, (uint32_t)(nt * run), bar);
+            bulk_g2s(st + (size_t)c * nt * run, mat.base + t0 * nsb * g.cb, (uint32_t)(nt * run), bar);
         }
         return;
     }
@@ -569,9 +568,8 @@ __device__ __forceinline__ void stream_issue(const StreamSeg& g, const MatDev* m
         if (M == 2) { m = c / g.r16; tile = rg * g.r16 + (c - m * g.r16); }
         else { m = 2; tile = rg * ntile + c; }
         const MatDev mat = md[m];
-        const uint8_t* src = mat.base + ((long long)tile * nsb + (long long)part * g.sbs) * g.cb;
-        if (pol) bulk_g2s_hint(st + (size_t)c * run, src, (uint32_t)run, bar, pol);
-        else bulk_g2s(st + (size_t)c * run, src, (uint32_t)run, bar);
+        bulk_g2s(st + (size_t)c * run, mat.base + ((long long)tile * nsb + (long long)part * g.sbs) * g.cb,
+                 (uint32_t)run, bar);
     }
 }
 
@@ -652,29 +650,7 @@ expert_stream_kernel(GemvParams p, StreamConfig cfg, int32_t* err) {
         };
         bool ok = true;
         int k = 0;   // stages issued
-        const uint64_t pol = (M == 2 && p.prefetch_down) ? l2_policy_evict_first() : 0ull;
-        bool prefetched = !(M == 2 && p.prefetch_down);
-        auto prefetch = [&]() {
-            // the down matrices of the active slots and of the shared expert,
-            // this CTA's share, once the first stages are on their way
-            prefetched = true;
-            if (lane != 0) return;
-            const int na = p.mode == 2 ? 0 : n_active;
-            const int ns = (p.has_shared && p.mode != 1) ? 1 : 0;
-            long long g = 0;
-            for (int i = 0; i < na + ns; i++) {
-                const int e = i < na ? (p.slot_info ? p.slot_info[i].x : p.active[i]) : p.E;
-                const MatDev m = p.mats[(size_t)e * 3 + 2];
-                int bs, bb;
-                if (!block_spec(m.fmt, &bs, &bb)) continue;
-                const long long b = (m.nb * bb) & ~15LL;
-                for (long long o = 0; o < b; o += kPrefetchPiece, g++)
-                    if (g % gridDim.x == blockIdx.x)
-                        bulk_prefetch_l2(m.base + o, (uint32_t)(b - o < (long long)kPrefetchPiece ? b - o : (long long)kPrefetchPiece));
-            }
-        };
         for (int idx = 0, item = blockIdx.x; ok; idx++, item += gridDim.x) {
-            if (!prefetched && k >= S) prefetch();
             if (item >= n_items) {
                 // end marker in the next stage
                 const int s = k % S;
@@ -727,12 +703,11 @@ expert_stream_kernel(GemvParams p, StreamConfig cfg, int32_t* err) {
                     }
                     __syncwarp();
                     uint8_t* st = data + (size_t)s * cfg.stage_bytes;
-                    stream_issue<M>(g, md, cur.rg, part, st, &full[s], lane, pol);
+                    stream_issue<M>(g, md, cur.rg, part, st, &full[s], lane);
                     k++;
                 }
             }
         }
-        if (!prefetched && ok) prefetch();   // fewer stages than the ring holds
         if (lane == 0) {
             if (!ok) {
                 *abort_flag = 1;

@@ -40,11 +40,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
 // Bounded wait: gives up (returns false) after kWaitLimitNs of wall time.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
@@ -63,38 +58,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-// The same copy with an L2 eviction-priority policy (createpolicy): data
-// read once, marked evict_first, leaves room in L2 for lines prefetched for a
-// later stage.
-__device__ __forceinline__ uint64_t l2_policy_evict_first() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
-}
-__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
-        : "memory");
-}
-// Asynchronous prefetch of [src, src + bytes) into L2 (16-byte aligned, size a
-// multiple of 16); nothing waits for it.
-__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-// This CTA's share of an L2 prefetch of n ranges (ptr[i], bytes[i]), cut into
-// pieces of kPrefetchPiece bytes dealt round-robin over the grid; one thread.
-constexpr uint32_t kPrefetchPiece = 64 * 1024;
-__device__ __forceinline__ void prefetch_share(const uint8_t* const* ptr, const long long* bytes, int n) {
-    long long g = 0;   // global piece index
-    for (int i = 0; i < n; i++) {
-        const long long b = bytes[i] & ~15LL;
-        for (long long o = 0; o < b; o += kPrefetchPiece, g++)
-            if (g % gridDim.x == blockIdx.x) bulk_prefetch_l2(ptr[i] + o, (uint32_t)(b - o < (long long)kPrefetchPiece ? b - o : (long long)kPrefetchPiece));
-    }
-}
-
 __device__ __forceinline__ void fence_barrier_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
 __device__ __forceinline__ void named_barrier(int id, int threads) {
     asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");

@@ -207,15 +207,6 @@ cudaError_t launch_k(bool pdl, void (*kern)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
-// L2 prefetch mask of new layers (qrm_layer::l2_prefetch).
-int l2_prefetch_default() {
-    if (const char* e = getenv("QRM_L2_PREFETCH")) return atoi(e) & 3;
-    return 3;
-}
-// largest prefetch of down matrices during gate/up: what fits in the 126 MB
-// L2 beside the lines the gate/up stream passes through
-constexpr double kPrefetchMaxBytes = 96.0 * 1024 * 1024;
-
 // The streaming integer kernel's launch shape for one matrix launch.
 struct StreamSel {
     int ntk = 1;
@@ -387,6 +378,9 @@ struct qrm_layer {
     cudaStream_t stream = nullptr;
     // weights
     uint8_t* slab = nullptr;
+    size_t slab_bytes = 0;
+    bool slab_owned = true;       // false: a slot of a qrm_stack (layer weights streamed into it)
+    uint8_t* image = nullptr;     // streamed layer: pinned host copy of its slab in device layout
     std::vector<qrm::MatDev> mats;      // (E+1)*3
     std::vector<size_t> mat_bytes;
     qrm::MatDev* mats_dev = nullptr;
@@ -419,10 +413,7 @@ struct qrm_layer {
     // on B200 (configs 1-5: from 4 tokens per expert, or 64 shared tokens)
     int umma_min_tpe = 4;
     int umma_min_shared = 64;
-    // L2 prefetch of weights ahead of the stage that reads them (mask): 1 the
-    // shared expert's during the router, 2 the down matrices during gate/up
-    // (QRM_L2_PREFETCH overrides, for measurements)
-    int l2_prefetch = l2_prefetch_default();
+
     __half* act16 = nullptr;      // [Tx*k + Tx][d] f16 gate/up inputs in dispatch order
     __half* h16 = nullptr;        // [Tx*k + Tx][f] f16 down inputs
     qrm::UmmaItem* umma_items = nullptr;   // [2][cap]: gate/up items, down items
@@ -507,6 +498,7 @@ static void free_layer(qrm_layer* L) {
     }
     // a peer that may still write into it keeps the mailbox (leaked, not freed)
     if (L->mbox && met) cudaFree(L->mbox);
+    if (!L->slab_owned) L->slab = nullptr;   // the stack's slot
     L->xn_all = nullptr;
     L->idx_all = nullptr;
     L->yrecv = nullptr;
@@ -586,7 +578,8 @@ extern "C" __attribute__((visibility("hidden"))) int qrm_set_error(int code, con
 }
 extern "C" const char* qrm_last_error(void) { return g_err.c_str(); }
 
-static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out);
+static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out,
+                        uint8_t* ext_slab = nullptr);
 
 extern "C" int qrm_create(const qrm_layer_desc* desc, qrm_layer** out) {
     return create_layer(desc, 0, 1, nullptr, out);
@@ -744,7 +737,8 @@ static int umma_setup(qrm_layer* L) {
     return QRM_OK;
 }
 
-static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out) {
+static int create_layer(const qrm_layer_desc* desc, int rank, int world, const void* nccl_id, qrm_layer** out,
+                        uint8_t* ext_slab) {
     if (!out) return fail(QRM_E_INVALID, "out is NULL");
     *out = nullptr;
     int rc = check_desc(desc);
@@ -758,6 +752,12 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
     QRM_CUDA(cudaGetDeviceProperties(&prop, desc->device));
     if (prop.major != 10) return fail(QRM_E_CUDA, "device %d is sm_%d%d; libqrmoe is built for sm_100a", desc->device, prop.major, prop.minor);
     QRM_CUDA(cudaSetDevice(desc->device));
+    // the give-up limit of the bounded waits on this device (both units)
+    if (const char* e = getenv("QRM_WAIT_LIMIT_US")) {
+        const uint64_t ns = (uint64_t)std::max(1LL, atoll(e)) * 1000ull;
+        QRM_CUDA(qrm::set_wait_limit_here(ns));
+        QRM_CUDA(qrm::umma_set_wait_limit(ns));
+    }
     qrm_layer* L = new qrm_layer();
     L->desc = *desc;
     L->k = std::min(desc->n_active, 8);
@@ -794,8 +794,13 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
             total += ((size_t)nb + 255) / 256 * 256;
         }
     }
-    if (cudaMalloc(&L->slab, total) != cudaSuccess)
+    L->slab_bytes = total;
+    if (ext_slab) {
+        L->slab = ext_slab;
+        L->slab_owned = false;
+    } else if (cudaMalloc(&L->slab, total) != cudaSuccess) {
         return bail(fail(QRM_E_NOMEM, "cannot allocate %zu bytes of expert weights", total));
+    }
     for (size_t i = 0; i < L->mats.size(); i++)
         if (L->mat_bytes[i]) L->mats[i].base = L->slab + off[i];
     if (cudaMalloc(&L->mats_dev, sizeof(qrm::MatDev) * L->mats.size()) != cudaSuccess ||
@@ -952,6 +957,8 @@ static int upload_common(qrm_layer* L, int expert, int which, int fmt, const voi
         QRM_CUDA(cudaGetLastError());
     }
     QRM_CUDA(cudaStreamSynchronize(L->stream));
+    // a streamed layer of a stack keeps its weights in a host image of its slab
+    if (L->image) QRM_CUDA(cudaMemcpy(L->image + (m.base - L->slab), m.base, L->mat_bytes[i], cudaMemcpyDeviceToHost));
     L->uploaded[i] = 1;
     return QRM_OK;
 }
@@ -973,19 +980,28 @@ extern "C" int qrm_download_expert(qrm_layer* L, int expert, int which, void* by
     const qrm::MatDev& m = L->mats[i];
     QRM_CUDA(cudaSetDevice(L->desc.device));
     const bool tiled = layer_tiled(m.fmt, L->desc.d_model, L->desc.expert_ffn, which != 2);
+    // a streamed layer's bytes are in its host image (its slot holds whichever
+    // layer ran last)
+    const uint8_t* img = L->image ? L->image + (m.base - L->slab) : nullptr;
     if (m.fmt == qrm::Q4_K && !tiled) {
-        QRM_CUDA(cudaMemcpy(bytes, m.base, nbytes, cudaMemcpyDeviceToHost));
+        if (img) memcpy(bytes, img, nbytes);
+        else QRM_CUDA(cudaMemcpy(bytes, m.base, nbytes, cudaMemcpyDeviceToHost));
         return QRM_OK;
     }
     uint8_t* tmp = nullptr;
-    QRM_CUDA(cudaMalloc(&tmp, nbytes));
+    QRM_CUDA(cudaMalloc(&tmp, 2 * nbytes));
+    const uint8_t* src = m.base;
+    if (img) {
+        cudaMemcpy(tmp + nbytes, img, nbytes, cudaMemcpyHostToDevice);
+        src = tmp + nbytes;
+    }
     int bs, bb;
     qrm::block_spec(m.fmt, &bs, &bb);
     if (tiled)
-        qrm::tile_relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, m.cols / 256, m.base, tmp,
+        qrm::tile_relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, m.cols / 256, src, tmp,
                                                                          (long long)(nbytes / bb), 0);
     else
-        qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, m.base, tmp, (long long)(nbytes / bb), 0);
+        qrm::relayout_kernel<<<L->sm_count * 8, 256, 0, L->stream>>>(m.fmt, bb, src, tmp, (long long)(nbytes / bb), 0);
     cudaError_t e1 = cudaStreamSynchronize(L->stream);
     cudaError_t e2 = cudaMemcpy(bytes, tmp, nbytes, cudaMemcpyDeviceToHost);
     cudaFree(tmp);
@@ -1050,14 +1066,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     if (T <= qrm::route_fused_max_tokens(d, E) && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
         // one launch: every CTA its experts' logits, the last CTA top-k + dispatch
         const int grid = (E + qrm::kRouteEPC - 1) / qrm::kRouteEPC;
-        qrm::RouteFusedParams fp{rp, L->router_lm, tp, dp, {}, {}, 0};
-        if (shared && (L->l2_prefetch & 1)) {
-            for (int w = 0; w < 3; w++) {
-                fp.pf_ptr[w] = L->mats[(size_t)E * 3 + w].base;
-                fp.pf_bytes[w] = (long long)L->mat_bytes[(size_t)E * 3 + w];
-            }
-            fp.n_pf = 3;
-        }
+        qrm::RouteFusedParams fp{rp, L->router_lm, tp, dp};
         nl++;
         qrm::route_fused_kernel<<<grid, qrm::kRouteThreads, qrm::route_fused_smem(d, T, E), s>>>(fp);
         QRM_CUDA(cudaGetLastError());
@@ -1228,14 +1237,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         const int fr = gu ? D.fmt_gate : D.fmt_down;
         const int fs = gu ? D.fmt_sh_gate : D.fmt_sh_down;
         gp.pdl = (!prof && (L->pdl & (gu ? 1 : 2))) ? (gu ? 1 : 2) : 0;   // profiling events sit between the launches
-        // down weights into L2 during gate/up when they fit beside the stream
-        // (decode batches): at most min(T*k, local experts) routed matrices
-        if (gu && (L->l2_prefetch & 2)) {
-            const size_t e0 = (size_t)L->first_expert * 3 + 2;
-            const double pf = (double)std::min(Tx * k, L->n_local) * L->mat_bytes[e0] +
-                              (shared ? (double)L->mat_bytes[(size_t)E * 3 + 2] : 0.0);
-            gp.prefetch_down = pf <= kPrefetchMaxBytes ? 1 : 0;
-        }
+
         // routed + shared expert in one integer-kernel launch when the pair of
         // formats has one
         StreamSel sp;
@@ -1562,6 +1564,174 @@ extern "C" int qrm_last_profile(qrm_layer* L, float* ms, double* bytes) {
     return QRM_OK;
 }
 
+// ---------------------------------------------------------------- layer stack
+// n MoE layers of one shape run back to back on a device-resident residual
+// stream (the MoE part of ForwardLegacy, StreamingEngine.cs:213-286: every
+// layer x += MoeFfn(RmsNorm(x))).  The first n_res layers keep their weights
+// in HBM; when the budget does not hold them all, the others keep theirs in
+// pinned host images (the slab bytes in device layout, captured at upload)
+// and are streamed through two device slots by layer parity, each copy on a
+// copy stream overlapping the compute of the layer before -- the GPU
+// counterpart of PrefetchPipeline's ping-pong staging (PrefetchPipeline.cs:
+// 64-166), whose over-budget fallback (:131-135) becomes "stream from host".
+struct qrm_stack {
+    qrm_layer_desc desc{};
+    int n = 0, n_res = 0;
+    std::vector<qrm_layer*> layers;
+    size_t slab_bytes = 0;
+    uint8_t* slot[2] = {};
+    std::vector<uint8_t*> images;      // [n - n_res] pinned host images
+    cudaStream_t copy = nullptr;
+    cudaEvent_t copied[2] = {}, freed[2] = {};
+    float* act[2] = {};                // residual stream between layers [max_tokens][d]
+};
+
+static void free_stack(qrm_stack* S) {
+    if (!S) return;
+    cudaSetDevice(S->desc.device);
+    cudaDeviceSynchronize();
+    for (qrm_layer* L : S->layers) free_layer(L);
+    for (uint8_t* p : S->images)
+        if (p) cudaFreeHost(p);
+    for (int i = 0; i < 2; i++) {
+        if (S->slot[i]) cudaFree(S->slot[i]);
+        if (S->act[i]) cudaFree(S->act[i]);
+        if (S->copied[i]) cudaEventDestroy(S->copied[i]);
+        if (S->freed[i]) cudaEventDestroy(S->freed[i]);
+    }
+    if (S->copy) cudaStreamDestroy(S->copy);
+    delete S;
+}
+
+extern "C" int qrm_stack_create(const qrm_layer_desc* desc, int n_layers, size_t hbm_budget, qrm_stack** out) {
+    if (!out) return fail(QRM_E_INVALID, "out is NULL");
+    *out = nullptr;
+    int rc = check_desc(desc);
+    if (rc) return rc;
+    if (n_layers <= 0) return fail(QRM_E_INVALID, "n_layers must be positive");
+    QRM_CUDA(cudaSetDevice(desc->device));
+    qrm_stack* S = new qrm_stack();
+    S->desc = *desc;
+    S->n = n_layers;
+    auto bail = [&](int code) { free_stack(S); return code; };
+    // layer 0 tells the slab size of every layer (one shape)
+    qrm_layer* L0 = nullptr;
+    if ((rc = create_layer(desc, 0, 1, nullptr, &L0))) return bail(rc);
+    S->layers.push_back(L0);
+    S->slab_bytes = L0->slab_bytes;
+    const size_t lb = S->slab_bytes;
+    if (hbm_budget == 0 || lb * (size_t)n_layers <= hbm_budget) {
+        S->n_res = n_layers;
+    } else {
+        // two slots for the streamed layers, the rest of the budget resident
+        S->n_res = hbm_budget >= 2 * lb ? (int)std::min<size_t>((hbm_budget - 2 * lb) / lb, n_layers) : 0;
+        S->n_res = std::max(S->n_res, 1);   // layer 0 exists already
+        if (S->n_res >= n_layers) S->n_res = n_layers;
+    }
+    const int ns = n_layers - S->n_res;
+    if (ns > 0) {
+        if (cudaMalloc(&S->slot[0], lb) != cudaSuccess || cudaMalloc(&S->slot[1], lb) != cudaSuccess)
+            return bail(fail(QRM_E_NOMEM, "stream slots (2 x %zu bytes)", lb));
+        if (cudaStreamCreateWithFlags(&S->copy, cudaStreamNonBlocking) != cudaSuccess)
+            return bail(fail(QRM_E_CUDA, "copy stream"));
+        for (int i = 0; i < 2; i++) {
+            if (cudaEventCreateWithFlags(&S->copied[i], cudaEventDisableTiming) != cudaSuccess ||
+                cudaEventCreateWithFlags(&S->freed[i], cudaEventDisableTiming) != cudaSuccess)
+                return bail(fail(QRM_E_CUDA, "events"));
+            QRM_CUDA(cudaEventRecord(S->freed[i], S->copy));
+        }
+    }
+    for (int l = 1; l < n_layers; l++) {
+        qrm_layer* L = nullptr;
+        const bool streamed = l >= S->n_res;
+        if ((rc = create_layer(desc, 0, 1, nullptr, &L, streamed ? S->slot[(l - S->n_res) & 1] : nullptr)))
+            return bail(rc);
+        S->layers.push_back(L);
+        if (streamed) {
+            uint8_t* img = nullptr;
+            if (cudaMallocHost(&img, lb) != cudaSuccess)
+                return bail(fail(QRM_E_NOMEM, "pinned host image of layer %d (%zu bytes)", l, lb));
+            memset(img, 0, lb);
+            S->images.push_back(img);
+            L->image = img;
+        }
+    }
+    for (int i = 0; i < 2; i++)
+        if (cudaMalloc(&S->act[i], sizeof(float) * (size_t)desc->max_tokens * desc->d_model) != cudaSuccess)
+            return bail(fail(QRM_E_NOMEM, "residual stream buffers"));
+    *out = S;
+    return QRM_OK;
+}
+
+extern "C" void qrm_stack_destroy(qrm_stack* S) { free_stack(S); }
+
+extern "C" int qrm_stack_layer(qrm_stack* S, int i, qrm_layer** layer) {
+    if (!S || !layer) return fail(QRM_E_INVALID, "NULL argument");
+    if (i < 0 || i >= S->n) return fail(QRM_E_INVALID, "layer %d of %d", i, S->n);
+    *layer = S->layers[i];
+    return QRM_OK;
+}
+
+extern "C" int qrm_stack_info(qrm_stack* S, int* n_resident, size_t* layer_bytes) {
+    if (!S) return fail(QRM_E_INVALID, "NULL stack");
+    if (n_resident) *n_resident = S->n_res;
+    if (layer_bytes) *layer_bytes = S->slab_bytes;
+    return QRM_OK;
+}
+
+extern "C" int qrm_stack_load_qw(qrm_stack* S, const char* path, int first_layer) {
+    if (!S) return fail(QRM_E_INVALID, "NULL stack");
+    for (int l = 0; l < S->n; l++) {
+        int rc = qrm_load_qw(S->layers[l], path, first_layer + l);
+        if (rc) return rc;
+    }
+    return QRM_OK;
+}
+
+extern "C" int qrm_stack_forward_device(qrm_stack* S, const float* x_dev, int T, int flags, float* out_dev,
+                                        void* stream) {
+    if (!S || !x_dev || !out_dev) return fail(QRM_E_INVALID, "NULL argument");
+    if (T <= 0 || T > S->desc.max_tokens) return fail(QRM_E_CAPACITY, "T = %d outside 1..%d", T, S->desc.max_tokens);
+    QRM_CUDA(cudaSetDevice(S->desc.device));
+    cudaStream_t s = stream ? (cudaStream_t)stream : S->layers[0]->stream;
+    const int ns = S->n - S->n_res;
+    // the first two streamed layers' weights go into their slots as soon as
+    // the layers that used the slots in the previous forward are done
+    auto issue = [&](int j) -> int {   // streamed layer j (layer n_res + j) into slot j & 1
+        const int sl = j & 1;
+        QRM_CUDA(cudaStreamWaitEvent(S->copy, S->freed[sl], 0));
+        QRM_CUDA(cudaMemcpyAsync(S->slot[sl], S->images[j], S->slab_bytes, cudaMemcpyHostToDevice, S->copy));
+        QRM_CUDA(cudaEventRecord(S->copied[sl], S->copy));
+        return QRM_OK;
+    };
+    int rc;
+    for (int j = 0; j < std::min(ns, 2); j++)
+        if ((rc = issue(j))) return rc;
+    const float* cur = x_dev;
+    for (int l = 0; l < S->n; l++) {
+        float* dst = l == S->n - 1 ? out_dev : S->act[l & 1];
+        const int j = l - S->n_res;
+        if (j >= 0) QRM_CUDA(cudaStreamWaitEvent(s, S->copied[j & 1], 0));
+        rc = qrm_forward_device(S->layers[l], cur, T, flags, dst, nullptr, nullptr, s);
+        if (rc) return rc;
+        if (j >= 0) {
+            QRM_CUDA(cudaEventRecord(S->freed[j & 1], s));
+            if (j + 2 < ns && (rc = issue(j + 2))) return rc;
+        }
+        cur = dst;
+    }
+    return QRM_OK;
+}
+
+extern "C" int qrm_stack_sync(qrm_stack* S) {
+    if (!S) return fail(QRM_E_INVALID, "NULL stack");
+    for (qrm_layer* L : S->layers) {
+        int rc = qrm_sync(L);
+        if (rc) return rc;
+    }
+    return QRM_OK;
+}
+
 // ---------------------------------------------------------------- matrix operator
 
 struct qrm_matrix {
@@ -1686,6 +1856,92 @@ extern "C" int qrm_matrix_gemv(qrm_matrix* M, const float* x_dev, int T, float* 
     return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, M->misc + 5, s);
 }
 
+// ---------------------------------------------------------------- dense FFN
+// StreamingEngine.DenseFfn / DenseFfnOut (StreamingEngine.cs:599-622) from
+// three matrix operators: g = W_gate xn, u = W_up xn, h = SwiGLU(g, u),
+// y = W_down h, out = x + y (AxpyF32 with alpha 1) or out = y.
+struct qrm_ffn {
+    qrm_matrix* m[3] = {};
+    int device = 0, d = 0, f = 0, max_tokens = 0, sm_count = 0;
+    float *g = nullptr, *u = nullptr, *y = nullptr;
+};
+
+namespace qrm {
+// h = SwiGLU(g, u) in place of g (Glm5Ops.LimitedSwiglu / SiluMulInPlace)
+__global__ void ffn_swiglu_kernel(float* __restrict__ g, const float* __restrict__ u, long long n, float limit) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        g[i] = swiglu(g[i], u[i], limit);
+}
+// out = x + 1 * y (SimdMath.AxpyF32, alpha 1: the product is exact) or y
+__global__ void ffn_residual_kernel(const float* __restrict__ x, const float* __restrict__ y, float* __restrict__ out,
+                                    long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = x ? __fadd_rn(x[i], y[i]) : y[i];
+}
+}  // namespace qrm
+
+extern "C" int qrm_ffn_create(qrm_matrix* gate, qrm_matrix* up, qrm_matrix* down, int max_tokens, qrm_ffn** out) {
+    if (!out || !gate || !up || !down) return fail(QRM_E_INVALID, "NULL argument");
+    *out = nullptr;
+    if (max_tokens <= 0) return fail(QRM_E_INVALID, "max_tokens must be positive");
+    if (gate->device != up->device || gate->device != down->device)
+        return fail(QRM_E_INVALID, "the three matrices are on different devices");
+    const int f = gate->mat.rows, d = gate->mat.cols;
+    if (up->mat.rows != f || up->mat.cols != d || down->mat.rows != d || down->mat.cols != f)
+        return fail(QRM_E_INVALID, "shapes gate %dx%d, up %dx%d, down %dx%d do not form an FFN", gate->mat.rows,
+                    gate->mat.cols, up->mat.rows, up->mat.cols, down->mat.rows, down->mat.cols);
+    QRM_CUDA(cudaSetDevice(gate->device));
+    qrm_ffn* F = new qrm_ffn();
+    F->m[0] = gate;
+    F->m[1] = up;
+    F->m[2] = down;
+    F->device = gate->device;
+    F->d = d;
+    F->f = f;
+    F->max_tokens = max_tokens;
+    F->sm_count = gate->sm_count;
+    if (cudaMalloc(&F->g, sizeof(float) * (size_t)max_tokens * f) != cudaSuccess ||
+        cudaMalloc(&F->u, sizeof(float) * (size_t)max_tokens * f) != cudaSuccess ||
+        cudaMalloc(&F->y, sizeof(float) * (size_t)max_tokens * d) != cudaSuccess) {
+        if (F->g) cudaFree(F->g);
+        if (F->u) cudaFree(F->u);
+        delete F;
+        return fail(QRM_E_NOMEM, "FFN work buffers");
+    }
+    *out = F;
+    return QRM_OK;
+}
+
+extern "C" void qrm_ffn_destroy(qrm_ffn* F) {
+    if (!F) return;
+    cudaSetDevice(F->device);
+    cudaDeviceSynchronize();
+    cudaFree(F->g);
+    cudaFree(F->u);
+    cudaFree(F->y);
+    delete F;
+}
+
+extern "C" int qrm_ffn_forward(qrm_ffn* F, const float* xn_dev, const float* x_dev, int T, float swiglu_limit,
+                               float* out_dev, void* stream) {
+    if (!F || !xn_dev || !out_dev) return fail(QRM_E_INVALID, "NULL argument");
+    if (T <= 0 || T > F->max_tokens) return fail(QRM_E_CAPACITY, "T = %d outside 1..%d", T, F->max_tokens);
+    QRM_CUDA(cudaSetDevice(F->device));
+    cudaStream_t s = (cudaStream_t)stream;
+    int rc;
+    if ((rc = qrm_matrix_gemv(F->m[0], xn_dev, T, F->g, stream))) return rc;
+    if ((rc = qrm_matrix_gemv(F->m[1], xn_dev, T, F->u, stream))) return rc;
+    const long long nf = (long long)T * F->f, nd = (long long)T * F->d;
+    qrm::ffn_swiglu_kernel<<<(int)std::min<long long>((nf + 255) / 256, (long long)F->sm_count * 8), 256, 0, s>>>(
+        F->g, F->u, nf, swiglu_limit);
+    QRM_CUDA(cudaGetLastError());
+    if ((rc = qrm_matrix_gemv(F->m[2], F->g, T, F->y, stream))) return rc;
+    qrm::ffn_residual_kernel<<<(int)std::min<long long>((nd + 255) / 256, (long long)F->sm_count * 8), 256, 0, s>>>(
+        x_dev, F->y, out_dev, nd);
+    QRM_CUDA(cudaGetLastError());
+    return QRM_OK;
+}
+
 // ---------------------------------------------------------------- matrix operator, no allocation
 // qrm_matrix_gemv_static keeps the activation tables of the integer
 // tensor-core kernel in this fixed device array (one copy per device, shared
@@ -1755,6 +2011,74 @@ extern "C" int qrm_matrix_gemv_static(qrm_matrix* M, const float* x_dev, int T, 
         gp.xtab_rows = T;
     }
     return launch_gemv(M->mat.fmt, false, pick_nt(T), gp, M->sm_count, M->misc + 5, s);
+}
+
+// ---------------------------------------------------------------- self-tests
+namespace qrm {
+// the binary32 exp of the routing kernels on consecutive bit patterns
+__global__ void selftest_expf_kernel(uint32_t first, uint32_t count, uint32_t* __restrict__ out) {
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < count; i += gridDim.x * blockDim.x)
+        out[i] = __float_as_uint(expf_glibc(__uint_as_float(first + i)));
+}
+// the library's give-up waits on things nothing completes: warp 0 on an
+// mbarrier nothing arrives at (the expert kernels' stage wait), warp 1 on a
+// peer flag nothing raises (the expert-parallel wait); each records whether
+// it gave up
+__global__ void selftest_waits_kernel(const uint32_t* flag, int32_t* err, int32_t* gave_up) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == 0) {
+        const bool ok = mbar_wait_abort(&bar, 0u, &abort_flag);
+        if (lane == 0) {
+            gave_up[0] = ok ? 0 : 1;
+            if (!ok) atomicOr(err, (int)ERR_TIMEOUT);
+        }
+    } else if (warp == 1 && lane == 0) {
+        const bool ok = ep_wait_flag(flag, 1u);
+        gave_up[1] = ok ? 0 : 1;
+        if (!ok) atomicOr(err, (int)ERR_TIMEOUT);
+    }
+}
+}  // namespace qrm
+
+extern "C" int qrm_selftest_expf(uint32_t first, uint32_t count, uint32_t* out_dev, void* stream) {
+    if (!out_dev) return fail(QRM_E_INVALID, "NULL argument");
+    if (!count) return QRM_OK;
+    qrm::selftest_expf_kernel<<<1184, 256, 0, (cudaStream_t)stream>>>(first, count, out_dev);
+    QRM_CUDA(cudaGetLastError());
+    return QRM_OK;
+}
+
+extern "C" int qrm_selftest_waits(int device, int64_t limit_us, int* gave_up) {
+    if (limit_us <= 0 || limit_us > 10000000) return fail(QRM_E_INVALID, "limit %lld us outside 1 us .. 10 s", (long long)limit_us);
+    QRM_CUDA(cudaSetDevice(device));
+    int32_t* buf = nullptr;   // flag | err | gave_up[2]
+    QRM_CUDA(cudaMalloc(&buf, 4 * sizeof(int32_t)));
+    QRM_CUDA(cudaMemset(buf, 0, 4 * sizeof(int32_t)));
+    uint64_t old = 0;
+    cudaMemcpyFromSymbol(&old, qrm::g_wait_limit_ns, sizeof old);
+    QRM_CUDA(qrm::set_wait_limit_here((uint64_t)limit_us * 1000ull));
+    qrm::selftest_waits_kernel<<<1, 64>>>(reinterpret_cast<const uint32_t*>(buf), buf + 1, buf + 2);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    int32_t h[4] = {};
+    if (e == cudaSuccess) e = cudaMemcpy(h, buf, sizeof h, cudaMemcpyDeviceToHost);
+    qrm::set_wait_limit_here(old);
+    cudaFree(buf);
+    if (e != cudaSuccess) return fail(QRM_E_CUDA, "wait self-test: %s", cudaGetErrorString(e));
+    if (gave_up) {
+        gave_up[0] = h[2];
+        gave_up[1] = h[3];
+    }
+    return (h[1] & qrm::ERR_TIMEOUT) ? fail(QRM_E_TIMEOUT, "bounded waits gave up after %lld us", (long long)limit_us)
+                                     : QRM_OK;
 }
 
 // ---------------------------------------------------------------- synthetic data

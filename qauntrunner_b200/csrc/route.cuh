@@ -697,11 +697,6 @@ struct RouteFusedParams {
     const float* router_lm;    // [E][8][P] lane-major router rows
     TopkParams tp;
     DispatchParams dp;
-    // matrices whose weights do not depend on the routing (the shared
-    // expert's), prefetched into L2 while the router runs; n_pf = 0: none
-    const uint8_t* pf_ptr[3];
-    long long pf_bytes[3];
-    int n_pf;
 };
 
 // order-preserving key of a ranking value: larger value -> larger key, NaN
@@ -929,9 +924,6 @@ route_fused_kernel(RouteFusedParams fp) {
         const uint32_t wb = (uint32_t)(sizeof(float) * P8);
         mbar_arrive_expect_tx(&bar[2], wb * ne);
         for (int e = 0; e < ne; e++) bulk_g2s(W + e * P8, fp.router_lm + (size_t)(e0 + e) * P8, wb, &bar[2]);
-        // HBM is otherwise idle during the chains: this CTA's share of the
-        // routing-independent weights into L2 for the expert stages
-        if (fp.n_pf > 0) prefetch_share(fp.pf_ptr, fp.pf_bytes, fp.n_pf);
     }
     // what the last CTA's ranking needs, staged while the chains run
     if (fp.tp.bias) {

@@ -12,6 +12,8 @@ namespace qrm {
 
 static_assert(sizeof(UmmaItem) == kUmmaItemBytes, "work item size");
 
+cudaError_t umma_set_wait_limit(uint64_t ns) { return set_wait_limit_here(ns); }
+
 bool umma_format(int fmt) { return fmt == Q4_K || fmt == Q8_0 || fmt == Q4_0 || fmt == Q6_K || fmt == TRI; }
 
 // cuTensorMapEncodeTiled from the driver (no link-time dependency on libcuda)
@@ -93,7 +95,11 @@ long long umma_item_cap(int n_local, long long Tk, long long T, int rb_gateup, i
 
 template <int FA, int FB, bool GU>
 static cudaError_t launch_t(const CUtensorMap& map, const UmmaParams& p, int grid, cudaStream_t s) {
-    const UmmaSmem sm = umma_smem(FA, FB);
+    static const int raw_min = [] {
+        const char* e = getenv("QRM_UMMA_RAW_MIN");   // ring split for tuning runs
+        return e ? std::max(2, std::min(6, atoi(e))) : 0;
+    }();
+    const UmmaSmem sm = umma_smem(FA, FB, raw_min);
     // one CTA per SM (it holds all of tensor memory): more than half the shared memory
     if (sm.total <= 114 * 1024 || sm.raw_stages < 2 || sm.b_stages < 2) return cudaErrorInvalidConfiguration;
     static bool attr = false;

@@ -17,6 +17,8 @@ struct UmmaItem {
     int n;        // tokens (1..256)
 };
 
+// the grouped kernel's wait limit on the current device (QRM_WAIT_LIMIT_US)
+cudaError_t umma_set_wait_limit(uint64_t ns);
 // true when matrices of format fmt in the tiled layout can take the path
 bool umma_format(int fmt);
 // f16 [rows][K] row-major matrix at base as a TMA tensor map (boxes of 64

@@ -107,6 +107,12 @@ class SynthLayer:
                        swiglu_limit=c["swiglu_limit"], rms_eps=c["rms_eps"], fmt=self.fmt,
                        shared_fmt=self.fmt_sh if self.shared else self.fmt, device=dev, max_tokens=max_tokens,
                        rank=rank, world=world, nccl_id=nccl_id)
+        self.upload_into(torch, Q, dev, L)
+        return L
+
+    def upload_into(self, torch, Q, dev, L):
+        """Uploads this layer's weights into an existing layer L (a MoeLayer or
+        a layer of a MoeStack) on cuda:dev."""
         first, count = L.expert_range()
         for e in range(first, first + count):
             for w in range(3):
@@ -122,7 +128,6 @@ class SynthLayer:
             L.upload_logit_offset(offset)
         L.upload_norm(norm)
         torch.cuda.synchronize()
-        return L
 
     # ---------------------------------------------------------------- oracle
     def oracle_case(self, torch, Q, dev, experts=None):

@@ -26,7 +26,7 @@ def test_layer_from_qw(tmp_path, cfgname, over, router_fmt, layer):
     case = make_case(cfgname, seed=41, **over)
     path = str(tmp_path / f"{cfgname}.qw")
     router, bias = case_to_qw(path, case, layer=layer, router_fmt=router_fmt, n_layers=layer + 1,
-                              header_reserve=4096 if layer else 0)
+                              header_reserve=(1 << 16) if layer else 0)
     case.router = router                  # the values the file holds
     if bias is not None:
         case.router_bias = bias
