@@ -285,6 +285,26 @@ def run_reference(args, rank, world, out):
 
 # ------------------------------------------------------------------ GPU leg
 
+def profile_traffic(cfg_name, T, gateup):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary of this workload (profiles/), with the capture it comes from; None
+    when no capture covers the workload."""
+    if cfg_name != "c5" or T != 1 or not gateup:
+        return None
+    path = os.path.join(ROOT, "profiles", "expert_stream_c5_decode.md")
+    try:
+        with open(path) as fh:
+            for line in fh:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return (float(line.split(":")[1]),
+                            "ncu dram__bytes_read.sum + dram__bytes_write.sum of the gate/up launch, "
+                            "profiles/expert_stream_c5_decode.md (32-expert capture of the same shapes and "
+                            "routing width; per-launch bytes do not depend on the expert count)")
+    except OSError:
+        pass
+    return None
+
+
 def expert_flops(cfg, counts, T, shared):
     """2 * MACs of the expert products of one forward: per routed assignment
     and shared token 3 d*f (gate, up, down)."""
@@ -528,6 +548,10 @@ def run_one(args, cfg_name, T, rank, world, dist, torch, Q):
         roofline = dict(bound="hbm", kernel="whole layer step per rank (expert parallel: no per-stage events)",
                         achieved=ach, peak=hbm, unit="GB/s", frac=ach / hbm, peak_kind=f"{peak_kind} hbm_gbs",
                         traffic=None)
+    if world == 1 and roofline and roofline.get("bound") == "hbm":
+        tr = profile_traffic(cfg_name, T, "gate/up" in roofline["kernel"])
+        if tr:
+            roofline["traffic"], roofline["traffic_source"] = tr
     layer_gbs = layer_bytes / (total_ms / args.steps / 1000.0) / 1e9
     layer_hbm = dict(achieved_gbs=layer_gbs, frac_of_8tbs=layer_gbs / NOMINAL_HBM_GBS, frac_of_measured=layer_gbs / hbm,
                      bytes_per_step=layer_bytes)

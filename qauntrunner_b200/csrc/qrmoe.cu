@@ -858,7 +858,9 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
     // kernels with large dynamic shared memory
     if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(qrm::route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(qrm::dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess)
+        cudaFuncSetAttribute(qrm::dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
+        cudaFuncSetAttribute(qrm::logits_lm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)qrm::logits_lm_smem()) != cudaSuccess)
         return bail(fail(QRM_E_CUDA, "kernel attribute"));
     *out = L;
     return QRM_OK;
@@ -1085,9 +1087,10 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             } else {
                 xn = x;
             }
-            dim3 grid((T + qrm::kLT - 1) / qrm::kLT, (E + qrm::kLE - 1) / qrm::kLE);
+            dim3 grid((T + qrm::kLMT - 1) / qrm::kLMT, (E + qrm::kLME - 1) / qrm::kLME);
             nl++;
-            qrm::logits_tiled_kernel<<<grid, 256, 0, s>>>(xn, L->router, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
+            qrm::logits_lm_kernel<<<grid, qrm::kLMThreads, qrm::logits_lm_smem(), s>>>(
+                xn, L->router_lm, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
         }
         QRM_CUDA(cudaGetLastError());
         mark(1, -1);

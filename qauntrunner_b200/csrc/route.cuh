@@ -234,97 +234,6 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     }
 }
 
-// Large-T router logits: CTA tile of 16 tokens x 16 experts, 256 threads,
-// thread = (token pair, expert quad, lane j) -> 8 independent chains.
-constexpr int kLT = 16, kLE = 16, kLCH = 64;
-__global__ void __launch_bounds__(256)
-logits_tiled_kernel(const float* __restrict__ xn, const float* __restrict__ router,
-                    const float* __restrict__ offset, float* __restrict__ logits, int T, int d, int E) {
-    __shared__ __align__(16) float Xs[2][kLT][kLCH];
-    __shared__ __align__(16) float Ws[2][kLE][kLCH];
-    __shared__ float red[kLT][kLE][9];
-    const int tid = threadIdx.x;
-    const int j = tid & 7, eg = (tid >> 3) & 3, tg = tid >> 5;
-    const int t0 = blockIdx.x * kLT, e0 = blockIdx.y * kLE;
-    const int d8 = d / 8 * 8;
-    const int nch = d8 / kLCH;               // full chunks (d8 % 64 handled below)
-    float acc[2][4];
-#pragma unroll
-    for (int a = 0; a < 2; a++)
-#pragma unroll
-        for (int b = 0; b < 4; b++) acc[a][b] = 0.f;
-
-    auto load = [&](int buf, int c) {
-        // 16 rows x 64 cols each of X and W: 2 * 256 float4 -> 2 per thread
-        for (int i = tid; i < 2 * kLT * (kLCH / 4); i += 256) {
-            int isw = i >= kLT * (kLCH / 4);
-            int k = isw ? i - kLT * (kLCH / 4) : i;
-            int r = k / (kLCH / 4), q = k % (kLCH / 4);
-            if (!isw) {
-                int t = t0 + r;
-                if (t < T) cp_async16(&Xs[buf][r][4 * q], xn + (size_t)t * d + c * kLCH + 4 * q);
-                else *(float4*)&Xs[buf][r][4 * q] = make_float4(0, 0, 0, 0);
-            } else {
-                int e = e0 + r;
-                if (e < E) cp_async16(&Ws[buf][r][4 * q], router + (size_t)e * d + c * kLCH + 4 * q);
-                else *(float4*)&Ws[buf][r][4 * q] = make_float4(0, 0, 0, 0);
-            }
-        }
-        cp_async_commit();
-    };
-    if (nch > 0) load(0, 0);
-    for (int c = 0; c < nch; c++) {
-        if (c + 1 < nch) { load((c + 1) & 1, c + 1); cp_async_wait<1>(); }
-        else cp_async_wait<0>();
-        __syncthreads();
-        const int b = c & 1;
-#pragma unroll
-        for (int s = 0; s < kLCH / 8; s++) {
-            const int col = 8 * s + j;
-            float xv0 = Xs[b][2 * tg][col], xv1 = Xs[b][2 * tg + 1][col];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                float wv = Ws[b][4 * eg + q][col];
-                acc[0][q] = __fadd_rn(acc[0][q], __fmul_rn(wv, xv0));
-                acc[1][q] = __fadd_rn(acc[1][q], __fmul_rn(wv, xv1));
-            }
-        }
-        __syncthreads();
-    }
-    // remaining full groups of 8 columns beyond the last 64-column chunk
-    for (int i = nch * kLCH; i < d8; i += 8) {
-#pragma unroll
-        for (int a = 0; a < 2; a++) {
-            int t = t0 + 2 * tg + a;
-            float xv = t < T ? xn[(size_t)t * d + i + j] : 0.f;
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                int e = e0 + 4 * eg + q;
-                float wv = e < E ? router[(size_t)e * d + i + j] : 0.f;
-                acc[a][q] = __fadd_rn(acc[a][q], __fmul_rn(wv, xv));
-            }
-        }
-    }
-#pragma unroll
-    for (int a = 0; a < 2; a++)
-#pragma unroll
-        for (int q = 0; q < 4; q++) red[2 * tg + a][4 * eg + q][j] = acc[a][q];
-    __syncthreads();
-    {
-        int tt = tid >> 4, ee = tid & 15;
-        int t = t0 + tt, e = e0 + ee;
-        if (t < T && e < E) {
-            float s;
-            int i;
-            if (d >= 8) { s = hsum8_seq(red[tt][ee]); i = d8; }
-            else { s = 0.f; i = 0; }
-            for (; i < d; i++) s = __fadd_rn(s, __fmul_rn(router[(size_t)e * d + i], xn[(size_t)t * d + i]));
-            if (offset) s = __fadd_rn(s, offset[e]);
-            logits[(size_t)t * E + e] = s;
-        }
-    }
-}
-
 // ---------------------------------------------------------------------------
 // Top-k: one warp per token.
 // Ranking = Array.Sort(idx, (a, b) => v[b].CompareTo(v[a])): value
@@ -656,6 +565,109 @@ __device__ __forceinline__ float lane_chain4(const float* __restrict__ a, const 
         acc = __fadd_rn(acc, __fmul_rn(x.w, y.w));
     }
     return acc;
+}
+
+// ---------------------------------------------------------------------------
+// Large-T router logits.  CTA tile: 32 tokens x 32 experts, 512 threads;
+// thread (token quad tq, expert quad eq, lane j) runs the 16 chains of lane j
+// for its 4 tokens x 4 experts (SimdMath.DotF32's lane j: acc + w*x over
+// columns j, j+8, ... in order, products and sums rounded separately), so the
+// logits stay bit-exact.  Chunks of kLMC steps (8*kLMC columns) of the token
+// rows (row-major) and of the experts' lane-major router rows (router_lm)
+// stream into shared memory with cp.async, two chunks in flight; a 128-bit
+// load covers four steps of one expert, the token columns of lane j are four
+// conflict-free scalar loads.  16 independent chains per thread keep the FP32
+// pipes busy (the previous 16 x 16 tile with 8 chains and 4-way bank
+// conflicts on the router loads ran at about a fifth of FP32 peak).
+constexpr int kLMT = 32, kLME = 32, kLMC = 16, kLMThreads = 512;
+constexpr int kLMXPitch = 8 * kLMC + 4;   // floats per token row of a chunk
+constexpr int kLMWPitch = kLMC + 4;       // floats per (expert, lane): the 8 lanes start 4 banks apart
+constexpr int kLMBuf = kLMT * kLMXPitch + kLME * 8 * kLMWPitch;   // floats of one chunk buffer
+inline size_t logits_lm_smem() { return sizeof(float) * 2 * kLMBuf; }
+
+__global__ void __launch_bounds__(kLMThreads, 2)
+logits_lm_kernel(const float* __restrict__ xn, const float* __restrict__ router_lm, const float* __restrict__ offset,
+                 float* __restrict__ logits, int T, int d, int E) {
+    extern __shared__ __align__(16) float lsm[];
+    const int tid = threadIdx.x, j = tid & 7, eq = (tid >> 3) & 7, tq = tid >> 6;
+    const int t0 = blockIdx.x * kLMT, e0 = blockIdx.y * kLME;
+    const int nm = d / 8, P = route_lane_pitch(d);            // d % 32 == 0: nm % 4 == 0
+    const int nch = (nm + kLMC - 1) / kLMC;
+    // chunk c into buffer b: token rows (32 x 8*kLMC floats) and lane-major
+    // router rows (32 experts x 8 lanes x kLMC floats), 2 + 2 copies of 16 B per thread
+    auto load = [&](int b, int c) {
+        float* X = lsm + b * kLMBuf;
+        float* W = X + kLMT * kLMXPitch;
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int i = tid + u * kLMThreads, r = i >> 5, q = i & 31;     // token row r, 16-byte piece q
+            const int col = 8 * kLMC * c + 4 * q;
+            float* dst = X + r * kLMXPitch + 4 * q;
+            if (t0 + r < T && col < d) cp_async16(dst, xn + (size_t)(t0 + r) * d + col);
+            else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int i = tid + u * kLMThreads, row = i >> 2, q = i & 3;    // row = expert * 8 + lane
+            const int e = e0 + (row >> 3), m = kLMC * c + 4 * q;
+            float* dst = W + row * kLMWPitch + 4 * q;
+            if (e < E && m < nm) cp_async16(dst, router_lm + ((size_t)e * 8 + (row & 7)) * P + m);
+            else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        cp_async_commit();
+    };
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) acc[a][b] = 0.f;
+    load(0, 0);
+    for (int c = 0; c < nch; c++) {
+        if (c + 1 < nch) {
+            load((c + 1) & 1, c + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float* X = lsm + (c & 1) * kLMBuf;
+        const float* W = X + kLMT * kLMXPitch;
+        const int steps = min(kLMC, nm - kLMC * c);   // a multiple of 4
+        for (int q = 0; q < steps / 4; q++) {
+            float x[4][4];
+#pragma unroll
+            for (int a = 0; a < 4; a++)
+#pragma unroll
+                for (int s = 0; s < 4; s++) x[a][s] = X[(4 * tq + a) * kLMXPitch + 8 * (4 * q + s) + j];
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const float4 w = *reinterpret_cast<const float4*>(W + ((4 * eq + b) * 8 + j) * kLMWPitch + 4 * q);
+#pragma unroll
+                for (int a = 0; a < 4; a++) {
+                    acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(w.x, x[a][0]));
+                    acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(w.y, x[a][1]));
+                    acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(w.z, x[a][2]));
+                    acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(w.w, x[a][3]));
+                }
+            }
+        }
+        __syncthreads();
+    }
+    // lane sums in order: red[token][expert][lane]
+    float* red = lsm;
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int b = 0; b < 4; b++) red[((4 * tq + a) * kLME + 4 * eq + b) * 8 + j] = acc[a][b];
+    __syncthreads();
+    for (int i = tid; i < kLMT * kLME; i += kLMThreads) {
+        const int tt = i / kLME, ee = i - tt * kLME, t = t0 + tt, e = e0 + ee;
+        if (t < T && e < E) {
+            float s = hsum8_seq(red + (size_t)i * 8);
+            if (offset) s = __fadd_rn(s, offset[e]);
+            logits[(size_t)t * E + e] = s;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------

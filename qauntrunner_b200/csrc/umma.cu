@@ -95,11 +95,7 @@ long long umma_item_cap(int n_local, long long Tk, long long T, int rb_gateup, i
 
 template <int FA, int FB, bool GU>
 static cudaError_t launch_t(const CUtensorMap& map, const UmmaParams& p, int grid, cudaStream_t s) {
-    static const int raw_min = [] {
-        const char* e = getenv("QRM_UMMA_RAW_MIN");   // ring split for tuning runs
-        return e ? std::max(2, std::min(6, atoi(e))) : 0;
-    }();
-    const UmmaSmem sm = umma_smem(FA, FB, raw_min);
+    const UmmaSmem sm = umma_smem(FA, FB);
     // one CTA per SM (it holds all of tensor memory): more than half the shared memory
     if (sm.total <= 114 * 1024 || sm.raw_stages < 2 || sm.b_stages < 2) return cudaErrorInvalidConfiguration;
     static bool attr = false;

@@ -331,15 +331,16 @@ struct UmmaSmem {
     int b_stages;       // B ring depth
     size_t b_off, x_off, total;
 };
-// Ring depths: at least raw_min raw stages (three, two for the largest
-// formats, or raw_min when given), as many B tiles as fit up to 8, then more
-// raw stages with what is left.
-__host__ inline UmmaSmem umma_smem(int fa, int fb, int raw_min_req = 0) {
+// Ring depths: at least three raw stages (two for the largest formats), as
+// many B tiles as fit up to 8, then more raw stages with what is left (two
+// raw stages and five B tiles for the Q8_0 shared expert of C5 measured the
+// same at T 4096, and slower for C4).
+__host__ inline UmmaSmem umma_smem(int fa, int fb) {
     UmmaSmem s;
     s.raw_bytes = std::max(umma_raw_bytes(fa), umma_raw_bytes(fb));
     const int budget = 227 * 1024 - 1024 /* alignment slack */ - 1024 /* control */ - 1024 /* B alignment */ -
                        kUmmaStageBytes;
-    const int raw_min = raw_min_req >= 2 ? raw_min_req : (3 * s.raw_bytes + 4 * kUmmaBBytes <= budget ? 3 : 2);
+    const int raw_min = 3 * s.raw_bytes + 4 * kUmmaBBytes <= budget ? 3 : 2;
     s.b_stages = std::min(kUmmaBRingMax, (budget - raw_min * s.raw_bytes) / kUmmaBBytes);
     s.raw_stages = std::min(kUmmaRawRingMax, (budget - s.b_stages * kUmmaBBytes) / s.raw_bytes);
     s.b_off = ((size_t)1024 + (size_t)s.raw_stages * s.raw_bytes + 1023) / 1024 * 1024;
