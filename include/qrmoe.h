@@ -48,10 +48,14 @@ enum {
 };
 
 /* QuantFormat ids as stored in .qw headers (src/QuantRunner.Core/Dtypes.cs:6-26).
- * Expert matrices may use Q4_0, Q8_0, Q4_K, Q6_K or TRI. */
+ * Expert matrices may use any block format: Q4_0, Q8_0, Q4_K, Q6_K and TRI
+ * run on the tensor-core kernels; Q2_K, Q3_K, Q5_K, I8_BLK, B1, B1X, T1E and
+ * T1E_LO are kept exactly as stored and run on the CUDA-core kernel
+ * (decoders of BlockDequantizer.cs, T1E's rANS stream of EntropyCoder.cs). */
 enum {
-    QRM_F32 = 0, QRM_F16 = 1, QRM_BF16 = 2, QRM_Q4_0 = 3, QRM_Q8_0 = 4,
-    QRM_Q4_K = 6, QRM_Q6_K = 7, QRM_TRI = 8
+    QRM_F32 = 0, QRM_F16 = 1, QRM_BF16 = 2, QRM_Q4_0 = 3, QRM_Q8_0 = 4, QRM_Q2_K = 5,
+    QRM_Q4_K = 6, QRM_Q6_K = 7, QRM_TRI = 8, QRM_I8_BLK = 9, QRM_Q3_K = 10, QRM_Q5_K = 11,
+    QRM_B1 = 12, QRM_B1X = 13, QRM_T1E = 14, QRM_T1E_LO = 15
 };
 
 /* Which matrix of an expert (canonical names, src/QuantRunner.Core/Models/

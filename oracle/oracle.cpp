@@ -46,6 +46,14 @@ int orc_block_spec(int fmt, int* bs, int* bb) {
         case ORC_Q4_K: s = 256; b = 144; break;
         case ORC_Q6_K: s = 256; b = 210; break;
         case ORC_TRI: s = 64; b = 18; break;
+        case ORC_Q2_K: s = 256; b = 84; break;
+        case ORC_Q3_K: s = 256; b = 110; break;
+        case ORC_Q5_K: s = 256; b = 176; break;
+        case ORC_I8_BLK: s = 256; b = 258; break;
+        case ORC_B1: s = 256; b = 34; break;
+        case ORC_B1X: s = 256; b = 47; break;
+        case ORC_T1E: s = 256; b = 40; break;
+        case ORC_T1E_LO: s = 256; b = 32; break;
         default: return -1;
     }
     if (bs) *bs = s;
@@ -359,6 +367,54 @@ static inline void scale_min_k4(int j, const uint8_t* q, int* sc, int* m) {
     }
 }
 
+// Q3_K's 16 signed 6-bit scales from the 12 packed bytes (the kmask shuffle
+// over three little-endian words), BlockDequantizer.cs:130-143, DotKernels.cs:287-298
+static void q3k_scales(const uint8_t* packed, int* sc) {
+    uint32_t a0 = (uint32_t)(packed[0] | (packed[1] << 8) | (packed[2] << 16) | ((uint32_t)packed[3] << 24));
+    uint32_t a1 = (uint32_t)(packed[4] | (packed[5] << 8) | (packed[6] << 16) | ((uint32_t)packed[7] << 24));
+    uint32_t a2 = (uint32_t)(packed[8] | (packed[9] << 8) | (packed[10] << 16) | ((uint32_t)packed[11] << 24));
+    uint32_t tmp = a2;
+    uint32_t r2 = ((a0 >> 4) & 0x0f0f0f0fu) | (((tmp >> 4) & 0x03030303u) << 4);
+    uint32_t r3 = ((a1 >> 4) & 0x0f0f0f0fu) | (((tmp >> 6) & 0x03030303u) << 4);
+    uint32_t r0 = (a0 & 0x0f0f0f0fu) | (((tmp >> 0) & 0x03030303u) << 4);
+    uint32_t r1 = (a1 & 0x0f0f0f0fu) | (((tmp >> 2) & 0x03030303u) << 4);
+    const uint32_t aux[4] = {r0, r1, r2, r3};
+    for (int i = 0; i < 16; i++) sc[i] = (int)(int8_t)(uint8_t)(aux[i / 4] >> (8 * (i % 4))) - 32;
+}
+
+// 2-bit code of weight w (0..255) of a Q2_K / Q3_K block's qs (bit planes)
+static inline int q2_code(const uint8_t* q, int w) {
+    int shift = 2 * ((w % 128) / 32);
+    return (q[32 * (w / 128) + (w % 128) % 32] >> shift) & 3;
+}
+
+// EntropyCoder.Decode3 (EntropyCoder.cs:83-110): rANS, M = 256, L = 2^23.
+// Returns -1 where the reference throws (truncated or corrupt stream).
+static int rans_decode3(const uint8_t* src, int len, int n, uint32_t f0, uint32_t f1, uint8_t* out) {
+    const uint32_t M = 256, L = 1u << 23;
+    uint32_t f2 = M - f0 - f1;
+    int p = 0;
+    uint32_t x = 0;
+    for (int b = 0; b < 4; b++) {
+        if (p >= len) return -1;
+        x = (x << 8) | src[p++];
+    }
+    for (int i = 0; i < n; i++) {
+        while (x < L) {
+            if (p >= len) return -1;
+            x = (x << 8) | src[p++];
+        }
+        uint32_t slot = x & (M - 1), s, f, c;
+        if (slot < f0) { s = 0; f = f0; c = 0; }
+        else if (slot < f0 + f1) { s = 1; f = f1; c = f0; }
+        else { s = 2; f = f2; c = f0 + f1; }
+        if (f == 0) return -1;
+        x = f * (x >> 8) + slot - c;
+        out[i] = (uint8_t)s;
+    }
+    return 0;
+}
+
 int orc_dequantize(int fmt, const uint8_t* s, int64_t n, float* y) {
     int bs, bb;
     if (orc_block_spec(fmt, &bs, &bb) != 0 || n % bs != 0) return -1;
@@ -429,6 +485,74 @@ int orc_dequantize(int fmt, const uint8_t* s, int64_t n, float* y) {
                     int code = (s[2 + i / 4] >> (2 * (i & 3))) & 3;
                     y[i] = code == 1 ? scale : code == 2 ? -scale : 0.f;
                 }
+            }
+            return 0;
+        case ORC_Q2_K:  // BlockDequantizer.cs:87-114
+            for (int64_t b = 0; b < nb; b++, s += 84, y += 256) {
+                float d = orc_f16_to_f32(rd16(s + 80)), dmin = orc_f16_to_f32(rd16(s + 82));
+                for (int sub = 0; sub < 16; sub++) {
+                    float a = d * (s[sub] & 0xF), m = dmin * (s[sub] >> 4);
+                    for (int i = 0; i < 16; i++) {
+                        int w = sub * 16 + i;
+                        y[w] = a * q2_code(s + 16, w) - m;
+                    }
+                }
+            }
+            return 0;
+        case ORC_Q3_K:  // BlockDequantizer.cs:117-151
+            for (int64_t b = 0; b < nb; b++, s += 110, y += 256) {
+                float d = orc_f16_to_f32(rd16(s + 108));
+                int sc[16];
+                q3k_scales(s + 96, sc);
+                for (int w = 0; w < 256; w++) {
+                    int qv = q2_code(s + 32, w);
+                    if ((s[w % 32] & (1 << (w / 32))) == 0) qv -= 4;
+                    y[w] = d * sc[w / 16] * qv;
+                }
+            }
+            return 0;
+        case ORC_Q5_K:  // BlockDequantizer.cs:198-226
+            for (int64_t b = 0; b < nb; b++, s += 176, y += 256) {
+                float d = orc_f16_to_f32(rd16(s)), dmin = orc_f16_to_f32(rd16(s + 2));
+                const uint8_t *packed = s + 4, *ql = s + 16, *qh = s + 144;
+                for (int sub = 0; sub < 8; sub++) {
+                    int scI, mI;
+                    scale_min_k4(sub, packed, &scI, &mI);
+                    float a = d * scI, m = dmin * mI;
+                    int j = sub / 2;
+                    const uint8_t* q = ql + j * 32;
+                    int u1 = 1 << (2 * j), u2 = 2 << (2 * j);
+                    if ((sub & 1) == 0)
+                        for (int i = 0; i < 32; i++) y[sub * 32 + i] = a * ((q[i] & 0xF) + ((qh[i] & u1) != 0 ? 16 : 0)) - m;
+                    else
+                        for (int i = 0; i < 32; i++) y[sub * 32 + i] = a * ((q[i] >> 4) + ((qh[i] & u2) != 0 ? 16 : 0)) - m;
+                }
+            }
+            return 0;
+        case ORC_I8_BLK:  // BlockDequantizer.cs:278-290
+            for (int64_t b = 0; b < nb; b++, s += 258, y += 256) {
+                float d = orc_f16_to_f32(rd16(s));
+                for (int i = 0; i < 256; i++) y[i] = d * (int8_t)s[2 + i];
+            }
+            return 0;
+        case ORC_B1:  // BlockDequantizer.cs:299-313
+        case ORC_B1X:  // BlockDequantizer.cs:315-336
+            for (int64_t b = 0; b < nb; b++, s += bb, y += 256) {
+                float a = orc_f16_to_f32(rd16(s));
+                for (int i = 0; i < 256; i++) y[i] = (s[2 + (i >> 3)] & (1 << (i & 7))) != 0 ? a : -a;
+                if (fmt == ORC_B1X) {
+                    int k = s[34];
+                    for (int e = 0; e < k; e++) y[s[35 + 3 * e]] = orc_f16_to_f32(rd16(s + 35 + 3 * e + 1));
+                }
+            }
+            return 0;
+        case ORC_T1E:  // BlockDequantizer.cs:338-359
+        case ORC_T1E_LO:
+            for (int64_t b = 0; b < nb; b++, s += bb, y += 256) {
+                uint8_t syms[256];
+                float a = orc_f16_to_f32(rd16(s + 4));
+                if (rans_decode3(s + 6, bb - 6, 256, rd16(s), rd16(s + 2), syms) != 0) return -1;
+                for (int i = 0; i < 256; i++) y[i] = syms[i] == 1 ? a : syms[i] == 2 ? -a : 0.f;
             }
             return 0;
         default: return -1;
@@ -621,6 +745,138 @@ static float dot_tri(const uint8_t* w, const float* x, int cols) {
     return sum;
 }
 
+static float dot_q2_k(const uint8_t* w, const float* x, int cols) {
+    // DotKernels.DotQ2_K, DotKernels.cs:240-266 (+ SubSum 270-275)
+    int nb = cols / 256;
+    float sum = 0.f;
+    for (int b = 0; b < nb; b++, w += 84, x += 256) {
+        float d = orc_f16_to_f32(rd16(w + 80)), dmin = orc_f16_to_f32(rd16(w + 82));
+        for (int sub = 0; sub < 16; sub++) {
+            float a = d * (w[sub] & 0xF);
+            float m = dmin * (w[sub] >> 4);
+            int r = sub * 16;
+            float dsub = 0;
+            for (int i = 0; i < 16; i++) dsub += q2_code(w + 16, r + i) * x[r + i];
+            sum += a * dsub - m * subsum(x + r, 16);
+        }
+    }
+    return sum;
+}
+
+static float dot_q3_k(const uint8_t* w, const float* x, int cols) {
+    // DotKernels.DotQ3_K, DotKernels.cs:280-318
+    int nb = cols / 256;
+    float sum = 0.f;
+    int sc[16];
+    for (int b = 0; b < nb; b++, w += 110, x += 256) {
+        float d = orc_f16_to_f32(rd16(w + 108));
+        q3k_scales(w + 96, sc);
+        for (int sub = 0; sub < 16; sub++) {
+            float a = d * sc[sub];
+            int r = sub * 16;
+            float dsub = 0;
+            for (int i = 0; i < 16; i++) {
+                int wI = r + i;
+                int qv = q2_code(w + 32, wI);
+                if ((w[wI % 32] & (1 << (wI / 32))) == 0) qv -= 4;
+                dsub += qv * x[wI];
+            }
+            sum += a * dsub;
+        }
+    }
+    return sum;
+}
+
+static float dot_q5_k(const uint8_t* w, const float* x, int cols) {
+    // DotKernels.DotQ5_K, DotKernels.cs:378-418
+    int nb = cols / 256;
+    float sum = 0.f;
+    for (int b = 0; b < nb; b++, w += 176, x += 256) {
+        float d = orc_f16_to_f32(rd16(w)), dmin = orc_f16_to_f32(rd16(w + 2));
+        const uint8_t *packed = w + 4, *ql = w + 16, *qh = w + 144;
+        for (int sub = 0; sub < 8; sub++) {
+            int scI, mI;
+            scale_min_k4(sub, packed, &scI, &mI);
+            float a = d * scI, m = dmin * mI;
+            int j = sub / 2;
+            const uint8_t* q = ql + j * 32;
+            int u1 = 1 << (2 * j), u2 = 2 << (2 * j);
+            float dsub = 0, xsub = 0;
+            int wBase = sub * 32;
+            for (int i = 0; i < 32; i++) {
+                int q5 = (sub & 1) == 0 ? (q[i] & 0xF) + ((qh[i] & u1) != 0 ? 16 : 0)
+                                        : (q[i] >> 4) + ((qh[i] & u2) != 0 ? 16 : 0);
+                dsub += q5 * x[wBase + i];
+                xsub += x[wBase + i];
+            }
+            sum += a * dsub - m * xsub;
+        }
+    }
+    return sum;
+}
+
+// DotKernels.DotI8Bytes (vector branch), DotKernels.cs:209-234, n = 16:
+// two 8-lane products added into one accumulator, then HSum
+static float dot_i8_bytes16(const uint8_t* q, const float* x) {
+    float acc[8];
+    for (int l = 0; l < 8; l++) acc[l] = 0.f + (float)(int8_t)q[l] * x[l];
+    for (int l = 0; l < 8; l++) acc[l] = acc[l] + (float)(int8_t)q[8 + l] * x[8 + l];
+    return hsum8(acc);
+}
+
+static float dot_i8_blk(const uint8_t* w, const float* x, int cols) {
+    // DotKernels.DotI8Blk, DotKernels.cs:476-495 (vector branch)
+    int nb = cols / 256;
+    float sum = 0.f;
+    for (int b = 0; b < nb; b++, w += 258, x += 256) {
+        float d = orc_f16_to_f32(rd16(w));
+        float dot = 0;
+        for (int i = 0; i < 256; i += 16) dot += dot_i8_bytes16(w + 2 + i, x + i);
+        sum += d * dot;
+    }
+    return sum;
+}
+
+static float dot_b1(const uint8_t* w, const float* x, int cols, bool exc) {
+    // DotKernels.DotB1 / DotB1X (DotKernels.cs:515-556) with ExpandSigns 559-569
+    int nb = cols / 256, bb = exc ? 47 : 34;
+    float sum = 0.f;
+    float sf[256];
+    for (int b = 0; b < nb; b++, w += bb, x += 256) {
+        float a = orc_f16_to_f32(rd16(w));
+        for (int i = 0; i < 256; i++) sf[i] = (w[2 + (i >> 3)] & (1 << (i & 7))) != 0 ? 1.f : -1.f;
+        sum += a * orc_dot_f32(sf, x, 256);
+        if (exc) {
+            int k = w[34];
+            for (int e = 0; e < k; e++) {
+                int idx = w[35 + 3 * e];
+                float v = orc_f16_to_f32(rd16(w + 35 + 3 * e + 1));
+                float sgn = (w[2 + (idx >> 3)] & (1 << (idx & 7))) != 0 ? 1.f : -1.f;
+                sum += (v - a * sgn) * x[idx];
+            }
+        }
+    }
+    return sum;
+}
+
+static float dot_t1e(const uint8_t* w, const float* x, int cols, int stream) {
+    // DotKernels.DotT1E, DotKernels.cs:572-593
+    int nb = cols / 256;
+    float sum = 0.f;
+    uint8_t syms[256];
+    for (int b = 0; b < nb; b++, w += 6 + stream, x += 256) {
+        float a = orc_f16_to_f32(rd16(w + 4));
+        if (rans_decode3(w + 6, stream, 256, rd16(w), rd16(w + 2), syms) != 0) return NAN;
+        float dot = 0;
+        for (int i = 0; i < 256; i++) {
+            float v = syms[i] == 1 ? a : syms[i] == 2 ? -a : 0.f;
+            dot += v * x[i];
+        }
+        sum += dot;
+    }
+    return sum;
+}
+
 float orc_dot_row(int fmt, const uint8_t* w, const float* x, int cols) {
     switch (fmt) {
         case ORC_F32: {
@@ -635,6 +891,14 @@ float orc_dot_row(int fmt, const uint8_t* w, const float* x, int cols) {
         case ORC_Q4_K: return dot_q4_k(w, x, cols);
         case ORC_Q6_K: return dot_q6_k(w, x, cols);
         case ORC_TRI: return dot_tri(w, x, cols);
+        case ORC_Q2_K: return dot_q2_k(w, x, cols);
+        case ORC_Q3_K: return dot_q3_k(w, x, cols);
+        case ORC_Q5_K: return dot_q5_k(w, x, cols);
+        case ORC_I8_BLK: return dot_i8_blk(w, x, cols);
+        case ORC_B1: return dot_b1(w, x, cols, false);
+        case ORC_B1X: return dot_b1(w, x, cols, true);
+        case ORC_T1E: return dot_t1e(w, x, cols, 34);
+        case ORC_T1E_LO: return dot_t1e(w, x, cols, 26);
         default: return NAN;
     }
 }

@@ -33,7 +33,8 @@ extern "C" {
 
 /* QuantFormat ids, src/QuantRunner.Core/Dtypes.cs:6-26 */
 enum { ORC_F32 = 0, ORC_F16 = 1, ORC_BF16 = 2, ORC_Q4_0 = 3, ORC_Q8_0 = 4,
-       ORC_Q4_K = 6, ORC_Q6_K = 7, ORC_TRI = 8 };
+       ORC_Q2_K = 5, ORC_Q4_K = 6, ORC_Q6_K = 7, ORC_TRI = 8, ORC_I8_BLK = 9, ORC_Q3_K = 10,
+       ORC_Q5_K = 11, ORC_B1 = 12, ORC_B1X = 13, ORC_T1E = 14, ORC_T1E_LO = 15 };
 
 /* Dtypes.cs:38-65 */
 int     orc_block_spec(int fmt, int* block_size, int* block_bytes);
@@ -49,13 +50,18 @@ void     orc_f32_to_f16_batch(const float* x, uint16_t* y, int64_t n);
 /* BlockQuantizer.cs: Q4_0 69-93, Q8_0 97-116, Q4_K 248-318, Q6_K 398-446,
  * TRI 456-521.  fmt 108 selects QuantizeTriLegacy 525-550.  Returns 0 or -1. */
 int orc_quantize(int fmt, const float* src, int64_t n, uint8_t* dst);
-/* BlockDequantizer.cs: Q4_0 52-69, Q8_0 71-84, Q4_K 168-195, Q6_K 228-256,
- * TRI 258-276; F32/F16/BF16 via Dtypes. */
+/* BlockDequantizer.cs: Q4_0 52-69, Q8_0 71-84, Q2_K 87-114, Q3_K 117-151,
+ * Q4_K 168-195, Q5_K 198-226, Q6_K 228-256, TRI 258-276, I8_BLK 278-290,
+ * B1 299-313, B1X 315-336, T1E / T1E_LO 338-359 (rANS: EntropyCoder.Decode3,
+ * EntropyCoder.cs:83-110; -1 where the reference throws); F32/F16/BF16 via
+ * Dtypes. */
 int orc_dequantize(int fmt, const uint8_t* src, int64_t n, float* dst);
 
 /* DotKernels.DotRow (DotKernels.cs:24-46) with the Vector256 paths of
- * DotF32 51-54 / DotQ4_0 132-179 / DotQ8_0 184-205 / DotQ4_K 325-357 /
- * DotQ6_K 423-451 / DotTri 456-471. */
+ * DotF32 51-54 / DotQ4_0 132-179 / DotQ8_0 184-205 / DotQ2_K 240-266 /
+ * DotQ3_K 280-318 / DotQ4_K 325-357 / DotQ5_K 378-418 / DotQ6_K 423-451 /
+ * DotTri 456-471 / DotI8Blk 476-495 / DotB1 515-531 / DotB1X 533-556 /
+ * DotT1E 572-593. */
 float orc_dot_row(int fmt, const uint8_t* w, const float* x, int cols);
 /* DotKernels.MatVec 599-607 (sequential). */
 int orc_matvec(int fmt, const uint8_t* w, int64_t rows, int64_t cols,

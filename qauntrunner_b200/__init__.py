@@ -28,13 +28,23 @@ class QuantFormat(enum.IntEnum):
     BF16 = 2
     Q4_0 = 3
     Q8_0 = 4
+    Q2_K = 5
     Q4_K = 6
     Q6_K = 7
     TRI = 8
+    I8_BLK = 9
+    Q3_K = 10
+    Q5_K = 11
+    B1 = 12
+    B1X = 13
+    T1E = 14
+    T1E_LO = 15
 
 
 TRI_LEGACY = 108  # quantiser selector for BlockQuantizer.QuantizeTriLegacy (same storage as TRI)
-BLOCK_SPEC = {0: (1, 4), 1: (1, 2), 2: (1, 2), 3: (32, 20), 4: (32, 34), 6: (256, 144), 7: (256, 210), 8: (64, 18)}
+BLOCK_SPEC = {0: (1, 4), 1: (1, 2), 2: (1, 2), 3: (32, 20), 4: (32, 34), 5: (256, 84), 6: (256, 144), 7: (256, 210),
+              8: (64, 18), 9: (256, 258), 10: (256, 110), 11: (256, 176), 12: (256, 34), 13: (256, 47), 14: (256, 40),
+              15: (256, 32)}
 GATE, UP, DOWN = 0, 1, 2
 SHARED_EXPERT = -1
 APPLY_NORM, ADD_RESIDUAL = 1, 2

@@ -7,7 +7,10 @@
 namespace qrm {
 
 // QuantFormat ids (Dtypes.cs:6-26)
-enum Fmt : int32_t { F32 = 0, F16 = 1, BF16 = 2, Q4_0 = 3, Q8_0 = 4, Q4_K = 6, Q6_K = 7, TRI = 8 };
+enum Fmt : int32_t {
+    F32 = 0, F16 = 1, BF16 = 2, Q4_0 = 3, Q8_0 = 4, Q2_K = 5, Q4_K = 6, Q6_K = 7, TRI = 8,
+    I8_BLK = 9, Q3_K = 10, Q5_K = 11, B1 = 12, B1X = 13, T1E = 14, T1E_LO = 15
+};
 
 // Dtypes.BlockSpec (Dtypes.cs:38-57)
 __host__ __device__ inline bool block_spec(int fmt, int* bs, int* bb) {
@@ -20,12 +23,27 @@ __host__ __device__ inline bool block_spec(int fmt, int* bs, int* bb) {
         case Q4_K: *bs = 256; *bb = 144; return true;
         case Q6_K: *bs = 256; *bb = 210; return true;
         case TRI: *bs = 64; *bb = 18; return true;
+        case Q2_K: *bs = 256; *bb = 84; return true;
+        case Q3_K: *bs = 256; *bb = 110; return true;
+        case Q5_K: *bs = 256; *bb = 176; return true;
+        case I8_BLK: *bs = 256; *bb = 258; return true;
+        case B1: *bs = 256; *bb = 34; return true;
+        case B1X: *bs = 256; *bb = 47; return true;
+        case T1E: *bs = 256; *bb = 40; return true;
+        case T1E_LO: *bs = 256; *bb = 32; return true;
         default: return false;
     }
 }
 
+// Formats kept in HBM exactly as stored in .qw (no field grouping) and taken
+// by the register kernel only: Q2_K, Q3_K, Q5_K, I8_BLK, B1, B1X, T1E, T1E_LO.
+inline bool is_raw_fmt(int fmt) {
+    return fmt == Q2_K || fmt == Q3_K || fmt == Q5_K || fmt == I8_BLK || fmt == B1 || fmt == B1X || fmt == T1E ||
+           fmt == T1E_LO;
+}
+
 inline bool is_expert_fmt(int fmt) {
-    return fmt == Q4_0 || fmt == Q8_0 || fmt == Q4_K || fmt == Q6_K || fmt == TRI;
+    return fmt == Q4_0 || fmt == Q8_0 || fmt == Q4_K || fmt == Q6_K || fmt == TRI || is_raw_fmt(fmt);
 }
 
 // A quantised matrix in HBM.  Q4_K keeps the .qw block bytes unchanged

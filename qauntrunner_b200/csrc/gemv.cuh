@@ -75,6 +75,16 @@ template <> __device__ __forceinline__ int unit_col<Q6_K>(int u, int i) {
 template <> __device__ __forceinline__ int unit_col<Q4_0>(int u, int i) { return 32 * u + i; }
 template <> __device__ __forceinline__ int unit_col<Q8_0>(int u, int i) { return 32 * u + i; }
 template <> __device__ __forceinline__ int unit_col<TRI>(int u, int i) { return 32 * u + i; }
+// the raw formats: unit u = weights [32u, 32u + 32) of the row (256-weight
+// blocks: block u / 8, quarter-pair u % 8)
+template <> __device__ __forceinline__ int unit_col<Q2_K>(int u, int i) { return 32 * u + i; }
+template <> __device__ __forceinline__ int unit_col<Q3_K>(int u, int i) { return 32 * u + i; }
+template <> __device__ __forceinline__ int unit_col<Q5_K>(int u, int i) { return 32 * u + i; }
+template <> __device__ __forceinline__ int unit_col<I8_BLK>(int u, int i) { return 32 * u + i; }
+template <> __device__ __forceinline__ int unit_col<B1>(int u, int i) { return 32 * u + i; }
+template <> __device__ __forceinline__ int unit_col<B1X>(int u, int i) { return 32 * u + i; }
+template <> __device__ __forceinline__ int unit_col<T1E>(int u, int i) { return 32 * u + i; }
+template <> __device__ __forceinline__ int unit_col<T1E_LO>(int u, int i) { return 32 * u + i; }
 
 // Per-token activation registers of one unit and the partial sums the
 // formats need.
@@ -261,6 +271,251 @@ template <> struct WUnit<TRI> {
         return h2f(sh) * (p - n);
     }
 };
+
+// ---------------------------------------------------------------- raw formats
+// Blocks exactly as stored in .qw (row r, block b at (r * blocks_per_row + b)
+// * block bytes); fields are read with loads no wider than the block's
+// alignment.  Each unit decodes its 32 weights to f32 (the decoder formulas of
+// BlockDequantizer.cs) and accumulates w * x in f32.
+__device__ __forceinline__ uint32_t ldb(const uint8_t* p) { return __ldg(p); }
+__device__ __forceinline__ uint32_t ldh(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned short*>(p)); }
+__device__ __forceinline__ uint32_t ldw(const uint8_t* p) { return __ldg(reinterpret_cast<const unsigned int*>(p)); }
+template <int BB>
+__device__ __forceinline__ const uint8_t* raw_block(const MatDev& m, int row, int u) {
+    return m.base + ((size_t)row * (m.cols >> 8) + (u >> 3)) * BB;
+}
+
+// Q2_K (84 B: scales[16] | qs[64] | d | dmin; BlockDequantizer.cs:87-114):
+// weight w: code (qs[32*(w/128) + w%32] >> 2*((w%128)/32)) & 3, sub-block
+// w/16: y = d*(sc & 15)*q - dmin*(sc >> 4).  Unit uu covers sub-blocks 2uu, 2uu+1.
+template <> struct WUnit<Q2_K> {
+    uint32_t q[8], scw, dd;
+    int uu;
+    __device__ __forceinline__ void load(const MatDev& m, int row, int u) {
+        const uint8_t* b = raw_block<84>(m, row, u);   // 84 = 4 x 21: 4-byte aligned
+        uu = u & 7;
+        const uint8_t* qs = b + 16 + 32 * (uu >> 2);
+#pragma unroll
+        for (int i = 0; i < 8; i++) q[i] = ldw(qs + 4 * i);
+        scw = ldh(b + 2 * uu);                        // sc[2uu] | sc[2uu+1] << 8
+        dd = ldw(b + 80);                             // d | dmin << 16
+    }
+    __device__ __forceinline__ float dot(const XUnit& xu) const {
+        const int sh = 2 * (uu & 3);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const float qv = (float)((q[i >> 2] >> (8 * (i & 3) + sh)) & 3u);
+            if (i < 16) a0 = fmaf(qv, xu.x[i], a0);
+            else a1 = fmaf(qv, xu.x[i], a1);
+        }
+        const float d = h2f((uint16_t)(dd & 0xFFFF)), dmin = h2f((uint16_t)(dd >> 16));
+        const uint32_t s0 = scw & 0xFF, s1 = scw >> 8;
+        return d * ((float)(s0 & 15) * a0 + (float)(s1 & 15) * a1) -
+               dmin * ((float)(s0 >> 4) * (xu.s[0] + xu.s[1]) + (float)(s1 >> 4) * (xu.s[2] + xu.s[3]));
+    }
+};
+
+// Q3_K (110 B: hmask[32] | qs[64] | scales[12] | d; BlockDequantizer.cs:117-151):
+// code as Q2_K, minus 4 where hmask[w%32] lacks bit w/32; 16 signed 6-bit
+// scales (kmask shuffle of the 12 packed bytes); y = d*sc*q.
+template <> struct WUnit<Q3_K> {
+    uint32_t q[8], hm[8];
+    int sc0, sc1, uu;
+    uint32_t dh;
+    __device__ __forceinline__ void load(const MatDev& m, int row, int u) {
+        const uint8_t* b = raw_block<110>(m, row, u);  // 2-byte aligned
+        uu = u & 7;
+        const uint8_t* qs = b + 32 + 32 * (uu >> 2);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            q[i] = ldh(qs + 4 * i) | (ldh(qs + 4 * i + 2) << 16);
+            hm[i] = ldh(b + 4 * i) | (ldh(b + 4 * i + 2) << 16);
+        }
+        // scales 2uu, 2uu+1 of the shuffle: index i -> word i/4 of (r0, r1, r2, r3)
+        uint32_t a[3];
+#pragma unroll
+        for (int w = 0; w < 3; w++) a[w] = ldh(b + 96 + 4 * w) | (ldh(b + 96 + 4 * w + 2) << 16);
+        auto scale = [&](int i) {
+            const int g = i >> 2, by = i & 3;
+            const uint32_t lo = g & 1 ? a[1] : a[0];
+            const uint32_t nib = (g >= 2 ? (lo >> 4) : lo) & 0x0F0F0F0Fu;
+            const uint32_t hi = (a[2] >> (2 * g)) & 0x03030303u;
+            const uint32_t r = nib | (hi << 4);
+            return (int)((r >> (8 * by)) & 0xFF) - 32;
+        };
+        sc0 = scale(2 * uu);
+        sc1 = scale(2 * uu + 1);
+        dh = ldh(b + 108);
+    }
+    __device__ __forceinline__ float dot(const XUnit& xu) const {
+        const int sh = 2 * (uu & 3);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            int qv = (int)((q[i >> 2] >> (8 * (i & 3) + sh)) & 3u);
+            if (((hm[i >> 2] >> (8 * (i & 3) + uu)) & 1u) == 0) qv -= 4;
+            if (i < 16) a0 = fmaf((float)qv, xu.x[i], a0);
+            else a1 = fmaf((float)qv, xu.x[i], a1);
+        }
+        return h2f((uint16_t)dh) * ((float)sc0 * a0 + (float)sc1 * a1);
+    }
+};
+
+// Q5_K (176 B: d | dmin | scales[12] | ql[128] | qh[32]; BlockDequantizer.cs:
+// 198-226): unit uu = sub-block uu; q = nibble (uu&1) of ql[32*(uu/2) + i]
+// + 16 * bit uu of qh[i]; y = d*sc*q - dmin*m (GetScaleMinK4).
+template <> struct WUnit<Q5_K> {
+    uint4 hdr, l0, l1, h0, h1;
+    int uu;
+    __device__ __forceinline__ void load(const MatDev& m, int row, int u) {
+        const uint8_t* b = raw_block<176>(m, row, u);  // 176 = 16 x 11: 16-byte aligned
+        uu = u & 7;
+        hdr = __ldg(reinterpret_cast<const uint4*>(b));
+        const uint8_t* ql = b + 16 + 32 * (uu >> 1);
+        l0 = ld_stream16(ql);
+        l1 = ld_stream16(ql + 16);
+        h0 = __ldg(reinterpret_cast<const uint4*>(b + 144));
+        h1 = __ldg(reinterpret_cast<const uint4*>(b + 160));
+    }
+    __device__ __forceinline__ float dot(const XUnit& xu) const {
+        const uint32_t L[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+        const uint32_t H[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        const int ls = 4 * (uu & 1);
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) {
+            const uint32_t qv = ((L[i >> 2] >> (8 * (i & 3) + ls)) & 15u) + 16u * ((H[i >> 2] >> (8 * (i & 3) + uu)) & 1u);
+            a = fmaf((float)qv, xu.x[i], a);
+        }
+        // GetScaleMinK4 (BlockDequantizer.cs:155-166) on scale bytes 4..15 of the block
+        const uint32_t sw[3] = {hdr.y, hdr.z, hdr.w};
+        auto byte = [&](int i) -> uint32_t { return (sw[i >> 2] >> (8 * (i & 3))) & 0xFF; };
+        uint32_t sc, mn;
+        if (uu < 4) { sc = byte(uu) & 63; mn = byte(uu + 4) & 63; }
+        else { sc = (byte(uu + 4) & 0xF) | ((byte(uu - 4) >> 6) << 4); mn = (byte(uu + 4) >> 4) | ((byte(uu) >> 6) << 4); }
+        const float d = h2f((uint16_t)(hdr.x & 0xFFFF)), dmin = h2f((uint16_t)(hdr.x >> 16));
+        return d * (float)sc * a - dmin * (float)mn * ((xu.s[0] + xu.s[1]) + (xu.s[2] + xu.s[3]));
+    }
+};
+
+// I8_BLK (258 B: d | int8 q[256]; BlockDequantizer.cs:278-290): y = d*q.
+template <> struct WUnit<I8_BLK> {
+    uint32_t q[8];
+    uint32_t dh;
+    __device__ __forceinline__ void load(const MatDev& m, int row, int u) {
+        const uint8_t* b = raw_block<258>(m, row, u);  // 2-byte aligned
+        const uint8_t* qs = b + 2 + 32 * (u & 7);
+#pragma unroll
+        for (int i = 0; i < 8; i++) q[i] = ldh(qs + 4 * i) | (ldh(qs + 4 * i + 2) << 16);
+        dh = ldh(b);
+    }
+    __device__ __forceinline__ float dot(const XUnit& xu) const {
+        float a = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) a = fmaf((float)(int8_t)((q[i >> 2] >> (8 * (i & 3))) & 0xFF), xu.x[i], a);
+        return h2f((uint16_t)dh) * a;
+    }
+};
+
+// B1 (34 B: f16 a | sign mask[32]; BlockDequantizer.cs:299-313): y = +a where
+// bit i of the mask is set, else -a.  B1X (47 B) adds k <= 4 exact values
+// (u8 idx, f16 v) at byte 35 (BlockDequantizer.cs:315-336).
+template <int FMT, int BB>
+struct WUnitB1 {
+    uint32_t mask, ah;
+    int uu, k;
+    uint32_t ex[4];   // idx | v << 16 of the block's exceptions (B1X)
+    __device__ __forceinline__ void load(const MatDev& m, int row, int u) {
+        const uint8_t* b = raw_block<BB>(m, row, u);
+        uu = u & 7;
+        const uint8_t* mk = b + 2 + 4 * uu;
+        mask = ldb(mk) | (ldb(mk + 1) << 8) | (ldb(mk + 2) << 16) | (ldb(mk + 3) << 24);
+        ah = ldb(b) | (ldb(b + 1) << 8);
+        k = 0;
+        if (FMT == B1X) {
+            k = min((int)ldb(b + 34), 4);
+            for (int e = 0; e < k; e++) {
+                const uint8_t* p = b + 35 + 3 * e;
+                ex[e] = ldb(p) | (ldb(p + 1) << 16) | (ldb(p + 2) << 24);
+            }
+        }
+    }
+    __device__ __forceinline__ float dot(const XUnit& xu) const {
+        float pos = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; i++) pos += ((mask >> i) & 1u) ? xu.x[i] : 0.f;
+        const float sx = (xu.s[0] + xu.s[1]) + (xu.s[2] + xu.s[3]);
+        const float a = h2f((uint16_t)ah);
+        float r = a * (2.f * pos - sx);
+        for (int e = 0; e < k; e++) {
+            const int idx = (int)(ex[e] & 0xFF) - 32 * uu;
+            if (idx < 0 || idx >= 32) continue;
+            const float v = h2f((uint16_t)(ex[e] >> 16));
+            float xv = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; i++) xv = i == idx ? xu.x[i] : xv;
+            r += (v - (((mask >> idx) & 1u) ? a : -a)) * xv;
+        }
+        return r;
+    }
+};
+template <> struct WUnit<B1> : WUnitB1<B1, 34> {};
+template <> struct WUnit<B1X> : WUnitB1<B1X, 47> {};
+
+// T1E / T1E_LO (u16 n0 | u16 nP | f16 a | rANS stream of SB bytes;
+// BlockDequantizer.cs:338-359, EntropyCoder.Decode3, EntropyCoder.cs:83-110):
+// symbols 0 -> 0, 1 -> +a, 2 -> -a.  The stream decodes front to back, so the
+// unit decodes symbols 0 .. 32uu+31 and keeps its 32.  A corrupt stream (one
+// the reference's decoder rejects: it would read past its bytes, or decode a
+// zero-frequency symbol) gives some finite values; every loop stays bounded.
+template <int SB>
+struct WUnitT1E {
+    const uint8_t* b;
+    int uu;
+    __device__ __forceinline__ void load(const MatDev& m, int row, int u) {
+        b = raw_block<6 + SB>(m, row, u);
+        uu = u & 7;
+    }
+    __device__ __forceinline__ float dot(const XUnit& xu) const {
+        const uint32_t f0 = ldb(b) | (ldb(b + 1) << 8), f1 = ldb(b + 2) | (ldb(b + 3) << 8);
+        const float a = h2f((uint16_t)(ldb(b + 4) | (ldb(b + 5) << 8)));
+        const uint32_t f2 = 256u - f0 - f1, L = 1u << 23;
+        const uint8_t* src = b + 6;
+        int p = 0;
+        uint32_t x = 0;
+        for (int i = 0; i < 4; i++) x = (x << 8) | (p < SB ? ldb(src + p++) : 0u);
+        uint32_t pm = 0, nm = 0;   // this unit's +a and -a weights
+        const int first = 32 * uu;
+        for (int i = 0; i < first + 32; i++) {
+            while (x < L) {
+                if (p >= SB + 4) { x = L; break; }   // past the stream: corrupt
+                x = (x << 8) | (p < SB ? ldb(src + p) : 0u);
+                p++;
+            }
+            const uint32_t slot = x & 255u;
+            uint32_t s, f, c;
+            if (slot < f0) { s = 0; f = f0; c = 0; }
+            else if (slot < f0 + f1) { s = 1; f = f1; c = f0; }
+            else { s = 2; f = f2; c = f0 + f1; }
+            if (f == 0 || f > 256u) break;        // corrupt: zero-frequency symbol or bad counts
+            x = f * (x >> 8) + slot - c;
+            if (i >= first) {
+                if (s == 1) pm |= 1u << (i - first);
+                else if (s == 2) nm |= 1u << (i - first);
+            }
+        }
+        float pos = 0.f, neg = 0.f;
+#pragma unroll
+        for (int q = 0; q < 32; q++) {
+            pos += ((pm >> q) & 1u) ? xu.x[q] : 0.f;
+            neg += ((nm >> q) & 1u) ? xu.x[q] : 0.f;
+        }
+        return a * (pos - neg);
+    }
+};
+template <> struct WUnit<T1E> : WUnitT1E<34> {};
+template <> struct WUnit<T1E_LO> : WUnitT1E<26> {};
 
 // ------------------------------------------------------------ reduction
 

@@ -330,15 +330,35 @@ int launch_gemv(int fmt, bool gateup, int nt, const qrm::GemvParams& p, int sm_c
             e = launch_gemv_nt<F, 1, kRDown>(nt, p, sm_count * occ, block, s);                  \
         }                                                                                       \
         break;
+    // formats stored as in .qw: the register kernel
+#define QRM_GEMV_RAW(F)                                                                         \
+    case F:                                                                                     \
+        if (gateup) {                                                                           \
+            occ = gemv_occupancy<F, 2, kRGateUp>(nt, block);                                    \
+            e = launch_gemv_nt<F, 2, kRGateUp>(nt, p, sm_count * occ, block, s);                \
+        } else {                                                                                \
+            occ = gemv_occupancy<F, 1, kRDown>(nt, block);                                      \
+            e = launch_gemv_nt<F, 1, kRDown>(nt, p, sm_count * occ, block, s);                  \
+        }                                                                                       \
+        break;
     switch (fmt) {
         QRM_GEMV_CASE(qrm::Q4_K)
         QRM_GEMV_CASE(qrm::Q4_0)
         QRM_GEMV_CASE(qrm::Q8_0)
         QRM_GEMV_CASE(qrm::Q6_K)
         QRM_GEMV_CASE(qrm::TRI)
+        QRM_GEMV_RAW(qrm::Q2_K)
+        QRM_GEMV_RAW(qrm::Q3_K)
+        QRM_GEMV_RAW(qrm::Q5_K)
+        QRM_GEMV_RAW(qrm::I8_BLK)
+        QRM_GEMV_RAW(qrm::B1)
+        QRM_GEMV_RAW(qrm::B1X)
+        QRM_GEMV_RAW(qrm::T1E)
+        QRM_GEMV_RAW(qrm::T1E_LO)
         default: return fail(QRM_E_FORMAT, "format %d has no expert kernel", fmt);
     }
 #undef QRM_GEMV_CASE
+#undef QRM_GEMV_RAW
     if (e != cudaSuccess) return fail(QRM_E_CUDA, "expert kernel launch: %s", cudaGetErrorString(e));
     return QRM_OK;
 }
@@ -934,7 +954,7 @@ static int upload_common(qrm_layer* L, int expert, int which, int fmt, const voi
     if (dev) QRM_CUDA(cudaDeviceSynchronize());
     uint8_t* dst = const_cast<uint8_t*>(m.base);
     const bool tiled = layer_tiled(fmt, L->desc.d_model, L->desc.expert_ffn, which != 2);
-    if (fmt == qrm::Q4_K && !tiled) {
+    if ((fmt == qrm::Q4_K && !tiled) || qrm::is_raw_fmt(fmt)) {
         QRM_CUDA(cudaMemcpyAsync(dst, bytes, nbytes, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, L->stream));
     } else {
         const uint8_t* src = (const uint8_t*)bytes;
@@ -985,7 +1005,7 @@ extern "C" int qrm_download_expert(qrm_layer* L, int expert, int which, void* by
     // a streamed layer's bytes are in its host image (its slot holds whichever
     // layer ran last)
     const uint8_t* img = L->image ? L->image + (m.base - L->slab) : nullptr;
-    if (m.fmt == qrm::Q4_K && !tiled) {
+    if ((m.fmt == qrm::Q4_K && !tiled) || qrm::is_raw_fmt(m.fmt)) {
         if (img) memcpy(bytes, img, nbytes);
         else QRM_CUDA(cudaMemcpy(bytes, m.base, nbytes, cudaMemcpyDeviceToHost));
         return QRM_OK;
@@ -1783,7 +1803,7 @@ extern "C" int qrm_matrix_create(int device, int fmt, int64_t rows, int64_t cols
     if (imma_usable(fmt, (int)rows, (int)cols, false))
         qrm::tile_relayout_kernel<<<M->sm_count * 8, 256>>>(fmt, bb, (int)(cols / 256), staging, M->data,
                                                             (long long)(nbytes / bb), 1);
-    else if (fmt == qrm::Q4_K) cudaMemcpy(M->data, staging, nbytes, cudaMemcpyDeviceToDevice);
+    else if (fmt == qrm::Q4_K || qrm::is_raw_fmt(fmt)) cudaMemcpy(M->data, staging, nbytes, cudaMemcpyDeviceToDevice);
     else qrm::relayout_kernel<<<M->sm_count * 8, 256>>>(fmt, bb, staging, M->data, (long long)(nbytes / bb), 1);
     cudaError_t e = cudaDeviceSynchronize();
     cudaFree(staging);

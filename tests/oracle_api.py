@@ -14,9 +14,13 @@ ORACLE_DIR = os.path.join(ROOT, "oracle")
 ORACLE_SO = os.path.join(ORACLE_DIR, "liboracle.so")
 
 F32, F16, BF16, Q4_0, Q8_0, Q4_K, Q6_K, TRI = 0, 1, 2, 3, 4, 6, 7, 8
+Q2_K, I8_BLK, Q3_K, Q5_K, B1, B1X, T1E, T1E_LO = 5, 9, 10, 11, 12, 13, 14, 15
+RAW_FORMATS = (Q2_K, Q3_K, Q5_K, I8_BLK, B1, B1X, T1E, T1E_LO)
 TRI_LEGACY = 108
 BLOCK_SPEC = {F32: (1, 4), F16: (1, 2), BF16: (1, 2), Q4_0: (32, 20), Q8_0: (32, 34),
-              Q4_K: (256, 144), Q6_K: (256, 210), TRI: (64, 18)}
+              Q4_K: (256, 144), Q6_K: (256, 210), TRI: (64, 18), Q2_K: (256, 84), Q3_K: (256, 110),
+              Q5_K: (256, 176), I8_BLK: (256, 258), B1: (256, 34), B1X: (256, 47), T1E: (256, 40),
+              T1E_LO: (256, 32)}
 APPLY_NORM, ADD_RESIDUAL = 1, 2
 
 _lib = None
