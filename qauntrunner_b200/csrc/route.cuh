@@ -788,39 +788,35 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
         }
     }
     __syncthreads();
-    // selection by rank: candidate c of token t has rank #{j : key_j > key_c
-    // or (key_j == key_c and j < c)} (value descending, index ascending, a
-    // total order), computed by every thread for its candidates in a short
-    // loop (the tail runs once per forward on one CTA: compact code matters
-    // more than instruction count); ranks below k name the selected experts
+    // selection, one warp per token: lane l holds the keys of candidates
+    // l, l+32, ... in registers; k rounds of "largest key, then lowest index"
+    // (value descending, index ascending: a total order) by two warp
+    // reductions each, with no block-wide synchronisation
     int* rsel = asg + 32;   // [T][kMaxK] (the weight scratch follows)
-    // a thread ranks up to 4 candidates of one token at once (c = tid + 128 m),
-    // each key load shared by them, four independent loads in flight
-    constexpr int CM = kMaxE / kRouteThreads;
-#pragma unroll 1
-    for (int t = 0; t < T; t++) {
+    if (warp < T) {
+        const int t = warp;
         const uint32_t* kt = key + (size_t)t * E;
-        uint32_t kc[CM];
-        int rank[CM];
+        uint32_t kc[J];   // key + 1 of candidate lane + 32 i (0: none or taken)
 #pragma unroll
-        for (int m = 0; m < CM; m++) {
-            const int c = tid + kRouteThreads * m;
-            kc[m] = c < E ? kt[c] : 0u;
-            rank[m] = 0;
+        for (int i = 0; i < J; i++) {
+            const int c = lane + 32 * i;
+            kc[i] = c < E ? kt[c] + 1u : 0u;   // keys are below 0xFF800001: no wrap
         }
-        const int ncm = (E - tid + kRouteThreads - 1) / kRouteThreads;   // candidates of this thread
-#pragma unroll 4
-        for (int j = 0; j < E; j++) {
-            const uint32_t q = kt[j];
+#pragma unroll 1
+        for (int r = 0; r < k; r++) {
+            uint32_t bk = 0u;
+            int bi = 0;
 #pragma unroll
-            for (int m = 0; m < CM; m++) {
-                const int c = tid + kRouteThreads * m;
-                rank[m] += (q > kc[m] || (q == kc[m] && j < c)) ? 1 : 0;
-            }
+            for (int i = 0; i < J; i++)
+                if (kc[i] > bk) { bk = kc[i]; bi = i; }   // strict: the lowest i (index) among equal keys
+            const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+            const uint32_t wc = __reduce_min_sync(0xffffffffu, bk == wk ? (uint32_t)(lane + 32 * bi) : 0xffffffffu);
+            const bool mine = (int)wc - 32 * bi == lane && bk == wk;   // the owner drops the winner
+#pragma unroll
+            for (int i = 0; i < J; i++)
+                if (mine && i == bi) kc[i] = 0u;
+            if (lane == 0) rsel[t * kMaxK + r] = (int)wc;
         }
-#pragma unroll
-        for (int m = 0; m < CM; m++)
-            if (m < ncm && rank[m] < k) rsel[t * kMaxK + rank[m]] = tid + kRouteThreads * m;
     }
     __syncthreads();
     if (warp < T) {
@@ -847,16 +843,14 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
     }
     for (int a = n + tid; a < 32; a += kRouteThreads) asg[a] = 0x7fffffff;   // padding sorts last
     __syncthreads();
-    int av[32];
-#pragma unroll
-    for (int q = 0; q < 8; q++) {
-        const int4 v = reinterpret_cast<const int4*>(asg)[q];
-        av[4 * q] = v.x; av[4 * q + 1] = v.y; av[4 * q + 2] = v.z; av[4 * q + 3] = v.w;
-    }
+    // Compact loops from here on (not unrolled): this code runs on one CTA
+    // once per forward, usually with its instructions cold in every cache, so
+    // its length costs more than its instruction count.
+#pragma unroll 1
     for (int e = tid; e <= E; e += kRouteThreads) {
         int c = 0;
-#pragma unroll
-        for (int a = 0; a < 32; a++) c += av[a] < e ? 1 : 0;
+#pragma unroll 1
+        for (int a = 0; a < n; a++) c += asg[a] < e ? 1 : 0;
         p.offsets[e] = c;
     }
     if (warp == 0) {
@@ -867,10 +861,11 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
         const bool local = a < n && e >= p.first_expert && e < p.first_expert + p.n_local;
         const unsigned firsts = __ballot_sync(0xffffffffu, first && local);
         int below = 0, dbelow = 0;
-#pragma unroll
-        for (int b = 0; b < 32; b++) {
-            below += av[b] < e ? 1 : 0;
-            dbelow += ((firsts >> b) & 1u) && av[b] < e ? 1 : 0;
+#pragma unroll 1
+        for (int b = 0; b < n; b++) {
+            const int eb = asg[b];
+            below += eb < e ? 1 : 0;
+            dbelow += ((firsts >> b) & 1u) && eb < e ? 1 : 0;
         }
         if (a < n) {
             const int pos = below + __popc(peers & ((1u << lane) - 1));   // stable inside an expert
