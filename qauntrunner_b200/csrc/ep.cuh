@@ -49,7 +49,7 @@ struct EpMailbox {
     long long out_flag;   // u32 [G]: epoch of the output rows received from rank q
     long long xn;         // f32 [G*T][d] gathered normalised tokens
     long long idx;        // i32 [G*T][k] gathered top-k indices
-    long long y;          // f32 [G][T*k][d] output rows of this rank's tokens, per holder
+    long long y;          // f32 [T*k][d] output rows of this rank's tokens (row t*k + j from its holder)
 };
 
 struct EpPeers {

@@ -597,6 +597,16 @@ struct GemvParams {
     const float* xq_a;
     const float* xq_b;
     int xq_split;
+    // expert parallelism over peer memory, down launches of the streaming
+    // kernel: every routed output row goes straight into its owner's mailbox
+    // (gathered token u = q*ep_T + t, slot j -> row t*k + j of owner q's y
+    // block) and the last consumer warp of the grid raises this rank's output
+    // flag in every owner's mailbox (null ep_base: rows stay in out_routed)
+    const unsigned long long* ep_base;   // [ep_G] mailboxes, mapped here
+    long long ep_y, ep_flag;             // mailbox offsets of the y block and the output flags
+    const uint32_t* ep_epoch;            // this forward's epoch (advanced by its dispatch)
+    uint32_t* ep_cnt;                    // consumer warps done (zero between launches)
+    int ep_G, ep_rank, ep_T;
     // launched as a programmatic dependent: 1 = wait for the predecessor
     // before anything, 2 = the producer streams weights before the wait (the
     // routing it reads was final two launches earlier; only the activations

@@ -490,6 +490,11 @@ __device__ __forceinline__ void stream_reduce(const GemvParams& p, const StreamC
         const float res = M == 2 ? swiglu(v[0], v[M - 1], p.limit) : v[0];
         const int tk = j.t0 + q;
         float* orow = j.shared ? p.out_shared + (size_t)tk * p.rows : p.out_routed + (size_t)(j.off + tk) * p.rows;
+        if (M == 1 && p.ep_base && !j.shared) {
+            // the owner's row of this assignment (a = u*k + s, u = owner*T + t)
+            const int a = p.perm[j.off + tk], u = a / p.k, s = a - u * p.k, own = u / p.ep_T, t = u - own * p.ep_T;
+            orow = reinterpret_cast<float*>(reinterpret_cast<char*>(p.ep_base[own]) + p.ep_y) + ((size_t)t * p.k + s) * p.rows;
+        }
         orow[(j.rg * r16 + i) * OUT + r] = res;
     }
     __syncwarp();
@@ -570,6 +575,24 @@ __device__ __forceinline__ void stream_issue(const StreamSeg& g, const MatDev* m
         const MatDev mat = md[m];
         bulk_g2s(st + (size_t)c * run, mat.base + ((long long)tile * nsb + (long long)part * g.sbs) * g.cb,
                  (uint32_t)run, bar);
+    }
+}
+
+// Expert parallelism (down launches that store into the owners' mailboxes):
+// a consumer warp that has finished all its work counts itself; the last of
+// the grid's cw * gridDim.x consumer warps makes every row store of the grid
+// visible system-wide and raises this rank's output flag at every owner.
+__device__ __forceinline__ void stream_ep_done(const GemvParams& p, int cw, int lane) {
+    __syncwarp();
+    if (lane != 0) return;
+    __threadfence_system();
+    if (atomicAdd(p.ep_cnt, 1u) != (uint32_t)(cw * gridDim.x) - 1u) return;
+    *p.ep_cnt = 0u;
+    __threadfence_system();
+    const uint32_t epoch = *p.ep_epoch;
+    for (int q = 0; q < p.ep_G; q++) {
+        uint32_t* f = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(p.ep_base[q]) + p.ep_flag) + p.ep_rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
     }
 }
 
@@ -762,7 +785,10 @@ expert_stream_kernel(GemvParams p, StreamConfig cfg, int32_t* err) {
         const uint32_t ph = (uint32_t)(k / S) & 1u;
         if (!warp_wait(&full[s], ph, abort_flag, err)) return;
         const int* h = hdr + s * kStreamHdrInts;
-        if (h[0] >= n_items) break;
+        if (h[0] >= n_items) {
+            if (M == 1 && p.ep_base) stream_ep_done(p, CW, lane);
+            break;
+        }
         const int seg = h[5], part = h[6];
         const StreamSeg& g = seg ? cfg.seg[1] : cfg.seg[0];
         if (part == 0) {

@@ -1184,6 +1184,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     const bool u_gu = L->umma_ok && (large || L->umma_forced_gu);
     const bool u_dn = L->umma_ok && (large || L->umma_forced_dn);
     const int Tk = Tx * k;
+    bool ep_stored = false;   // the down kernel stored the output rows into the owners' mailboxes
     if (u_gu || u_dn) {
         // work lists of both stages from the dispatch's slot table; f16
         // activations in dispatch order for a grouped gate/up
@@ -1303,6 +1304,20 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                 if (rc) return rc;
             }
         }
+        // expert parallelism over peer memory: the streaming down kernel stores
+        // the routed output rows into their owners' mailboxes and raises the
+        // output flags itself
+        if (!gu && ep && L->p2p && imma_usable(fr, gp.rows, gp.cols, false)) {
+            gp.ep_base = L->peer_base;
+            gp.ep_y = L->mb.y;
+            gp.ep_flag = L->mb.out_flag;
+            gp.ep_epoch = L->ep_state;
+            gp.ep_cnt = L->ep_state + 1 + G;
+            gp.ep_G = G;
+            gp.ep_rank = L->rank;
+            gp.ep_T = T;
+            ep_stored = true;
+        }
         if (pair) {
             gp.mode = 0;
             gp.ctr = &L->sched->ctr[gu ? 0 : 2];
@@ -1322,6 +1337,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             if (rc) return rc;
             gp.mode = 2;
             gp.ctr = &L->sched->ctr[gu ? 1 : 3];
+            gp.ep_base = nullptr;   // shared rows stay here
             rc = launch_gemv(fs, gu, nt, gp, L->sm_count, &L->sched->err, s);
             if (rc) return rc;
             nl += 2;
@@ -1332,11 +1348,15 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         // expert output rows straight into the owners' mailboxes; the owner
         // combines in slot order once every holder's rows are in
         const qrm::EpPeers pe = ep_peers(L);
-        // grid for the largest possible number of local assignments
-        const long long n4 = (long long)Tx * k * (d / 4);
-        const int pgrid = (int)std::max<long long>(1, std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 4));
-        qrm::ep_push_outputs_kernel<<<pgrid, 256, 0, s>>>(L->y, L->perm, L->offsets + E, T, k, d, pe);
-        QRM_CUDA(cudaGetLastError());
+        if (!ep_stored) {
+            // grid for the largest possible number of local assignments
+            const long long n4 = (long long)Tx * k * (d / 4);
+            const int pgrid =
+                (int)std::max<long long>(1, std::min<long long>((n4 + 255) / 256, (long long)L->sm_count * 4));
+            qrm::ep_push_outputs_kernel<<<pgrid, 256, 0, s>>>(L->y, L->perm, L->offsets + E, T, k, d, pe);
+            QRM_CUDA(cudaGetLastError());
+            nl++;
+        }
         mark(-1, 5);
         const long long m4 = (long long)T * (d / 4);
         const int grid = (int)std::min<long long>((m4 + 255) / 256, (long long)L->sm_count * 16);
@@ -1345,7 +1365,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                                                     reinterpret_cast<const uint32_t*>(L->mbox + L->mb.out_flag),
                                                     L->ep_state, G, &L->sched->err);
         QRM_CUDA(cudaGetLastError());
-        nl += 2;
+        nl++;
         combined = true;
     } else if (ep) {
         // expert output rows back to the token owners; the owner combines in slot order

@@ -65,6 +65,37 @@ __device__ __forceinline__ float lane_chain(const float* __restrict__ a, const f
     return acc;
 }
 
+// lane_chain(a, a, ...) with one load per step: acc + sum of a[i]*a[i] over
+// i = lane, lane+8, ... < n8, in that order (the RMSNorm sum of squares,
+// TransformerOps.cs:18-24)
+__device__ __forceinline__ float lane_chain_sq(const float* __restrict__ a, int lane, int n8, float acc) {
+    int i = 0;
+    if (n8 >= 256) {
+        float ra[16], p[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) { const float v = a[8 * u + lane]; p[u] = __fmul_rn(v, v); }
+#pragma unroll
+        for (int u = 0; u < 16; u++) ra[u] = a[128 + 8 * u + lane];
+        for (i = 256; i + 128 <= n8; i += 128) {
+#pragma unroll
+            for (int u = 0; u < 16; u++) {
+                acc = __fadd_rn(acc, p[u]);
+                p[u] = __fmul_rn(ra[u], ra[u]);
+                ra[u] = a[i + 8 * u + lane];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+            acc = __fadd_rn(acc, p[u]);
+            p[u] = __fmul_rn(ra[u], ra[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 16; u++) acc = __fadd_rn(acc, p[u]);
+    }
+    for (; i < n8; i += 8) acc = __fadd_rn(acc, __fmul_rn(a[i + lane], a[i + lane]));
+    return acc;
+}
+
 // Sequential HSum of eight lane accumulators (SimdMath.HSum).
 __device__ __forceinline__ float hsum8_seq(const float* a) {
     float s = 0.f;
@@ -151,7 +182,7 @@ route_small_kernel(RouteParams p) {
     if (norm_thread) {                                                            \
         const float* xr = X + nt * d + 8 * (C) * chg;                             \
         int stop = min(d8, 8 * ((C) + 1) * chg) - 8 * (C) * chg;                  \
-        if (stop > 0) acc = lane_chain(xr, xr, nj, stop, acc);                    \
+        if (stop > 0) acc = lane_chain_sq(xr, nj, stop, acc);                         \
     }
     QRM_ROUTE_CHUNK(0)
     QRM_ROUTE_CHUNK(1)
@@ -217,7 +248,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     const float* xr = x + (size_t)warp * d;
     const int d8 = d / 8 * 8;
     float acc = 0.f;
-    if (lane < 8 && d >= 8) acc = lane_chain(xr, xr, lane, d8, 0.f);
+    if (lane < 8 && d >= 8) acc = lane_chain_sq(xr, lane, d8, 0.f);
     float a[8];
 #pragma unroll
     for (int j = 0; j < 8; j++) a[j] = __shfl_sync(0xffffffffu, acc, j);
@@ -951,7 +982,7 @@ route_fused_kernel(RouteFusedParams fp) {
     // chain group g (token or (token, expert)) -> warp g % 4, lanes 8*(g/4)..+7,
     // so the groups issue from different schedulers
     const int cg = (tid >> 5) + 4 * ((tid & 31) >> 3), cj = tid & 7;
-    if (norm && cg < T) red[cg * 8 + cj] = lane_chain(X + cg * d, X + cg * d, cj, d8, 0.f);
+    if (norm && cg < T) red[cg * 8 + cj] = lane_chain_sq(X + cg * d, cj, d8, 0.f);
     __syncthreads();
     if (norm) {
         if (tid < T) {
