@@ -1142,7 +1142,10 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
     if (ep && L->p2p) {
         // records straight into every rank's mailbox; the dispatch waits for all of them
         const qrm::EpPeers pe = ep_peers(L);
-        const int nb = (int)std::min<long long>(((long long)T * d / 4 + 1023) / 1024, 16);
+        // blocks per destination: one per 1024 float4 of the rows, up to two
+        // waves of the GPU over all destinations (large batches move tens of MB)
+        const int nb = (int)std::max<long long>(
+            1, std::min<long long>(((long long)T * d / 4 + 1023) / 1024, std::max(16, 2 * L->sm_count / G)));
         qrm::ep_push_records_kernel<<<G * nb, 256, 0, s>>>(xn, topk_idx, T, d, k, E / G, pe);
         QRM_CUDA(cudaGetLastError());
         qrm::TopkParams tpx{L->logits, nullptr, L->idx_all, nullptr, Tx, E, k, 0, 1.f};
