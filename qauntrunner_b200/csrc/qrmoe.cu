@@ -99,6 +99,39 @@ int gemv_occupancy(int nt, int block) {
 constexpr int kRGateUp = 4;   // rows per gate/up item (x2 matrices)
 constexpr int kRDown = 8;     // rows per down item
 
+// Router logits tiles (route.cuh): every instantiation gets its shared memory
+// limit once; the launch takes the largest tile whose grid covers the SMs.
+static bool lm_tiles_setup() {
+    bool ok = true;
+#define QRM_LM_SETUP(TT, TE, NTG, NEG, KC, NS)                                                           \
+    ok = ok && cudaFuncSetAttribute(qrm::logits_lm_kernel<TT, TE, NTG, NEG, KC, NS>,                     \
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,                         \
+                                    (int)qrm::LMTile<TT, TE, NTG, NEG, KC, NS>::smem()) == cudaSuccess;
+    QRM_LM_TILES(QRM_LM_SETUP)
+#undef QRM_LM_SETUP
+    return ok;
+}
+
+static void launch_logits_lm(const float* xn, const float* router_lm, const float* offset, float* logits, int T, int d,
+                             int E, int sm_count, cudaStream_t s) {
+    bool done = false;
+#define QRM_LM_COUNT(TT, TE, NTG, NEG, KC, NS) +1
+    int left = 0 QRM_LM_TILES(QRM_LM_COUNT);   // the last tile runs whatever its grid
+#undef QRM_LM_COUNT
+#define QRM_LM_LAUNCH(TT, TE, NTG, NEG, KC, NS)                                                          \
+    if (!done) {                                                                                          \
+        using Tl = qrm::LMTile<TT, TE, NTG, NEG, KC, NS>;                                                 \
+        const dim3 grid((T + Tl::kT - 1) / Tl::kT, (E + Tl::kE - 1) / Tl::kE);                          \
+        if (--left == 0 || (long long)grid.x * grid.y >= sm_count) {                                      \
+            qrm::logits_lm_kernel<TT, TE, NTG, NEG, KC, NS><<<grid, Tl::kThreads, Tl::smem(), s>>>(       \
+                xn, router_lm, offset, logits, T, d, E);                                                  \
+            done = true;                                                                                  \
+        }                                                                                                 \
+    }
+    QRM_LM_TILES(QRM_LM_LAUNCH)
+#undef QRM_LM_LAUNCH
+}
+
 // Bulk-copy staged kernel: G consumer groups, NT tokens per pass.
 template <int FMT, int M, int R, int NT, int G>
 int launch_tma_g(const qrm::GemvParams& p, const qrm::TmaConfig& cfg, int cwg, int sm_count, int32_t* err,
@@ -879,8 +912,12 @@ static int create_layer(const qrm_layer_desc* desc, int rank, int world, const v
     if (cudaFuncSetAttribute(qrm::route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(qrm::route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess ||
         cudaFuncSetAttribute(qrm::dispatch_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess ||
-        cudaFuncSetAttribute(qrm::logits_lm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)qrm::logits_lm_smem()) != cudaSuccess)
+        cudaFuncSetAttribute(qrm::topk_dispatch_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)qrm::topk_dispatch_smem(256, qrm::kFusedTopkMaxT)) != cudaSuccess ||
+        cudaFuncSetAttribute(qrm::topk_dispatch_kernel<qrm::kMaxE / 32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)qrm::topk_dispatch_smem(qrm::kMaxE, qrm::kFusedTopkMaxT)) != cudaSuccess ||
+        cudaFuncSetAttribute(qrm::rmsnorm_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess ||
+        !lm_tiles_setup())
         return bail(fail(QRM_E_CUDA, "kernel attribute"));
     *out = L;
     return QRM_OK;
@@ -1103,27 +1140,35 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         } else {
             if (flags & QRM_APPLY_NORM) {
                 nl++;
-                qrm::rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, L->norm_w, L->xn, T, d, D.rms_eps);
+                if ((reinterpret_cast<uintptr_t>(x) & 15) == 0 && d % 4 == 0 &&
+                    qrm::rmsnorm_row_smem(d) <= 200 * 1024)
+                    qrm::rmsnorm_row_kernel<<<T, qrm::kNormRowThreads, qrm::rmsnorm_row_smem(d), s>>>(
+                        x, L->norm_w, L->xn, d, D.rms_eps);
+                else
+                    qrm::rmsnorm_kernel<<<(T + 7) / 8, 256, 0, s>>>(x, L->norm_w, L->xn, T, d, D.rms_eps);
             } else {
                 xn = x;
             }
-            dim3 grid((T + qrm::kLMT - 1) / qrm::kLMT, (E + qrm::kLME - 1) / qrm::kLME);
             nl++;
-            qrm::logits_lm_kernel<<<grid, qrm::kLMThreads, qrm::logits_lm_smem(), s>>>(
-                xn, L->router_lm, L->has_offset ? L->offset : nullptr, L->logits, T, d, E);
+            launch_logits_lm(xn, L->router_lm, L->has_offset ? L->offset : nullptr, L->logits, T, d, E, L->sm_count, s);
         }
         QRM_CUDA(cudaGetLastError());
         mark(1, -1);
-        // top-k and dispatch (fused into one single-CTA kernel for T <= 32)
-        const bool fused = T <= qrm::kFusedTopkMaxT;
-        if (!fused) {
+        // top-k and dispatch (one single-CTA kernel for T <= 32)
+        if (T <= qrm::kFusedTopkMaxT) {
+            mark(2, -1);
             nl++;
-            qrm::topk_kernel<<<(T + 3) / 4, 128, 0, s>>>(tp);
+            const size_t sm = qrm::topk_dispatch_smem(E, T);
+            if (E <= 256) qrm::topk_dispatch_kernel<8><<<1, qrm::kDispatchThreads, sm, s>>>(dp, tp);
+            else qrm::topk_dispatch_kernel<qrm::kMaxE / 32><<<1, qrm::kDispatchThreads, sm, s>>>(dp, tp);
+        } else {
+            nl += 2;
+            if (E <= 256) qrm::topk_kernel<8><<<(T + 3) / 4, 128, 0, s>>>(tp);
+            else qrm::topk_kernel<qrm::kMaxE / 32><<<(T + 3) / 4, 128, 0, s>>>(tp);
             QRM_CUDA(cudaGetLastError());
+            mark(2, -1);
+            qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E), s>>>(dp);
         }
-        mark(2, -1);
-        nl++;
-        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, T, fused), s>>>(dp, tp, fused ? 1 : 0);
         QRM_CUDA(cudaGetLastError());
         mark(3, 1);
     }
@@ -1148,11 +1193,10 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
             1, std::min<long long>(((long long)T * d / 4 + 1023) / 1024, std::max(16, 2 * L->sm_count / G)));
         qrm::ep_push_records_kernel<<<G * nb, 256, 0, s>>>(xn, topk_idx, T, d, k, E / G, pe);
         QRM_CUDA(cudaGetLastError());
-        qrm::TopkParams tpx{L->logits, nullptr, L->idx_all, nullptr, Tx, E, k, 0, 1.f};
         qrm::DispatchParams dpx{L->idx_all, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched,
                                 Tx, k, E, L->first_expert, L->n_local, shared ? 1 : 0,
                                 reinterpret_cast<const uint32_t*>(L->mbox + L->mb.rec_flag), L->ep_state, G, Tsh, 1};
-        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, Tx, false), s>>>(dpx, tpx, 0);
+        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E), s>>>(dpx);
         QRM_CUDA(cudaGetLastError());
         nl += 2;
         mark(-1, 2);
@@ -1168,12 +1212,11 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         qrm::ep_unpack_records_kernel<<<grid, 256, 0, s>>>(L->rec_all, Tx, d, k, L->xn_all, L->idx_all);
         QRM_CUDA(cudaGetLastError());
         // dispatch of all ranks' assignments; the active list holds this rank's experts
-        qrm::TopkParams tpx{L->logits, nullptr, L->idx_all, nullptr, Tx, E, k, 0, 1.f};
         qrm::DispatchParams dpx{L->idx_all, L->perm, L->inv_perm, L->pos_tok, L->slot_info, L->offsets, L->active, L->sched,
                                 Tx, k, E, L->first_expert, L->n_local, shared ? 1 : 0};
         dpx.T_sh = Tsh;
         dpx.local_only = 1;
-        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E, Tx, false), s>>>(dpx, tpx, 0);
+        qrm::dispatch_kernel<<<1, qrm::kDispatchThreads, qrm::dispatch_smem(E), s>>>(dpx);
         QRM_CUDA(cudaGetLastError());
         nl += 3;
         mark(-1, 2);

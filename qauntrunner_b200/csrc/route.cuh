@@ -239,7 +239,63 @@ route_small_kernel(RouteParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// Large-T RMSNorm: one warp per token; lanes 0..7 run the eight chains.
+// RMSNorm of one token row per CTA (256 threads): the row and the norm
+// weights are copied into shared memory with every 16-byte piece in flight
+// at once, then lanes 0..7 of warp 0 run the eight chains from there (a
+// chain of d/8 dependent adds fed from DRAM would wait on the memory latency
+// every few steps), and all threads write the scaled row.  x 16-byte aligned,
+// d % 4 == 0.
+constexpr int kNormRowThreads = 256;
+inline size_t rmsnorm_row_smem(int d) { return sizeof(float) * 2 * (size_t)d; }
+
+__global__ void __launch_bounds__(kNormRowThreads) rmsnorm_row_kernel(const float* __restrict__ x,
+                                                                      const float* __restrict__ w,
+                                                                      float* __restrict__ xn, int d, float eps) {
+    extern __shared__ __align__(16) float nrm[];   // [d] row | [d] weights
+    __shared__ float sc;
+    const int tid = threadIdx.x, t = blockIdx.x;
+    const float* xr = x + (size_t)t * d;
+    float* sw = nrm + d;
+    for (int i = tid; i < d / 4; i += kNormRowThreads) {
+        cp_async16(nrm + 4 * i, xr + 4 * i);
+        if (w) cp_async16(sw + 4 * i, w + 4 * i);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    if (tid < 32) {
+        const int d8 = d / 8 * 8;
+        float acc = 0.f;
+        if (tid < 8 && d >= 8) acc = lane_chain_sq(nrm, tid, d8, 0.f);
+        float a[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) a[j] = __shfl_sync(0xffffffffu, acc, j);
+        if (tid == 0) {
+            float ss = 0.f;
+            int i0 = 0;
+            if (d >= 8) { ss = hsum8_seq(a); i0 = d8; }
+            for (int i = i0; i < d; i++) ss = __fadd_rn(ss, __fmul_rn(nrm[i], nrm[i]));
+            sc = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d), eps)));
+        }
+    }
+    __syncthreads();
+    const float scale = sc;
+    float* o = xn + (size_t)t * d;
+    for (int i = tid; i < d / 4; i += kNormRowThreads) {
+        float4 v = reinterpret_cast<const float4*>(nrm)[i];
+        v.x = __fmul_rn(v.x, scale); v.y = __fmul_rn(v.y, scale);
+        v.z = __fmul_rn(v.z, scale); v.w = __fmul_rn(v.w, scale);
+        if (w) {
+            const float4 g = reinterpret_cast<const float4*>(sw)[i];
+            v.x = __fmul_rn(v.x, g.x); v.y = __fmul_rn(v.y, g.y);
+            v.z = __fmul_rn(v.z, g.z); v.w = __fmul_rn(v.w, g.w);
+        }
+        reinterpret_cast<float4*>(o)[i] = v;
+    }
+}
+
+// RMSNorm for any row alignment: one warp per token; lanes 0..7 run the eight
+// chains straight from global memory.
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                float* __restrict__ xn, int T, int d, float eps) {
     int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -269,13 +325,6 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 // Top-k: one warp per token.
 // Ranking = Array.Sort(idx, (a, b) => v[b].CompareTo(v[a])): value
 // descending, NaN last; exact ties by index ascending.
-__device__ __forceinline__ bool rank_before(float va, int ia, float vb, int ib) {
-    bool na = isnan(va), nb = isnan(vb);
-    if (na != nb) return nb;
-    if (!na && va != vb) return va > vb;
-    return ia < ib;
-}
-
 constexpr int kMaxE = 512;   // GlmMoeFfn caps n_experts at 512 (StreamingEngine.cs:733)
 constexpr int kMaxK = 8;     // StreamingEngine.cs:628
 
@@ -289,94 +338,150 @@ struct TopkParams {
     float routed_scale;
 };
 
-// One warp ranks the E scores of token t.  v (ranking values) and s (weight
-// sources) are this warp's shared scratch of kMaxE floats each.
-__device__ __forceinline__ void topk_token(const TopkParams& p, int t, int lane, float* v, float* s) {
-    const int E = p.E, k = p.k;
-    const float* lg = p.logits + (size_t)t * E;   // read through L2: other CTAs may have written it
-    if (!p.sigmoid) {
-        // max from float.MinValue; comparisons skip NaN like the reference loop
-        float mx = -3.40282347e+38f;
-        for (int i = lane; i < E; i += 32) { float a = __ldcg(lg + i); if (a > mx) mx = a; }
+// order-preserving key of a ranking value: larger value -> larger key, NaN
+// lowest, -0 == +0 (Array.Sort with v[b].CompareTo(v[a]), value descending)
+__device__ __forceinline__ uint32_t rank_key(float v) {
+    if (isnan(v)) return 0u;
+    const uint32_t u = __float_as_uint(__fadd_rn(v, 0.f));   // -0 -> +0
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// k rounds of "largest key, then lowest index" over the candidates whose
+// keys + 1 lane l holds in kc (candidate l + 32 i; 0 = none or taken): value
+// descending, index ascending, a total order, by two warp reductions per
+// round.  Returns the r-th winner on lane r < k.
+template <int J>
+__device__ __forceinline__ int warp_select(uint32_t (&kc)[J], int k, int lane) {
+    int sel = -1;
+#pragma unroll 1
+    for (int r = 0; r < k; r++) {
+        uint32_t bk = 0u;
+        int bi = 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) { float b = __shfl_xor_sync(0xffffffffu, mx, o); if (b > mx) mx = b; }
-        for (int i = lane; i < E; i += 32) s[i] = expf_glibc(__fsub_rn(__ldcg(lg + i), mx));
+        for (int i = 0; i < J; i++)
+            if (kc[i] > bk) { bk = kc[i]; bi = i; }   // strict: the lowest i (index) among equal keys
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+        const uint32_t wc = __reduce_min_sync(0xffffffffu, bk == wk ? (uint32_t)(lane + 32 * bi) : 0xffffffffu);
+        const bool mine = (int)wc - 32 * bi == lane && bk == wk;   // the owner drops the winner
+#pragma unroll
+        for (int i = 0; i < J; i++)
+            if (mine && i == bi) kc[i] = 0u;
+        if (lane == r) sel = (int)wc;
+    }
+    return sel;
+}
+
+// Top-k of token t by one warp.  Scores (softmax: StreamingEngine.cs:642-647,
+// max from float.MinValue skipping NaN, sequential sum; GLM sigmoid + bias:
+// 730-767) go to the warp's shared scratch sv (weight sources) and key
+// (ranking keys), E entries each; lane l then holds the keys of candidates l,
+// l+32, ... in registers for the selection (SelectTopK 801-810 /
+// SelectTopKIndices 793-799), and the weights are normalised in rank order
+// (the sum sequential on one lane's shuffles).  Writes topk_idx / topk_w of
+// token t and returns the r-th expert on lane r < k (-1 on the other lanes).
+// All loads are issued first (one memory round trip); the loops over E are
+// then kept rolled: this code runs once per forward, usually with its
+// instructions cold in every cache, so its length costs more than its
+// instruction count.  tab: the exp table in shared memory.
+template <int J>
+__device__ int topk_warp(const TopkParams& tp, int t, int lane, float* sv, uint32_t* key, const uint64_t* tab) {
+    const int E = tp.E, k = tp.k;
+    const float* lg = tp.logits + (size_t)t * E;   // read through L2: other CTAs wrote it
+    {   // logits into sv, bias bits into key
+        float lv[J], bv[J];
+#pragma unroll
+        for (int i = 0; i < J; i++) {
+            const int c = lane + 32 * i;
+            lv[i] = c < E ? __ldcg(lg + c) : 0.f;
+            bv[i] = c < E && tp.sigmoid && tp.bias ? tp.bias[c] : 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < J; i++) {
+            const int c = lane + 32 * i;
+            if (c < E) {
+                sv[c] = lv[i];
+                key[c] = __float_as_uint(bv[i]);
+            }
+        }
+    }
+    if (!tp.sigmoid) {
+        float mx = -3.40282347e+38f;
+#pragma unroll 1
+        for (int i = lane; i < E; i += 32) {
+            const float a = sv[i];
+            if (a > mx) mx = a;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) { const float b = __shfl_xor_sync(0xffffffffu, mx, o); if (b > mx) mx = b; }
+#pragma unroll 1
+        for (int i = lane; i < E; i += 32) sv[i] = expf_glibc_t(__fsub_rn(sv[i], mx), tab);
         __syncwarp();
         float sum = 0.f;
-        if (lane == 0) {
+        if (lane == 0) {   // sequential sum in index order
             int i = 0;
+#pragma unroll 1
             for (; i + 16 <= E; i += 16) {
                 float q[16];
 #pragma unroll
-                for (int u = 0; u < 16; u++) q[u] = s[i + u];
+                for (int u = 0; u < 16; u++) q[u] = sv[i + u];
 #pragma unroll
                 for (int u = 0; u < 16; u++) sum = __fadd_rn(sum, q[u]);
             }
-            for (; i < E; i++) sum = __fadd_rn(sum, s[i]);
+#pragma unroll 1
+            for (; i < E; i++) sum = __fadd_rn(sum, sv[i]);
         }
-        sum = __shfl_sync(0xffffffffu, sum, 0);
-        float inv = __fdiv_rn(1.f, sum);
-        for (int i = lane; i < E; i += 32) { float q = __fmul_rn(s[i], inv); s[i] = q; v[i] = q; }
-    } else {
+        const float inv = __fdiv_rn(1.f, __shfl_sync(0xffffffffu, sum, 0));
+        __syncwarp();
+#pragma unroll 1
         for (int i = lane; i < E; i += 32) {
-            float sg = __fdiv_rn(1.f, __fadd_rn(1.f, expf_glibc(-__ldcg(lg + i))));
-            s[i] = sg;
-            v[i] = p.bias ? __fadd_rn(sg, p.bias[i]) : sg;
+            const float q = __fmul_rn(sv[i], inv);
+            sv[i] = q;
+            key[i] = rank_key(q);
+        }
+    } else {
+#pragma unroll 1
+        for (int i = lane; i < E; i += 32) {
+            const float sg = __fdiv_rn(1.f, __fadd_rn(1.f, expf_glibc_t(-sv[i], tab)));
+            sv[i] = sg;
+            key[i] = rank_key(tp.bias ? __fadd_rn(sg, __uint_as_float(key[i])) : sg);
         }
     }
-    __syncwarp();
-    // k rounds of warp argmax under the reference ordering; lane owns i = lane + 32j
-    uint32_t taken = 0;
-    int sel[kMaxK];
+    uint32_t kc[J];
 #pragma unroll
-    for (int r = 0; r < kMaxK; r++) {
-        if (r < k) {
-            float bv = 0.f;
-            int bi = -1;
-            for (int j = 0, i = lane; i < E; j++, i += 32) {
-                if (taken & (1u << j)) continue;
-                float a = v[i];
-                if (bi < 0 || rank_before(a, i, bv, bi)) { bv = a; bi = i; }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (oi >= 0 && (bi < 0 || rank_before(ov, oi, bv, bi))) { bv = ov; bi = oi; }
-            }
-            sel[r] = bi;
-            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        }
+    for (int i = 0; i < J; i++) {
+        const int c = lane + 32 * i;
+        kc[i] = c < E ? key[c] + 1u : 0u;   // keys are below 0xFF800001: no wrap
     }
-    if (lane == 0) {
-        int32_t* oi = p.topk_idx + (size_t)t * k;
-        float* ow = p.topk_w + (size_t)t * k;
-        if (!p.sigmoid) {
-            float sum = 0.f;
-#pragma unroll
-            for (int r = 0; r < kMaxK; r++) if (r < k) sum = __fadd_rn(sum, s[sel[r]]);
-            if (sum <= 0.f) sum = 1.f;
-#pragma unroll
-            for (int r = 0; r < kMaxK; r++) if (r < k) { oi[r] = sel[r]; ow[r] = __fdiv_rn(s[sel[r]], sum); }
+    const int e = warp_select<J>(kc, k, lane);
+    const float se = lane < k ? sv[e] : 0.f;
+    float sum = 0.f;
+#pragma unroll 1
+    for (int r = 0; r < k; r++) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, se, r));
+    if (lane < k) {
+        float wv;
+        if (!tp.sigmoid) {
+            wv = __fdiv_rn(se, sum <= 0.f ? 1.f : sum);
         } else {
-            float wsum = 0.f;
-#pragma unroll
-            for (int r = 0; r < kMaxK; r++) if (r < k) wsum = __fadd_rn(wsum, s[sel[r]]);
-            float inv2 = __fdiv_rn(1.f, __fadd_rn(wsum, 1e-20f));
-#pragma unroll
-            for (int r = 0; r < kMaxK; r++)
-                if (r < k) { oi[r] = sel[r]; ow[r] = __fmul_rn(__fmul_rn(s[sel[r]], inv2), p.routed_scale); }
+            const float inv2 = __fdiv_rn(1.f, __fadd_rn(sum, 1e-20f));
+            wv = __fmul_rn(__fmul_rn(se, inv2), tp.routed_scale);
         }
+        tp.topk_idx[(size_t)t * k + lane] = e;
+        tp.topk_w[(size_t)t * k + lane] = wv;
     }
+    return e;
 }
 
-__global__ void topk_kernel(TopkParams p) {
-    __shared__ float sv[4][kMaxE];   // 4 warps per CTA
-    __shared__ float sc[4][kMaxE];
+// Top-k for batches above the fused dispatch: one warp per token, 4 per CTA.
+template <int J>
+__global__ void __launch_bounds__(128) topk_kernel(TopkParams p) {
+    __shared__ float sv[4][kMaxE];
+    __shared__ uint32_t key[4][kMaxE];
+    __shared__ uint64_t tab[32];
     const int wib = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < 32) tab[lane] = kExpfTabDev[lane];
+    __syncthreads();
     const int t = blockIdx.x * 4 + wib;
-    if (t >= p.T) return;
-    topk_token(p, t, lane, sv[wib], sc[wib]);
+    if (t < p.T) topk_warp<J>(p, t, lane, sv[wib], key[wib], tab);
 }
 
 // ---------------------------------------------------------------------------
@@ -413,17 +518,12 @@ struct DispatchParams {
 };
 
 constexpr int kDispatchThreads = 1024;
-constexpr int kFusedTopkMaxT = 32;   // fused top-k + dispatch: one warp per token
 
-inline size_t dispatch_smem(int E, int T, bool fused) {
-    size_t b = sizeof(int) * ((size_t)2 * (E + 1) + (size_t)32 * E + 64);
-    if (fused) b += sizeof(float) * (size_t)2 * min(T, kFusedTopkMaxT) * E;
-    return b;
-}
+inline size_t dispatch_smem(int E) { return sizeof(int) * ((size_t)2 * (E + 1) + (size_t)32 * E + 64); }
 
-// Dispatch, one CTA of 1024 threads.  With `fused` (T <= 32) the CTA first
-// runs the top-k of every token (one warp each).
-__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchParams p, TopkParams tp, int fused) {
+// Dispatch, one CTA of 1024 threads (counting sort: per-expert counts, scans,
+// a stable scatter in rounds of 1024 assignments).
+__global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchParams p) {
     extern __shared__ __align__(16) int dsm[];
     const int E = p.E;
     int n = p.T * p.k;
@@ -443,11 +543,6 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
     int* wc = base + (E + 1);        // [32][E]
     int* wsum = wc + 32 * E;         // [64] scan scratch
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (fused) {
-        float* tsc = reinterpret_cast<float*>(wsum + 64);
-        if (warp < p.T) topk_token(tp, warp, lane, tsc + (size_t)warp * 2 * E, tsc + (size_t)warp * 2 * E + E);
-        __syncthreads();
-    }
     for (int e = tid; e <= E; e += kDispatchThreads) cnt[e] = 0;
     __syncthreads();
     const int lo = p.local_only ? p.first_expert : 0, hi = p.local_only ? p.first_expert + p.n_local : E;
@@ -536,6 +631,96 @@ __global__ void __launch_bounds__(kDispatchThreads) dispatch_kernel(DispatchPara
     if (tid == 0 && p.has_shared) p.slot_info[na] = make_int4(E, 0, p.T_sh, 0);
 }
 
+// Top-k and dispatch of a batch of T <= 32 tokens (n = T*k <= 256
+// assignments) in one CTA of 1024 threads: warp t ranks token t
+// (topk_warp), then the dispatch is computed directly, one thread per
+// assignment a (expert e_a): pos(a) = #{b : e_b < e_a} + #{b < a : e_b == e_a}
+// (stable inside an expert), offsets[e] = #{b : e_b < e}; the active list
+// holds the local experts with assignments, ascending.  The same positions,
+// offsets and slots as dispatch_kernel, with rolled loops over 128-bit
+// shared loads and three block barriers (the code runs cold once per forward).
+constexpr int kFusedTopkMaxT = 32;
+
+inline size_t topk_dispatch_smem(int E, int T) { return (size_t)2 * sizeof(float) * min(T, kFusedTopkMaxT) * E; }
+
+template <int J>
+__global__ void __launch_bounds__(kDispatchThreads) topk_dispatch_kernel(DispatchParams p, TopkParams tp) {
+    extern __shared__ __align__(16) float tsm[];   // [T][2][E]: weight sources, keys
+    __shared__ uint64_t tab[32];
+    // assignment arrays padded to a multiple of 4 with INT_MAX (counts nowhere)
+    __shared__ __align__(16) int asg[kFusedTopkMaxT * kMaxK];   // expert of assignment a
+    __shared__ __align__(16) int act[kFusedTopkMaxT * kMaxK];   // expert of a first local assignment, else INT_MAX
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = p.E, k = tp.k, n = tp.T * k, n4 = (n + 3) / 4;
+    if (tid < 32) tab[tid] = kExpfTabDev[tid];
+    if (tid >= n && tid < 4 * n4) asg[tid] = act[tid] = 0x7fffffff;
+    __syncthreads();
+    if (warp < tp.T) {
+        float* sv = tsm + (size_t)warp * 2 * E;
+        const int e = topk_warp<J>(tp, warp, lane, sv, reinterpret_cast<uint32_t*>(sv + E), tab);
+        if (lane < k) asg[warp * k + lane] = e;
+    }
+    __syncthreads();
+    const int4* a4 = reinterpret_cast<const int4*>(asg);
+    const int lo = p.local_only ? p.first_expert : 0, hi = p.local_only ? p.first_expert + p.n_local : E;
+#pragma unroll 1
+    for (int e = tid; e <= E; e += kDispatchThreads) {
+        int c = 0;
+#pragma unroll 2
+        for (int b = 0; b < n4; b++) {
+            const int4 q = a4[b];
+            c += (q.x >= lo && q.x < hi && q.x < e) + (q.y >= lo && q.y < hi && q.y < e) +
+                 (q.z >= lo && q.z < hi && q.z < e) + (q.w >= lo && q.w < hi && q.w < e);
+        }
+        p.offsets[e] = c;
+    }
+    int e = -1, below = 0, rank = 0, cnt = 0;
+    if (tid < n) {
+        e = asg[tid];
+        if (e < 0 || e >= E) atomicOr(&p.sched->err, (int)ERR_BOUNDS);
+        if (e < lo || e >= hi) e = -1;
+        if (e >= 0) {
+#pragma unroll 2
+            for (int b = 0; b < n4; b++) {
+                const int4 q = a4[b];
+                below += (q.x >= lo && q.x < e) + (q.y >= lo && q.y < e) + (q.z >= lo && q.z < e) + (q.w >= lo && q.w < e);
+                cnt += (q.x == e) + (q.y == e) + (q.z == e) + (q.w == e);
+                const int b0 = 4 * b;
+                rank += (b0 < tid && q.x == e) + (b0 + 1 < tid && q.y == e) + (b0 + 2 < tid && q.z == e) +
+                        (b0 + 3 < tid && q.w == e);
+            }
+        }
+    }
+    const bool is_act = e >= 0 && rank == 0 && e >= p.first_expert && e < p.first_expert + p.n_local;
+    if (tid < n) act[tid] = is_act ? e : 0x7fffffff;
+    const int nd = __syncthreads_count(is_act);
+    if (e >= 0) {
+        const int pos = below + rank;
+        p.perm[pos] = tid;
+        p.inv_perm[tid] = pos;
+        p.pos_tok[pos] = tid / k;
+        if (is_act) {
+            const int4* c4 = reinterpret_cast<const int4*>(act);
+            int dbelow = 0;
+#pragma unroll 2
+            for (int b = 0; b < n4; b++) {
+                const int4 q = c4[b];
+                dbelow += (q.x < e) + (q.y < e) + (q.z < e) + (q.w < e);
+            }
+            p.active[dbelow] = e;
+            p.slot_info[dbelow] = make_int4(e, below, cnt, tid / k);
+        }
+    }
+    if (tid == 0) {
+        if (p.has_shared) {
+            p.active[nd] = E;
+            p.slot_info[nd] = make_int4(E, 0, p.T_sh, 0);
+        }
+        p.sched->n_active = nd;
+        for (int q = 0; q < 4; q++) p.sched->ctr[q] = 0;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Lane-major router rows for the fused router: row e is stored as 8 lanes of P
 // floats, lane j holding columns j, j+8, j+16, ... (the columns of one
@@ -599,82 +784,99 @@ __device__ __forceinline__ float lane_chain4(const float* __restrict__ a, const 
 }
 
 // ---------------------------------------------------------------------------
-// Large-T router logits.  CTA tile: 32 tokens x 32 experts, 512 threads;
-// thread (token quad tq, expert quad eq, lane j) runs the 16 chains of lane j
-// for its 4 tokens x 4 experts (SimdMath.DotF32's lane j: acc + w*x over
-// columns j, j+8, ... in order, products and sums rounded separately), so the
-// logits stay bit-exact.  Chunks of kLMC steps (8*kLMC columns) of the token
-// rows (row-major) and of the experts' lane-major router rows (router_lm)
-// stream into shared memory with cp.async, two chunks in flight; a 128-bit
-// load covers four steps of one expert, the token columns of lane j are four
-// conflict-free scalar loads.  16 independent chains per thread keep the FP32
-// pipes busy (the previous 16 x 16 tile with 8 chains and 4-way bank
-// conflicts on the router loads ran at about a fifth of FP32 peak).
-constexpr int kLMT = 32, kLME = 32, kLMC = 16, kLMThreads = 512;
-constexpr int kLMXPitch = 8 * kLMC + 4;   // floats per token row of a chunk
-constexpr int kLMWPitch = kLMC + 4;       // floats per (expert, lane): the 8 lanes start 4 banks apart
-constexpr int kLMBuf = kLMT * kLMXPitch + kLME * 8 * kLMWPitch;   // floats of one chunk buffer
-inline size_t logits_lm_smem() { return sizeof(float) * 2 * kLMBuf; }
+// Router logits for batches beyond the single-launch routers, tiled.  A CTA
+// owns NTG*TT tokens x NEG*TE experts with NTG*NEG*8 threads; thread (token
+// group tg, expert group eg, lane j) runs the TT*TE chains of lane j for its
+// tokens x experts (SimdMath.DotF32's lane j: acc + w*x over columns j, j+8,
+// ... in order, products and sums rounded separately), so the logits stay
+// bit-exact.  Chunks of KC steps (8*KC columns) of the token rows
+// (row-major) and of the experts' lane-major router rows (router_lm) stream
+// into NS shared buffers with cp.async, NS-1 chunks in flight (the router
+// rows come from DRAM after the caches turned over, and a chain consumes a
+// chunk in a fraction of that latency); a 128-bit load covers four steps of
+// one expert, the token columns of lane j are four conflict-free scalar
+// loads (a warp holds one token group, so its expert groups read the same
+// token words).  The host picks the largest tile whose grid still covers the
+// SMs: the T*E*8 chains of d/8 dependent adds cannot be split, so at small T
+// the chains must spread over CTAs, and at large T more chains per thread
+// keep the FP32 pipes busy with fewer shared loads per product.
+template <int TT, int TE, int NTG, int NEG, int KC, int NS>
+struct LMTile {
+    static constexpr int kThreads = NTG * NEG * 8, kT = NTG * TT, kE = NEG * TE;
+    static constexpr int kXPitch = 8 * KC + 4;   // floats per token row of a chunk (4 banks apart)
+    static constexpr int kWPitch = KC + 4;       // floats per (expert, lane): the 8 lanes start 4 banks apart
+    static constexpr int kBuf = kT * kXPitch + kE * 8 * kWPitch;   // floats of one chunk buffer
+    static constexpr size_t smem() { return sizeof(float) * NS * kBuf; }
+    static_assert(NEG % 4 == 0, "a warp spans one token group");
+    static_assert(KC % 4 == 0 && (KC & (KC - 1)) == 0, "chunks of a power-of-two number of 4-step groups");
+    static_assert(NS >= 2 && kT * kE * 8 <= NS * kBuf, "lane sums fit the chunk buffers");
+};
 
-__global__ void __launch_bounds__(kLMThreads, 2)
+template <int TT, int TE, int NTG, int NEG, int KC, int NS>
+__global__ void __launch_bounds__(NTG * NEG * 8, 1024 / (NTG * NEG * 8))
 logits_lm_kernel(const float* __restrict__ xn, const float* __restrict__ router_lm, const float* __restrict__ offset,
                  float* __restrict__ logits, int T, int d, int E) {
+    using Tl = LMTile<TT, TE, NTG, NEG, KC, NS>;
+    constexpr int NT = Tl::kThreads, KT = Tl::kT, KE = Tl::kE, XPt = Tl::kXPitch, WPt = Tl::kWPitch;
+    constexpr int XQ = 2 * KC, WQ = KC / 4;     // 16-byte pieces per token row / per (expert, lane) row
+    constexpr int XP = KT * XQ, WP = KE * 8 * WQ;
     extern __shared__ __align__(16) float lsm[];
-    const int tid = threadIdx.x, j = tid & 7, eq = (tid >> 3) & 7, tq = tid >> 6;
-    const int t0 = blockIdx.x * kLMT, e0 = blockIdx.y * kLME;
+    const int tid = threadIdx.x, j = tid & 7, eg = (tid >> 3) % NEG, tg = tid / (8 * NEG);
+    const int t0 = blockIdx.x * KT, e0 = blockIdx.y * KE;
     const int nm = d / 8, P = route_lane_pitch(d);            // d % 32 == 0: nm % 4 == 0
-    const int nch = (nm + kLMC - 1) / kLMC;
-    // chunk c into buffer b: token rows (32 x 8*kLMC floats) and lane-major
-    // router rows (32 experts x 8 lanes x kLMC floats), 2 + 2 copies of 16 B per thread
-    auto load = [&](int b, int c) {
-        float* X = lsm + b * kLMBuf;
-        float* W = X + kLMT * kLMXPitch;
+    const int nch = (nm + KC - 1) / KC;
+    auto load = [&](int c) {
+        if (c < nch) {
+            float* X = lsm + (c % NS) * Tl::kBuf;
+            float* W = X + KT * XPt;
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int i = tid + u * kLMThreads, r = i >> 5, q = i & 31;     // token row r, 16-byte piece q
-            const int col = 8 * kLMC * c + 4 * q;
-            float* dst = X + r * kLMXPitch + 4 * q;
-            if (t0 + r < T && col < d) cp_async16(dst, xn + (size_t)(t0 + r) * d + col);
-            else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+            for (int u = 0; u < (XP + NT - 1) / NT; u++) {
+                const int i = tid + u * NT, r = i / XQ, q = i % XQ;     // token row r, piece q
+                if (XP % NT == 0 || i < XP) {
+                    const int col = 8 * KC * c + 4 * q;
+                    float* dst = X + r * XPt + 4 * q;
+                    if (t0 + r < T && col < d) cp_async16(dst, xn + (size_t)(t0 + r) * d + col);
+                    else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int i = tid + u * kLMThreads, row = i >> 2, q = i & 3;    // row = expert * 8 + lane
-            const int e = e0 + (row >> 3), m = kLMC * c + 4 * q;
-            float* dst = W + row * kLMWPitch + 4 * q;
-            if (e < E && m < nm) cp_async16(dst, router_lm + ((size_t)e * 8 + (row & 7)) * P + m);
-            else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int u = 0; u < (WP + NT - 1) / NT; u++) {
+                const int i = tid + u * NT, row = i / WQ, q = i % WQ;    // row = expert * 8 + lane
+                if (WP % NT == 0 || i < WP) {
+                    const int e = e0 + (row >> 3), m = KC * c + 4 * q;
+                    float* dst = W + row * WPt + 4 * q;
+                    if (e < E && m < nm) cp_async16(dst, router_lm + ((size_t)e * 8 + (row & 7)) * P + m);
+                    else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
         }
-        cp_async_commit();
+        cp_async_commit();   // empty groups past the end keep the accounting uniform
     };
-    float acc[4][4];
+    float acc[TT][TE];
 #pragma unroll
-    for (int a = 0; a < 4; a++)
+    for (int a = 0; a < TT; a++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) acc[a][b] = 0.f;
-    load(0, 0);
+        for (int b = 0; b < TE; b++) acc[a][b] = 0.f;
+#pragma unroll
+    for (int c = 0; c < NS - 1; c++) load(c);
     for (int c = 0; c < nch; c++) {
-        if (c + 1 < nch) {
-            load((c + 1) & 1, c + 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
+        load(c + NS - 1);
+        cp_async_wait<NS - 1>();   // chunk c has landed
         __syncthreads();
-        const float* X = lsm + (c & 1) * kLMBuf;
-        const float* W = X + kLMT * kLMXPitch;
-        const int steps = min(kLMC, nm - kLMC * c);   // a multiple of 4
+        const float* X = lsm + (c % NS) * Tl::kBuf;
+        const float* W = X + KT * XPt;
+        const int steps = min(KC, nm - KC * c);   // a multiple of 4
         for (int q = 0; q < steps / 4; q++) {
-            float x[4][4];
+            float x[TT][4];
 #pragma unroll
-            for (int a = 0; a < 4; a++)
+            for (int a = 0; a < TT; a++)
 #pragma unroll
-                for (int s = 0; s < 4; s++) x[a][s] = X[(4 * tq + a) * kLMXPitch + 8 * (4 * q + s) + j];
+                for (int s = 0; s < 4; s++) x[a][s] = X[(TT * tg + a) * XPt + 8 * (4 * q + s) + j];
 #pragma unroll
-            for (int b = 0; b < 4; b++) {
-                const float4 w = *reinterpret_cast<const float4*>(W + ((4 * eq + b) * 8 + j) * kLMWPitch + 4 * q);
+            for (int b = 0; b < TE; b++) {
+                const float4 w = *reinterpret_cast<const float4*>(W + ((TE * eg + b) * 8 + j) * WPt + 4 * q);
 #pragma unroll
-                for (int a = 0; a < 4; a++) {
+                for (int a = 0; a < TT; a++) {
                     acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(w.x, x[a][0]));
                     acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(w.y, x[a][1]));
                     acc[a][b] = __fadd_rn(acc[a][b], __fmul_rn(w.z, x[a][2]));
@@ -682,17 +884,18 @@ logits_lm_kernel(const float* __restrict__ xn, const float* __restrict__ router_
                 }
             }
         }
-        __syncthreads();
+        __syncthreads();   // buffer c % NS is refilled by the next iteration
     }
+    cp_async_wait<0>();
     // lane sums in order: red[token][expert][lane]
     float* red = lsm;
 #pragma unroll
-    for (int a = 0; a < 4; a++)
+    for (int a = 0; a < TT; a++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) red[((4 * tq + a) * kLME + 4 * eq + b) * 8 + j] = acc[a][b];
+        for (int b = 0; b < TE; b++) red[((TT * tg + a) * KE + TE * eg + b) * 8 + j] = acc[a][b];
     __syncthreads();
-    for (int i = tid; i < kLMT * kLME; i += kLMThreads) {
-        const int tt = i / kLME, ee = i - tt * kLME, t = t0 + tt, e = e0 + ee;
+    for (int i = tid; i < KT * KE; i += NT) {
+        const int tt = i / KE, ee = i - tt * KE, t = t0 + tt, e = e0 + ee;
         if (t < T && e < E) {
             float s = hsum8_seq(red + (size_t)i * 8);
             if (offset) s = __fadd_rn(s, offset[e]);
@@ -700,6 +903,11 @@ logits_lm_kernel(const float* __restrict__ xn, const float* __restrict__ router_
         }
     }
 }
+
+// The tiles the host chooses from, largest first (TT, TE, NTG, NEG, KC, NS):
+// 32 x 32 (16 chains per thread, two CTAs per SM), 16 x 16 (16), 8 x 8 (4),
+// 4 x 8 (2); the smaller tiles take longer chunks and deeper pipelines.
+#define QRM_LM_TILES(X) X(4, 4, 8, 8, 16, 2) X(4, 4, 4, 4, 16, 5) X(2, 2, 4, 4, 32, 6) X(1, 2, 4, 4, 32, 6)
 
 // ---------------------------------------------------------------------------
 // Fused small-T router: RMSNorm, router logits, top-k and dispatch in one
@@ -742,13 +950,6 @@ struct RouteFusedParams {
     DispatchParams dp;
 };
 
-// order-preserving key of a ranking value: larger value -> larger key, NaN
-// lowest, -0 == +0 (Array.Sort with v[b].CompareTo(v[a]), value descending)
-__device__ __forceinline__ uint32_t rank_key(float v) {
-    if (isnan(v)) return 0u;
-    const uint32_t u = __float_as_uint(__fadd_rn(v, 0.f));   // -0 -> +0
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
 
 // Top-k of every token and the dispatch of the n = T*k <= 32 assignments.
 // Scores: the whole CTA (softmax: StreamingEngine.cs:642-647 with the
@@ -833,21 +1034,8 @@ __device__ void route_tail(const TopkParams& tp, const DispatchParams& p, uint8_
             const int c = lane + 32 * i;
             kc[i] = c < E ? kt[c] + 1u : 0u;   // keys are below 0xFF800001: no wrap
         }
-#pragma unroll 1
-        for (int r = 0; r < k; r++) {
-            uint32_t bk = 0u;
-            int bi = 0;
-#pragma unroll
-            for (int i = 0; i < J; i++)
-                if (kc[i] > bk) { bk = kc[i]; bi = i; }   // strict: the lowest i (index) among equal keys
-            const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
-            const uint32_t wc = __reduce_min_sync(0xffffffffu, bk == wk ? (uint32_t)(lane + 32 * bi) : 0xffffffffu);
-            const bool mine = (int)wc - 32 * bi == lane && bk == wk;   // the owner drops the winner
-#pragma unroll
-            for (int i = 0; i < J; i++)
-                if (mine && i == bi) kc[i] = 0u;
-            if (lane == 0) rsel[t * kMaxK + r] = (int)wc;
-        }
+        const int e = warp_select<J>(kc, k, lane);
+        if (lane < k) rsel[t * kMaxK + lane] = e;
     }
     __syncthreads();
     if (warp < T) {

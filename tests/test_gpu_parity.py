@@ -133,6 +133,13 @@ def test_large_batch_routing_and_skew():
     assert_parity(case, x, NORM)
 
 
+@pytest.mark.parametrize("T", [2, 31, 32])
+def test_fused_topk_dispatch_bounds(T):
+    # batches at the edges of the single-CTA top-k + dispatch (T <= 32)
+    case = make_case("c5", seed=71, d_model=1024, expert_ffn=256, n_experts=64)
+    assert_parity(case, make_input(case, T, seed=72 + T), NORM)
+
+
 def test_forward_is_deterministic():
     case = make_case("c3", seed=61, d_model=1024, expert_ffn=512, n_experts=32)
     x = make_input(case, 17, seed=62)
