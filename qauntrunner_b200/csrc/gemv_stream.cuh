@@ -113,7 +113,8 @@ constexpr int kStreamMaxWarps = 16;            // consumer warps, one token per 
 constexpr int kStreamMaxWarps2 = 14;           // two tokens per pass
 constexpr int kStreamPasses1 = 1;              // passes per item chunk, one token per pass (T = 1)
 constexpr int kStreamPasses2 = 2;              // two tokens per pass
-constexpr int kStreamMaxR16 = 2;               // most 16-row MMA tiles per item
+constexpr int kStreamMaxR16 = 2;               // most 16-row MMA tiles per gate/up item
+constexpr int kStreamMaxR16Down = 4;           // most 16-row MMA tiles per down item
 constexpr int kStreamRedSlots = 4;
 constexpr int kStreamMaxChunk = 4;             // most tokens per item chunk
 // per-stage header: item, slot, e, off, chunk tokens, seg, part, row group,
@@ -155,14 +156,29 @@ struct StreamConfig {
     int cw;            // consumer warps
 };
 
+// Most 16-row MMA tiles per item: 2 for gate/up (the item then spans the whole
+// d_model in two 64 KB stages); 4 for down, whose rows are short (d_ff): a
+// 64-row item spans two stages, so the per-item reduction and hand-over come
+// once per two stages instead of once per stage.  QRM_STREAM_DOWN_R16
+// overrides the down cap for tuning runs.
+__host__ inline int stream_max_r16(int M) {
+    if (M == 2) return kStreamMaxR16;
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QRM_STREAM_DOWN_R16");
+        v = e ? std::max(1, std::min(kStreamMaxR16Down, atoi(e))) : kStreamMaxR16Down;
+    }
+    return v;
+}
+
 // Segment geometry for `cw` consumer warps.  Every warp keeps one MMA tile
 // of the item (cw / r16 warps per tile) and takes the same number of units
 // of it per stage; a unit is one super-block (halves = 1) or one half of one
 // (groups 0-3 or 4-7, halves = 2).  Chosen: the most MMA tiles per item
-// (r16 <= 2, dividing the rows and cw), then whole super-blocks before
-// halves, then the most super-blocks per stage (dividing the row) within
-// `target` bytes.
-__host__ inline bool stream_seg(int fmt, int M, int rows, int cols, int target, int cw, StreamSeg* g) {
+// (r16 <= max_r16, dividing the rows and cw), then whole
+// super-blocks before halves, then the most super-blocks per stage (dividing
+// the row) within `target` bytes.
+__host__ inline bool stream_seg(int fmt, int M, int rows, int cols, int target, int cw, int max_r16, StreamSeg* g) {
     *g = StreamSeg{};
     g->fmt = fmt;
     if (fmt < 0) return true;
@@ -170,7 +186,7 @@ __host__ inline bool stream_seg(int fmt, int M, int rows, int cols, int target, 
     if (!cb || cols % 256) return false;
     const int nsb = cols / 256;
     const int rows_per_mma = M == 2 ? 8 : 16;   // matrix rows per MMA tile
-    for (int r16 = kStreamMaxR16; r16 >= 1; r16--) {
+    for (int r16 = max_r16; r16 >= 1; r16--) {
         if (rows % (rows_per_mma * r16) || cw % r16) continue;
         const int wpt = cw / r16;   // warps per MMA tile
         for (int halves = 1; halves <= 2; halves++) {
@@ -208,11 +224,12 @@ __host__ inline int stream_target_bytes() {
 // hide the MMA and shared-load latencies), then the most segments on whole
 // super-block units, then the most warps (QRM_STREAM_CW forces a count for
 // tuning runs).  max_tok = the most tokens of one expert slot (the launch's
-// tokens).  tab_rows = table rows the launch reads;
+// tokens).  max_r16 = the most MMA tiles per item (stream_max_r16, or fewer
+// when the launch has few items).  tab_rows = table rows the launch reads;
 // they are kept resident when that leaves at least four stages, else read
 // from global memory.
 __host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols, int ntk, int tab_rows, int max_tok,
-                                 int smem_budget, StreamConfig* c) {
+                                 int smem_budget, int max_r16, StreamConfig* c) {
     if (fmt[0] < 0 && fmt[1] < 0) return false;
     const int target = stream_target_bytes();
     static int forced = -1;
@@ -228,7 +245,7 @@ __host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols,
         bool ok = true;
         int full = 0;
         for (int i = 0; i < 2; i++) {
-            if (!stream_seg(fmt[i], M, rows, cols, target, cw, &sg[i])) ok = false;
+            if (!stream_seg(fmt[i], M, rows, cols, target, cw, max_r16, &sg[i])) ok = false;
             else if (fmt[i] >= 0 && sg[i].halves == 1) full++;
         }
         const int score = (cw >= 12 ? 1000 : 0) + 100 * full + cw;

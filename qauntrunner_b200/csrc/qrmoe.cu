@@ -273,13 +273,21 @@ bool umma_only_format(int fmt) { return fmt == qrm::Q6_K || fmt == qrm::TRI; }
 
 // Plans a launch whose routed items use format fa and shared items format fb
 // (-1: none); false when no plan fits (the caller reports it).
-bool stream_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, StreamSel* sel) {
+bool stream_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, int sm_count, StreamSel* sel) {
     if (!p.xtab) return false;
     if (fa >= 0 && !imma_usable(fa, p.rows, p.cols, gateup)) return false;
     if (fb >= 0 && !imma_usable(fb, p.rows, p.cols, gateup)) return false;
     sel->ntk = T <= 1 ? 1 : 2;
     const int fmts[2] = {fa, fb};
-    return qrm::stream_plan(fmts, gateup ? 2 : 1, p.rows, p.cols, sel->ntk, p.xtab_rows, T, 227 * 1024, &sel->cfg);
+    // larger down items only while the launch keeps two items per SM (the
+    // routed slots are at most min(E, T*k))
+    const int M = gateup ? 2 : 1;
+    int max_r16 = qrm::stream_max_r16(M);
+    if (max_r16 > qrm::kStreamMaxR16) {
+        const long long slots = (fa >= 0 ? std::min<long long>(p.E, (long long)T * p.k) : 0) + (fb >= 0 ? 1 : 0);
+        if (slots * (p.rows / (16 * max_r16)) < 2LL * sm_count) max_r16 = qrm::kStreamMaxR16;
+    }
+    return qrm::stream_plan(fmts, M, p.rows, p.cols, sel->ntk, p.xtab_rows, T, 227 * 1024, max_r16, &sel->cfg);
 }
 
 // segment formats of a launch of mode p.mode whose matrices are all format fmt
@@ -308,7 +316,7 @@ int launch_stream_t(const qrm::GemvParams& p, const StreamSel& sel, int sm_count
 template <int FA, int FB, int M>
 int launch_stream(int fa, int fb, int T, const qrm::GemvParams& p, int sm_count, int32_t* err, cudaStream_t s) {
     StreamSel sel;
-    if (!stream_select(fa, fb, M == 2, T, p, &sel))
+    if (!stream_select(fa, fb, M == 2, T, p, sm_count, &sel))
         return fail(QRM_E_STATE, "internal: no stage plan for the %d x %d expert matrices", p.rows, p.cols);
     // in-kernel tables only with a resident plan (the caller checked)
     if (p.xq_a && sel.cfg.res_rows == 0) return fail(QRM_E_STATE, "internal: activation tables were not built");
@@ -1312,7 +1320,7 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
         // formats has one
         StreamSel sp;
         gp.mode = 0;
-        const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && stream_select(fr, fs, gu, Tx, gp, &sp);
+        const bool pair = want_tab && shared && !same_fmt && imma_pair_supported(fr, fs) && stream_select(fr, fs, gu, Tx, gp, L->sm_count, &sp);
         if (want_tab) {
             // the kernels quantise resident tables themselves when every
             // integer-kernel launch of this stage keeps them resident
@@ -1324,9 +1332,9 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                 const bool ur = imma_usable(fr, gp.rows, gp.cols, gu);
                 const bool us = shared && !same_fmt && imma_usable(fs, gp.rows, gp.cols, gu);
                 gp.mode = same_fmt ? 0 : 1;
-                const bool pr = ur && stream_select(fr, same_fmt && shared ? fr : -1, gu, Tx, gp, &sr);
+                const bool pr = ur && stream_select(fr, same_fmt && shared ? fr : -1, gu, Tx, gp, L->sm_count, &sr);
                 gp.mode = 2;
-                const bool ps = us && stream_select(-1, fs, gu, Tx, gp, &ss);
+                const bool ps = us && stream_select(-1, fs, gu, Tx, gp, L->sm_count, &ss);
                 gp.mode = 0;
                 in_kernel = (ur || us) && (!ur || (pr && sr.cfg.res_rows > 0)) && (!us || (ps && ss.cfg.res_rows > 0));
             }
