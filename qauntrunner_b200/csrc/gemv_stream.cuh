@@ -208,14 +208,18 @@ __host__ inline bool stream_seg(int fmt, int M, int rows, int cols, int target, 
     return false;
 }
 
-// The target stage size (bytes).  QRM_STREAM_STAGE_KB overrides it for tuning runs.
-__host__ inline int stream_target_bytes() {
+// The target stage size (bytes): 64 KB for gate/up; 80 KB for down, where a
+// 64-row item of a d_ff = 2048 Q4_K matrix (73.7 KB) then fills one stage
+// (two stages fit beside the resident tables; measured at C5 T = 4 / 16:
+// down 120 -> 107 us / 365 -> 325 us against two 36.9 KB stages per item).
+// QRM_STREAM_STAGE_KB overrides both for tuning runs.
+__host__ inline int stream_target_bytes(int M) {
     static int v = -1;
     if (v < 0) {
         const char* e = getenv("QRM_STREAM_STAGE_KB");
-        v = e ? std::max(4, atoi(e)) * 1024 : 64 * 1024;
+        v = e ? std::max(4, atoi(e)) * 1024 : 0;
     }
-    return v;
+    return v > 0 ? v : (M == 2 ? 64 : 80) * 1024;
 }
 
 // fmt[0] / fmt[1]: formats of the routed and the shared segment (-1: none).
@@ -231,7 +235,7 @@ __host__ inline int stream_target_bytes() {
 __host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols, int ntk, int tab_rows, int max_tok,
                                  int smem_budget, int max_r16, StreamConfig* c) {
     if (fmt[0] < 0 && fmt[1] < 0) return false;
-    const int target = stream_target_bytes();
+    const int target = stream_target_bytes(M);
     static int forced = -1;
     if (forced < 0) {
         const char* e = getenv("QRM_STREAM_CW");
