@@ -273,11 +273,26 @@ bool umma_only_format(int fmt) { return fmt == qrm::Q6_K || fmt == qrm::TRI; }
 
 // Plans a launch whose routed items use format fa and shared items format fb
 // (-1: none); false when no plan fits (the caller reports it).
+// Largest launch batch that takes the one-token-per-pass kernel: an expert
+// slot with more tokens then streams its weights once per token, which at two
+// tokens (single-GPU T = 2, or expert-parallel decode over two ranks) is rare
+// and cheaper than the two-token kernel's geometry (14 warps, more registers):
+// measured C5 T = 2 181 -> 164 us, two-GPU decode 166 -> 151 us.
+// QRM_STREAM_NTK1_MAX overrides it for tuning runs.
+int stream_ntk1_max() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QRM_STREAM_NTK1_MAX");
+        v = e ? std::max(1, atoi(e)) : 2;
+    }
+    return v;
+}
+
 bool stream_select(int fa, int fb, bool gateup, int T, const qrm::GemvParams& p, int sm_count, StreamSel* sel) {
     if (!p.xtab) return false;
     if (fa >= 0 && !imma_usable(fa, p.rows, p.cols, gateup)) return false;
     if (fb >= 0 && !imma_usable(fb, p.rows, p.cols, gateup)) return false;
-    sel->ntk = T <= 1 ? 1 : 2;
+    sel->ntk = T <= stream_ntk1_max() ? 1 : 2;
     const int fmts[2] = {fa, fb};
     // larger down items only while the launch keeps two items per SM (the
     // routed slots are at most min(E, T*k))
