@@ -116,16 +116,19 @@ __device__ __forceinline__ void xquant_group(float v, int lane, int gi, int K, u
 }
 
 // Quantises activation rows into tables (global memory), one warp per four
-// groups (K % 128 == 0).
-static __global__ void xquant_kernel(const float* __restrict__ src, int K, int rows, uint8_t* __restrict__ tab,
-                              int stride) {
+// groups (K % 128 == 0).  Rows below `split` come from src, the others from
+// src_b (row r - split): the routed and the shared rows of one stage in one
+// launch.
+static __global__ void xquant_kernel(const float* __restrict__ src, const float* __restrict__ src_b, int split, int K,
+                                     int rows, uint8_t* __restrict__ tab, int stride) {
     const int lane = threadIdx.x & 31;
     const int quads = K / 128;
     const long long total = (long long)rows * quads;
     for (long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5; w < total;
          w += ((long long)gridDim.x * blockDim.x) >> 5) {
         const int r = (int)(w / quads), c = (int)(w - (long long)r * quads);
-        const float4 v = reinterpret_cast<const float4*>(src + (size_t)r * K)[32 * c + lane];
+        const float* row = r < split ? src + (size_t)r * K : src_b + (size_t)(r - split) * K;
+        const float4 v = reinterpret_cast<const float4*>(row)[32 * c + lane];
         xquant_quad(v, lane, c, K, tab + (size_t)r * stride);
     }
 }

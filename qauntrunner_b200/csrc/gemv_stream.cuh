@@ -222,6 +222,21 @@ __host__ inline int stream_target_bytes(int M) {
     return v > 0 ? v : (M == 2 ? 64 : 80) * 1024;
 }
 
+// Tables stay resident in shared memory (quantised by the consumers while the
+// first stages stream in) when that leaves this many stages, or as many as
+// without them.  Two: a separate table launch before the stage costs more
+// than the third stage gains (C5 decode down 37.0 -> 32.9 us with two 73.7 KB
+// stages and resident tables; T = 4 gate/up 155 -> 142 us).
+// QRM_STREAM_RES_MIN overrides it for tuning runs.
+__host__ inline int stream_res_min_stages() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QRM_STREAM_RES_MIN");
+        v = e ? std::max(2, atoi(e)) : 2;
+    }
+    return v;
+}
+
 // fmt[0] / fmt[1]: formats of the routed and the shared segment (-1: none).
 // Consumer warps: among the counts (up to the register budget of NTK) for
 // which every segment has a balanced geometry, 12 or more warps first (they
@@ -230,8 +245,8 @@ __host__ inline int stream_target_bytes(int M) {
 // tuning runs).  max_tok = the most tokens of one expert slot (the launch's
 // tokens).  max_r16 = the most MMA tiles per item (stream_max_r16, or fewer
 // when the launch has few items).  tab_rows = table rows the launch reads;
-// they are kept resident when that leaves at least four stages, else read
-// from global memory.
+// they are kept resident when that leaves stream_res_min_stages() stages,
+// else read from global memory.
 __host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols, int ntk, int tab_rows, int max_tok,
                                  int smem_budget, int max_r16, StreamConfig* c) {
     if (fmt[0] < 0 && fmt[1] < 0) return false;
@@ -272,7 +287,7 @@ __host__ inline bool stream_plan(const int (&fmt)[2], int M, int rows, int cols,
     long long s_glb = avail / c->stage_bytes;
     s_res = std::min<long long>(s_res, kStreamMaxStages);
     s_glb = std::min<long long>(s_glb, kStreamMaxStages);
-    if (tab_rows > 0 && s_res >= std::min<long long>(4, s_glb)) {
+    if (tab_rows > 0 && s_res >= std::min<long long>(stream_res_min_stages(), s_glb)) {
         c->res_rows = tab_rows;
         c->stages = (int)s_res;
     } else {

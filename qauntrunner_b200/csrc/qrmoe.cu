@@ -346,11 +346,14 @@ int launch_stream_pair(bool gateup, int T, const qrm::GemvParams& p, int sm_coun
                   : launch_stream<qrm::Q4_K, qrm::Q8_0, 1>(qrm::Q4_K, qrm::Q8_0, T, p, sm_count, err, s);
 }
 
-int launch_xquant(const float* src, int K, int rows, uint8_t* tab, cudaStream_t s) {
+// rows < split from src, the rest from src_b (row r - split)
+int launch_xquant(const float* src, int K, int rows, uint8_t* tab, cudaStream_t s, const float* src_b = nullptr,
+                  int split = -1) {
     if (rows <= 0) return QRM_OK;
+    if (split < 0) split = rows;
     long long warps = (long long)rows * (K / 32);
     int grid = (int)std::min<long long>((warps + 7) / 8, 148 * 16);
-    qrm::xquant_kernel<<<grid, 256, 0, s>>>(src, K, rows, tab, qrm::xtab_stride(K));
+    qrm::xquant_kernel<<<grid, 256, 0, s>>>(src, src_b, split, K, rows, tab, qrm::xtab_stride(K));
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? QRM_OK : fail(QRM_E_CUDA, "xquant launch: %s", cudaGetErrorString(e));
 }
@@ -1363,12 +1366,9 @@ static int launch_forward(qrm_layer* L, const float* x, int T, int flags, float*
                     rc = launch_xquant(xs, d, Tx, L->xtab_gu, s);
                     nl++;
                 } else {
-                    rc = launch_xquant(L->h, f, Tx * k, L->xtab_dn, s);
+                    // routed rows, then the shared rows right after them
+                    rc = launch_xquant(L->h, f, Tx * k + (shared ? Tsh : 0), L->xtab_dn, s, L->hs, Tx * k);
                     nl++;
-                    if (!rc && shared) {
-                        rc = launch_xquant(L->hs, f, Tsh, L->xtab_dn + (size_t)qrm::xtab_stride(f) * Tx * k, s);
-                        nl++;
-                    }
                 }
                 if (rc) return rc;
             }
