@@ -455,6 +455,11 @@ struct qrm_layer {
     bool shared_enabled = false;        // GLM layer with n_shared > 0
     int sm_count = 0;
     cudaStream_t stream = nullptr;
+    // qrm_forward's pinned host staging (small batches, allocated on first use):
+    // [cap rows][d] inputs | [cap rows][d] outputs | [cap rows][k] indices |
+    // [cap rows][k] weights | error flags
+    char* host_stage = nullptr;
+    int host_stage_rows = 0;
     // weights
     uint8_t* slab = nullptr;
     size_t slab_bytes = 0;
@@ -588,6 +593,7 @@ static void free_layer(qrm_layer* L) {
                     L->rec_own, L->rec_all, L->ysend, L->yrecv_nccl, L->peer_base, L->ep_state, L->xch};
     for (void* p : ptrs)
         if (p) cudaFree(p);
+    if (L->host_stage) cudaFreeHost(L->host_stage);
     clear_graphs(L);
     for (cudaEvent_t e : L->ev)
         if (e) cudaEventDestroy(e);
@@ -1583,12 +1589,71 @@ extern "C" int qrm_sync(qrm_layer* L) {
     return QRM_OK;
 }
 
+// Batches whose rows fit this many bytes go through qrm_forward's pinned,
+// mapped staging: the caller's inputs are copied on the host and uploaded by
+// one asynchronous DMA, the combine writes the output rows straight into the
+// mapped staging (no read-back DMA), top-k and the error flags come back by
+// asynchronous DMAs on the forward's stream, and the call waits once.  A
+// pageable transfer is staged by the driver on its own, and each pageable
+// read-back and the separate error check wait for the device again (~78 us
+// per call at C5 decode).  Above this size the two host copies cost more than
+// the driver's pipelined pageable transfers.
+constexpr size_t kHostStageBytes = 256u << 10;
+
+static int forward_staged(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* topk_idx,
+                          float* topk_w) {
+    const int d = L->desc.d_model, k = L->k;
+    const size_t xb = sizeof(float) * (size_t)T * d, kb = sizeof(int32_t) * (size_t)T * k;
+    if (L->host_stage_rows < T) {
+        const int rows = (int)std::max<size_t>((size_t)T, kHostStageBytes / (sizeof(float) * d));
+        if (L->host_stage) cudaFreeHost(L->host_stage);
+        L->host_stage = nullptr;
+        L->host_stage_rows = 0;
+        const size_t bytes = 2 * sizeof(float) * (size_t)rows * d + 2 * sizeof(int32_t) * (size_t)rows * k + 64;
+        if (cudaHostAlloc(&L->host_stage, bytes, cudaHostAllocMapped) != cudaSuccess) {
+            L->host_stage = nullptr;
+            return fail(QRM_E_NOMEM, "pinned staging of %zu bytes", bytes);
+        }
+        L->host_stage_rows = rows;
+    }
+    const int cap = L->host_stage_rows;
+    float* hx = reinterpret_cast<float*>(L->host_stage);
+    float* hout = hx + (size_t)cap * d;
+    int32_t* hidx = reinterpret_cast<int32_t*>(hout + (size_t)cap * d);
+    float* hw = reinterpret_cast<float*>(hidx + (size_t)cap * k);
+    int32_t* herr = reinterpret_cast<int32_t*>(hw + (size_t)cap * k);
+    float* dout = nullptr;   // the output rows' device view of the mapped staging
+    QRM_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dout), hout, 0));
+    memcpy(hx, x, xb);
+    QRM_CUDA(cudaMemcpyAsync(L->x, hx, xb, cudaMemcpyHostToDevice, L->stream));
+    int rc = run_forward(L, L->x, T, flags, dout, L->topk_idx, L->topk_w, L->stream);
+    if (rc) return rc;
+    if (topk_idx) QRM_CUDA(cudaMemcpyAsync(hidx, L->topk_idx, kb, cudaMemcpyDeviceToHost, L->stream));
+    if (topk_w) QRM_CUDA(cudaMemcpyAsync(hw, L->topk_w, kb, cudaMemcpyDeviceToHost, L->stream));
+    QRM_CUDA(cudaMemcpyAsync(herr, &L->sched->err, sizeof(int32_t), cudaMemcpyDeviceToHost, L->stream));
+    QRM_CUDA(cudaStreamSynchronize(L->stream));
+    const int32_t err = *herr;
+    if (err) {
+        QRM_CUDA(cudaMemsetAsync(&L->sched->err, 0, sizeof(int32_t), L->stream));
+        QRM_CUDA(cudaStreamSynchronize(L->stream));
+        if (err & qrm::ERR_TIMEOUT) return fail(QRM_E_TIMEOUT, "a device wait timed out");
+        return fail(QRM_E_INVALID, "device reported error flags 0x%x (expert index out of range)", err);
+    }
+    memcpy(out, hout, xb);
+    if (topk_idx) memcpy(topk_idx, hidx, kb);
+    if (topk_w) memcpy(topk_w, hw, kb);
+    return QRM_OK;
+}
+
 extern "C" int qrm_forward(qrm_layer* L, const float* x, int T, int flags, float* out, int32_t* topk_idx, float* topk_w) {
     if (!L || !x || !out) return fail(QRM_E_INVALID, "NULL argument");
     int rc = forward_checks(L, T, flags);
     if (rc) return rc;
     QRM_CUDA(cudaSetDevice(L->desc.device));
     const size_t xb = sizeof(float) * (size_t)T * L->desc.d_model;
+    // one process per GPU and one layer stream: the staged path covers
+    // single-GPU layers; expert-parallel layers synchronise the whole device
+    if (L->world == 1 && xb <= kHostStageBytes) return forward_staged(L, x, T, flags, out, topk_idx, topk_w);
     QRM_CUDA(cudaMemcpyAsync(L->x, x, xb, cudaMemcpyHostToDevice, L->stream));
     rc = run_forward(L, L->x, T, flags, L->out, L->topk_idx, L->topk_w, L->stream);
     if (rc) return rc;
