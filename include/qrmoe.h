@@ -151,7 +151,12 @@ int qrm_load_qw(qrm_layer* layer, const char* path, int layer_index);
  * One MoE layer over T tokens (the reference runs T sequential Forward calls).
  * x [T x d] f32, out [T x d] f32.  Optional outputs (NULL to skip):
  * topk_idx [T x k] int32 (the experts in the reference's sorted order),
- * topk_w [T x k] f32 (their combine weights).  Synchronous. */
+ * topk_w [T x k] f32 (their combine weights).  Synchronous.  On a
+ * single-GPU layer, batches of at most 256 KiB of rows go through pinned,
+ * mapped host staging that the layer allocates on its first such call and
+ * keeps until qrm_destroy (at least 256 KiB of inputs and as much of
+ * outputs); larger batches and expert-parallel layers copy from the caller's
+ * arrays directly. */
 int qrm_forward(qrm_layer* layer, const float* x, int T, int flags, float* out,
                 int32_t* topk_idx, float* topk_w);
 /* Same on device buffers, asynchronous on `stream` (a cudaStream_t; NULL =
