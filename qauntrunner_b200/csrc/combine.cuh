@@ -20,10 +20,24 @@ struct CombineParams {
     const float* topk_w;     // [T x k]
     float* out;              // [T x d]
     int T, k, d;
+    // optional (qrm_forward's mapped host staging): block 0 also copies the
+    // top-k and the error flags there once the predecessors are done
+    const int32_t* topk_idx;  // [T x k]
+    const int32_t* err;
+    int32_t* copy_idx;
+    float* copy_w;
+    int32_t* copy_err;
 };
 
 __global__ void combine_kernel(CombineParams p) {
     pdl_wait();   // the expert outputs of the predecessor
+    if (p.copy_err && blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < p.T * p.k; i += blockDim.x) {
+            p.copy_idx[i] = p.topk_idx[i];
+            p.copy_w[i] = p.topk_w[i];
+        }
+        if (threadIdx.x == 0) *p.copy_err = *reinterpret_cast<const volatile int32_t*>(p.err);
+    }
     const int d4 = p.d >> 2;
     const long long total = (long long)p.T * d4;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
